@@ -1,0 +1,609 @@
+// beam_search.cu — persistent filtered graph beam search (one warp per route).
+//
+// Semantics follow the device-resident traversal loop of the reference,
+// run_pq_search_one_block (src/search/pq/backend_pq.cu:3988-5013) with
+// cooperative pickup, and its RaBitQ twin run_rabitq_search_one_block
+// (src/search/rabitq/backend_rabitq.cu:3496-4292): symmetric min-max
+// frontier of queue_size+1 entries, 4096-slot visited hash, stop top-k with
+// fixed/adaptive early stop, binary-heap result shortlist, DNF predicate with
+// the alpha penalty.  Every decision that fixes which ids come back (pickup
+// order, frontier admission/eviction, heap layouts, hash insertion order) is
+// kept identical; the B200 kernel parallelises the rest across the warp:
+//   * neighbour rows are read by 32 lanes at once and visited-tested in
+//     parallel (the reference tests all neighbours before any insertion of
+//     the same step, so a parallel test is exact), compacted in order by
+//     ballot/popc;
+//   * each lane scores whole candidates: the PQ ADC replays the reference's
+//     lane-strided partials and xor butterfly inside one thread, so 32
+//     candidates are scored in one dependent round instead of 32;
+//   * predicate pass bits and the frontier-threshold rejections are computed
+//     by all lanes; lane 0 only runs the surviving min-max heap insertions,
+//     which are order dependent.
+// Warps are persistent: each pulls route indices from a device counter.
+#include "pq_device.cuh"
+#include "rq_device.cuh"
+
+namespace gofann {
+namespace {
+
+constexpr int kWarpsPerBlock = 4;
+constexpr int kMaxSteps = 1 << 22;  // hard bound when max_steps == 0
+
+struct WarpState {
+    FPair now, next;
+    int heap_size, stop_size, topk_size, finished;
+    int exhausted, expanded, passed, len;
+    float stop_worst, penalty, maxv;
+    int brk, nfr, reject_all;
+    uint32_t n_dist, n_probe, n_admit;
+    uint32_t rej[2];
+    uint32_t pass[2];
+};
+
+struct BeamArgs {
+    gofann_graph graph;
+    AttrView attrs;
+    gofann_codes codes;
+    gofann_prepared prep;
+    gofann_routes routes;
+    gofann_search_params p;
+    gofann_search_out out;
+    uint32_t* hash;          // [total_warps][4096]
+    uint32_t* route_counter; // one uint32, zeroed before launch
+    int32_t* status;
+    uint32_t warp_smem;      // bytes of dynamic shared memory per warp
+};
+
+struct SmemLayout {
+    uint32_t frontier, topk, stop, list, sample, dist, prio, state, table, total;
+};
+
+__host__ __device__ inline uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
+
+__host__ __device__ inline SmemLayout smem_layout(const gofann_search_params& p, const gofann_codes& c,
+                                                  bool lut_shared)
+{
+    SmemLayout s;
+    uint32_t o = 0;
+    s.frontier = o; o = align16(o + (p.queue_size + 3) * sizeof(FPair));
+    s.topk = o; o = align16(o + (p.result_width + 1) * sizeof(RPair));
+    s.stop = o; o = align16(o + (GOFANN_MAX_TOPK + 2) * sizeof(SPair));
+    s.list = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
+    s.sample = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
+    s.dist = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
+    s.prio = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
+    s.state = o; o = align16(o + sizeof(WarpState));
+    s.table = o;
+    if (p.scorer == GOFANN_SCORER_PQ) {
+        if (lut_shared) o = align16(o + c.pq_dim * GOFANN_PQ_CENTROIDS * 4);
+    } else {
+        o = align16(o + 8 * (c.padded_dim / 32) * 4);
+    }
+    s.total = o;
+    return s;
+}
+
+__device__ __forceinline__ int adaptive_limit(int queue_limit, int expanded, int pass, int stop_width)
+{
+    // adaptive_early_stop_limit, backend_pq.cu:2822-2854
+    const int queue_base = queue_limit > 1 ? queue_limit : 1;
+    int base_limit = (queue_base + 1) / 2;
+    const int min_base = stop_width > 0 ? stop_width * 2 : 1;
+    base_limit = base_limit > min_base ? base_limit : min_base;
+    const int denom = (expanded + 16) > 1 ? (expanded + 16) : 1;
+    const int pw = pass + 8;
+    const int pest = pw < denom ? pw : denom;
+    const int rej = (denom - pest) > 0 ? (denom - pest) : 0;
+    const int64_t num = static_cast<int64_t>(queue_limit) * rej;
+    int extra = static_cast<int>((num + (2 * denom - 1)) / (2 * denom));
+    extra = extra > 0 ? extra : 0;
+    extra = extra < 32 ? extra : 32;
+    return base_limit + extra;
+}
+
+__device__ __forceinline__ bool stop_now(const gofann_search_params& p, const WarpState& st, int step)
+{
+    bool es = false;
+    if (p.early_stop_mode == GOFANN_EARLY_STOP_ADAPTIVE)
+        es = st.finished >= adaptive_limit(p.queue_size, st.expanded, st.passed, p.stop_width);
+    else if (p.early_stop_mode == GOFANN_EARLY_STOP_FIXED)
+        es = st.finished >= p.finish_limit;
+    const int cap = p.max_steps > 0 ? p.max_steps : kMaxSteps;
+    return st.exhausted || es || step >= cap;
+}
+
+// Cooperative pickup (backend_pq.cu:844-893): lexicographic min of
+// (first, index) over unused entries, same lane-strided scan and shfl_down
+// tree; lane 0 copies and marks the winner.
+__device__ __forceinline__ bool coop_pickup(FPair* f, int size, FPair* out, int lane)
+{
+    int bi = -1;
+    float bd = FLT_MAX;
+    for (int i = lane + 1; i < size; i += kWarp) {
+        const FPair e = f[i];
+        if (e.second & kPoolUsed) continue;
+        if (bi < 0 || e.first < bd || (!(bd < e.first) && !(e.first < bd) && i < bi)) { bi = i; bd = e.first; }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const int oi = __shfl_down_sync(kFull, bi, off);
+        const float od = __shfl_down_sync(kFull, bd, off);
+        if (oi >= 0 && (bi < 0 || od < bd || (!(bd < od) && !(od < bd) && oi < bi))) { bi = oi; bd = od; }
+    }
+    bi = __shfl_sync(kFull, bi, 0);
+    if (lane == 0 && bi >= 0) {
+        *out = f[bi];
+        f[bi].second |= kPoolUsed;
+    }
+    __syncwarp();
+    return bi >= 0;
+}
+
+template <int kScorer, bool kLutShared>
+struct Scorer {
+    const float* lut_row;  // PQ
+    RqQueryView rq;        // RaBitQ
+    __device__ __forceinline__ float operator()(const gofann_codes& c, uint32_t sample) const
+    {
+        if constexpr (kScorer == GOFANN_SCORER_PQ) {
+            return pq_adc_warp_order(lut_row, c.pq_codes + static_cast<size_t>(sample) * c.pq_dim,
+                                     static_cast<int>(c.pq_dim));
+        } else {
+            return rq_estimate(c, rq, sample);
+        }
+    }
+};
+
+template <int kScorer, bool kBias, bool kLutShared>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamArgs a)
+{
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const gofann_search_params& p = a.p;
+    const SmemLayout L = smem_layout(p, a.codes, kLutShared);
+    unsigned char* base = smem_raw + static_cast<size_t>(warp) * a.warp_smem;
+    FPair* frontier = reinterpret_cast<FPair*>(base + L.frontier);
+    RPair* topk = reinterpret_cast<RPair*>(base + L.topk);
+    SPair* stopk = reinterpret_cast<SPair*>(base + L.stop);
+    uint32_t* list = reinterpret_cast<uint32_t*>(base + L.list);
+    uint32_t* slist = reinterpret_cast<uint32_t*>(base + L.sample);
+    float* dist = reinterpret_cast<float*>(base + L.dist);
+    float* prio = reinterpret_cast<float*>(base + L.prio);
+    WarpState& st = *reinterpret_cast<WarpState*>(base + L.state);
+    float* table = reinterpret_cast<float*>(base + L.table);
+    const uint32_t gwarp = blockIdx.x * (blockDim.x >> 5) + warp;
+    uint32_t* hash = a.hash + static_cast<size_t>(gwarp) * kHashCap;
+    const int QS = p.queue_size, SW = p.stop_width, RW = p.result_width;
+    const uint32_t deg = a.graph.degree < GOFANN_MAX_DEGREE ? a.graph.degree : GOFANN_MAX_DEGREE;
+
+    for (;;) {
+        uint32_t route = 0;
+        if (lane == 0) route = atomicAdd(a.route_counter, 1u);
+        route = __shfl_sync(kFull, route, 0);
+        if (route >= a.routes.n_routes) break;
+
+        const uint32_t row = a.routes.query_row[route];
+        const uint32_t label_offset = a.graph.label_offset[a.routes.group_id[route]];
+        const uint32_t begin_id = a.routes.start_local[route];
+        const uint64_t qbit = a.routes.filter_bits ? a.routes.filter_bits[route] : ~0ull;
+        const bool pred_on = pred_enabled(a.routes, route);
+
+        // visited table clear (native_visited_hash::clear)
+        {
+            uint4* h4 = reinterpret_cast<uint4*>(hash);
+            const uint4 e = make_uint4(kU32Max, kU32Max, kU32Max, kU32Max);
+            for (int i = lane; i < kHashCap / 4; i += kWarp) h4[i] = e;
+        }
+        Scorer<kScorer, kLutShared> score;
+        if constexpr (kScorer == GOFANN_SCORER_PQ) {
+            const float* g = a.prep.pq_lut + static_cast<size_t>(row) * a.codes.pq_dim * GOFANN_PQ_CENTROIDS;
+            if constexpr (kLutShared) {
+                const float4* s4 = reinterpret_cast<const float4*>(g);
+                float4* d4 = reinterpret_cast<float4*>(table);
+                const int n4 = static_cast<int>(a.codes.pq_dim) * GOFANN_PQ_CENTROIDS / 4;
+                for (int i = lane; i < n4; i += kWarp) d4[i] = __ldg(s4 + i);
+                score.lut_row = table;
+            } else {
+                score.lut_row = g;
+            }
+        } else {
+            rq_build_planes(a.prep.rq_q8 + static_cast<size_t>(row) * a.codes.padded_dim,
+                            static_cast<int>(a.codes.padded_dim), reinterpret_cast<uint32_t*>(table), lane,
+                            kWarp);
+            score.rq.planes = reinterpret_cast<const uint32_t*>(table);
+            score.rq.scale = a.prep.rq_scale[row];
+            score.rq.k1 = a.prep.rq_k1xsumq[row];
+            score.rq.gdist = a.prep.rq_centroid_dist + static_cast<size_t>(row) * a.codes.num_anchors;
+        }
+        __syncwarp();
+
+        // start node (backend_pq.cu:4172-4209)
+        if (lane == 0) {
+            const uint32_t begin_sample = a.graph.row_to_sample[label_offset + begin_id];
+            const float start = score(a.codes, begin_sample);
+            float penalty = 0.0f;
+            if (kBias) {
+                const double wide = static_cast<double>(p.alpha) * fmax(static_cast<double>(fabsf(start)), 1e-6);
+                penalty = isfinite(wide) ? static_cast<float>(fmin(wide, static_cast<double>(FLT_MAX))) : 0.0f;
+            }
+            st.penalty = penalty;
+            st.heap_size = 1;
+            st.stop_size = 0;
+            st.topk_size = 0;
+            st.stop_worst = -FLT_MAX;
+            st.finished = 0;
+            st.exhausted = 0;
+            st.expanded = 0;
+            st.passed = 0;
+            st.n_dist = 1;
+            st.n_probe = 0;
+            st.n_admit = 0;
+            FPair kp;
+            kp.first = start;
+            kp.second = begin_id;
+            kp.base = start;
+            smmh_insert(frontier, st.heap_size, kp);
+            hash_add(hash, begin_id);
+        }
+        __syncwarp();
+        coop_pickup(frontier, st.heap_size, &st.now, lane);
+
+        int step = 0;
+        for (;;) {
+            if (step != 0 && st.heap_size <= 1) break;
+            ++step;
+            if (step != 1) {
+                FPair nx;
+                const bool found = coop_pickup(frontier, st.heap_size, &st.next, lane);
+                if (lane == 0) {
+                    if (!found) {
+                        st.exhausted = 1;
+                        nx.first = FLT_MAX; nx.second = kU32Max; nx.base = FLT_MAX;
+                        st.next = nx;
+                    } else if (st.stop_size == SW) {
+                        float pending = st.next.first;
+                        if (p.pending_base_stop && pred_on) {
+                            float m = fminf(FLT_MAX, kBias ? st.now.base : st.now.first);
+                            m = fminf(m, kBias ? st.next.base : st.next.first);
+                            for (int i = 1; i < st.heap_size; ++i)
+                                if (!(frontier[i].second & kPoolUsed))
+                                    m = fminf(m, kBias ? frontier[i].base : frontier[i].first);
+                            pending = m;
+                        }
+                        if (p.early_stop_mode != GOFANN_EARLY_STOP_OFF && st.stop_worst <= pending) ++st.finished;
+                    }
+                }
+                __syncwarp();
+            }
+            if (st.exhausted) break;
+            const uint32_t now_row = st.now.second & ~kPoolUsed;
+            const uint32_t grow = label_offset + now_row;
+
+            if (lane == 0) {
+                // filter verdict of the expanded node (backend_pq.cu:4394-4440)
+                const bool bit_match = a.graph.row_filter_mask ? (a.graph.row_filter_mask[grow] & qbit) != 0ull
+                                                               : qbit != 0ull;
+                const uint32_t sample = a.graph.row_to_sample[grow];
+                uint32_t active = 0, matched = 0;
+                if (a.routes.range_modes) {
+                    for (uint32_t i = 0; i < a.routes.range_count; ++i) {
+                        const size_t qf = static_cast<size_t>(route) * a.routes.range_count + i;
+                        const uint8_t mode = a.routes.range_modes[qf];
+                        if (mode == 0) continue;
+                        ++active;
+                        if (a.routes.range_lower && a.routes.range_upper && a.attrs.ranges &&
+                            range_match(mode, a.routes.range_lower[qf], a.routes.range_upper[qf],
+                                        a.attrs.ranges[static_cast<size_t>(sample) * a.routes.range_count + i]))
+                            ++matched;
+                    }
+                    if (!a.routes.range_lower || !a.routes.range_upper || !a.attrs.ranges) matched = 0;
+                }
+                const bool exact_range = active == 0 || matched == active;
+                int nfr = (p.full_label_check == 0 || labels_match(a.routes, a.attrs, route, sample)) ? 1 : 2;
+                if (pred_on) {
+                    nfr = pred_matches(a.routes, a.attrs, route, sample) ? 1 : 2;
+                    ++st.n_probe;
+                } else if (!a.routes.route_compiled || !a.routes.route_compiled[route]) {
+                    nfr = (nfr == 1 && bit_match && exact_range) ? 1 : 2;
+                }
+                st.nfr = nfr;
+                st.brk = stop_now(p, st, step) ? 1 : 0;
+                if (!st.brk) {
+                    ++st.expanded;
+                    if (nfr == 1) {
+                        // stop top-k and result heap (backend_pq.cu:4583-4630)
+                        ++st.passed;
+                        const float current = kBias ? st.now.base : st.now.first;
+                        RPair te;
+                        te.first = current;
+                        te.second = now_row;
+                        SPair se;
+                        se.first = current;
+                        se.pad = 0;
+                        se.second = (static_cast<uint64_t>(__float_as_uint(current)) << 32) | now_row;
+                        bool improved = false;
+                        if (st.stop_size < SW) {
+                            stopk[st.stop_size++] = se;
+                            bheap_push(stopk, st.stop_size);
+                            improved = true;
+                            if (st.stop_size == 1 || current > st.stop_worst) st.stop_worst = current;
+                        } else if (se.first < stopk[0].first) {
+                            stopk[st.stop_size++] = se;
+                            bheap_push(stopk, st.stop_size);
+                            const SPair removed = bheap_pop(stopk, st.stop_size);
+                            --st.stop_size;
+                            improved = true;
+                            const uint32_t removed_bits = static_cast<uint32_t>(removed.second >> 32);
+                            if (current > st.stop_worst) {
+                                st.stop_worst = current;
+                            } else if (removed_bits == __float_as_uint(st.stop_worst)) {
+                                st.stop_worst = -FLT_MAX;
+                                for (int i = 0; i < st.stop_size; ++i) {
+                                    const float pd = __uint_as_float(static_cast<uint32_t>(stopk[i].second >> 32));
+                                    if (pd > st.stop_worst) st.stop_worst = pd;
+                                }
+                            }
+                        }
+                        if (p.early_stop_mode == GOFANN_EARLY_STOP_ADAPTIVE && improved) st.finished = 0;
+                        if (st.topk_size < RW) {
+                            topk[st.topk_size++] = te;
+                            bheap_push(topk, st.topk_size);
+                        } else if (te.first < topk[0].first) {
+                            topk[st.topk_size++] = te;
+                            bheap_push(topk, st.topk_size);
+                            bheap_pop(topk, st.topk_size);
+                            --st.topk_size;
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (st.brk) break;
+
+            // neighbour list: parallel read + visited test, in-order compaction
+            const uint32_t* adj = a.graph.adjacency + static_cast<size_t>(grow) * a.graph.degree;
+            int len = 0;
+#pragma unroll
+            for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
+                const uint32_t i = half * kWarp + lane;
+                uint32_t idx = kU32Max;
+                if (i < deg) idx = __ldg(adj + i);
+                const bool keep = idx != kU32Max && !hash_test(hash, idx);
+                const unsigned m = __ballot_sync(kFull, keep);
+                if (keep) list[len + __popc(m & ((1u << lane) - 1u))] = idx;
+                len += __popc(m);
+            }
+            __syncwarp();
+            if (lane == 0) {
+                st.len = len;
+                st.brk = stop_now(p, st, step) ? 1 : 0;
+            }
+            __syncwarp();
+            if (st.brk) break;
+
+            // score every listed candidate, one candidate per lane
+            for (int i = lane; i < len; i += kWarp) {
+                const uint32_t s = __ldg(a.graph.row_to_sample + label_offset + list[i]);
+                slist[i] = s;
+                dist[i] = score(a.codes, s);
+            }
+            __syncwarp();
+            const bool full = st.heap_size >= QS + 1;
+            const float maxv = full ? frontier[2].first : 0.0f;
+#pragma unroll
+            for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
+                const int i = half * kWarp + lane;
+                bool reject = false;
+                if (i < len) {
+                    float pr = dist[i];
+                    if (kBias && pred_on) {
+                        const bool pass = pred_matches(a.routes, a.attrs, route, slist[i]);
+                        pr = pred_priority(dist[i], st.penalty, pass);
+                    }
+                    prio[i] = pr;
+                    reject = full && maxv < pr;  // definitely rejected (max only decreases)
+                }
+                const unsigned m = __ballot_sync(kFull, reject);
+                if (lane == 0) st.rej[half] = m;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                st.n_dist += static_cast<uint32_t>(len);
+                if (kBias && pred_on) st.n_probe += static_cast<uint32_t>(len);
+                for (int i = 0; i < len; ++i) {
+                    if ((st.rej[i >> 5] >> (i & 31)) & 1u) continue;
+                    FPair kp;
+                    kp.first = prio[i];
+                    kp.base = dist[i];
+                    kp.second = list[i];
+                    if (st.heap_size >= QS + 1 && frontier[2].first < kp.first) continue;
+                    smmh_insert(frontier, st.heap_size, kp);
+                    hash_add(hash, list[i]);
+                    ++st.n_admit;
+                    if (st.heap_size >= QS + 2) smmh_pop_max(frontier, st.heap_size);
+                }
+            }
+            __syncwarp();
+            if (step == 1) {
+                const bool found = coop_pickup(frontier, st.heap_size, &st.next, lane);
+                if (lane == 0 && !found) {
+                    st.exhausted = 1;
+                    FPair nx;
+                    nx.first = FLT_MAX; nx.second = kU32Max; nx.base = FLT_MAX;
+                    st.next = nx;
+                }
+            }
+            if (lane == 0) st.now = st.next;
+            __syncwarp();
+        }
+
+        // emit the shortlist ascending (in-place heap sort of the result heap)
+        if (lane == 0) {
+            const int valid = st.topk_size;
+            for (int i = 0; i < valid; ++i) {
+                const int n = valid - i;
+                const RPair r = bheap_pop(topk, n);
+                topk[n - 1] = r;
+            }
+            if (step >= (p.max_steps > 0 ? p.max_steps : kMaxSteps) && p.max_steps == 0 && a.status)
+                atomicExch(a.status, GOFANN_ERR_CAPACITY);
+        }
+        __syncwarp();
+        const int valid = st.topk_size;
+        uint32_t* oid = a.out.ids + static_cast<size_t>(route) * RW;
+        float* od = a.out.dists + static_cast<size_t>(route) * RW;
+        for (int i = lane; i < RW; i += kWarp) {
+            uint32_t id = kU32Max;
+            float d = FLT_MAX;
+            if (i < valid && topk[i].second != kU32Max) {
+                id = a.graph.row_to_sample[label_offset + topk[i].second];
+                d = topk[i].first;
+            }
+            oid[i] = id;
+            od[i] = d;
+        }
+        if (lane == 0) {
+            if (a.out.steps) a.out.steps[route] = step;
+            if (a.out.counters) {
+                uint32_t* c = a.out.counters + static_cast<size_t>(route) * 4;
+                c[0] = static_cast<uint32_t>(st.expanded);
+                c[1] = st.n_dist;
+                c[2] = st.n_probe;
+                c[3] = st.n_admit;
+            }
+        }
+        __syncwarp();
+    }
+}
+
+using KernelFn = void (*)(BeamArgs);
+
+KernelFn pick_kernel(int scorer, bool bias, bool lut_shared)
+{
+    if (scorer == GOFANN_SCORER_PQ) {
+        if (bias) return lut_shared ? beam_search_kernel<0, true, true> : beam_search_kernel<0, true, false>;
+        return lut_shared ? beam_search_kernel<0, false, true> : beam_search_kernel<0, false, false>;
+    }
+    return bias ? beam_search_kernel<1, true, false> : beam_search_kernel<1, false, false>;
+}
+
+// Persistent grid: at most one warp per route, at most what fits resident.
+uint32_t grid_blocks(uint32_t n_routes, int warps_per_block, int per_sm)
+{
+    const uint32_t need = (n_routes + warps_per_block - 1) / warps_per_block;
+    const uint32_t cap = static_cast<uint32_t>(per_sm > 0 ? per_sm : 1) * static_cast<uint32_t>(sm_count());
+    return need < cap ? need : cap;
+}
+
+constexpr size_t kCounterBytes = 256;  // route counter, kept 256-byte aligned
+
+}  // namespace
+}  // namespace gofann
+
+using namespace gofann;
+
+extern "C" {
+
+size_t gofann_beam_search_scratch_bytes(uint32_t n_routes)
+{
+    // Upper bound over variants: one table per warp of the persistent grid,
+    // which never exceeds one warp per route nor 64 warps per SM.
+    const uint32_t sms = static_cast<uint32_t>(sm_count() > 0 ? sm_count() : 148);
+    uint64_t warps = (static_cast<uint64_t>(n_routes) + kWarpsPerBlock - 1) / kWarpsPerBlock * kWarpsPerBlock;
+    const uint64_t cap = static_cast<uint64_t>(sms) * 64;
+    if (warps > cap) warps = cap;
+    if (warps == 0) warps = kWarpsPerBlock;
+    return kCounterBytes + warps * kHashCap * sizeof(uint32_t);
+}
+
+int gofann_beam_search(const gofann_graph* graph, const gofann_attrs* attrs, const gofann_codes* codes,
+                       const gofann_prepared* prep, const gofann_routes* routes,
+                       const gofann_search_params* params, const gofann_search_out* out, void* scratch,
+                       size_t scratch_bytes, void* stream)
+{
+    if (!graph || !codes || !prep || !routes || !params || !out || !scratch)
+        return fail(GOFANN_ERR_INVALID, "beam_search: null argument");
+    const gofann_search_params& p = *params;
+    if (p.queue_size < 2 || p.queue_size > GOFANN_MAX_QUEUE)
+        return fail(GOFANN_ERR_INVALID, "beam_search: queue_size %d outside 2..%d", p.queue_size, GOFANN_MAX_QUEUE);
+    if (p.stop_width < 1 || p.stop_width > GOFANN_MAX_TOPK)
+        return fail(GOFANN_ERR_INVALID, "beam_search: stop_width %d outside 1..%d", p.stop_width, GOFANN_MAX_TOPK);
+    if (p.result_width < 1 || p.result_width > GOFANN_MAX_RESULT_WIDTH)
+        return fail(GOFANN_ERR_INVALID, "beam_search: result_width %d outside 1..%d", p.result_width,
+                    GOFANN_MAX_RESULT_WIDTH);
+    if (p.early_stop_mode < 0 || p.early_stop_mode > 2)
+        return fail(GOFANN_ERR_INVALID, "beam_search: unknown early_stop_mode %d", p.early_stop_mode);
+    if (!graph->adjacency || !graph->row_to_sample || !graph->label_offset || graph->degree == 0)
+        return fail(GOFANN_ERR_INVALID, "beam_search: graph arrays missing");
+    if (!routes->query_row || !routes->group_id || !routes->start_local || !out->ids || !out->dists)
+        return fail(GOFANN_ERR_INVALID, "beam_search: route or output arrays missing");
+    const bool needs_attrs = routes->pred_offsets != nullptr || p.full_label_check != 0 ||
+                             routes->range_modes != nullptr;
+    if (needs_attrs && (!attrs || !attrs->label_indptr || !attrs->label_indices))
+        return fail(GOFANN_ERR_INVALID, "beam_search: predicates need the sample label CSR");
+    if (routes->pred_offsets && (!routes->clauses || !routes->pred_handles))
+        return fail(GOFANN_ERR_INVALID, "beam_search: predicate clause arrays missing");
+    bool lut_shared = false;
+    if (p.scorer == GOFANN_SCORER_PQ) {
+        if (!codes->pq_codes || !prep->pq_lut) return fail(GOFANN_ERR_INVALID, "beam_search: PQ arrays missing");
+        if (codes->pq_dim == 0 || codes->pq_dim > static_cast<uint32_t>(kMaxPqDim))
+            return fail(GOFANN_ERR_UNSUPPORTED, "beam_search: pq_dim %u outside 1..%d", codes->pq_dim, kMaxPqDim);
+        lut_shared = p.lut_in_shared != 0;
+    } else if (p.scorer == GOFANN_SCORER_RABITQ) {
+        if (!codes->rq_codes || !codes->rq_factors || !codes->rq_anchor_ids || !prep->rq_q8 || !prep->rq_scale ||
+            !prep->rq_k1xsumq || !prep->rq_centroid_dist)
+            return fail(GOFANN_ERR_INVALID, "beam_search: RaBitQ arrays missing");
+        if (codes->padded_dim == 0 || codes->padded_dim % 64 != 0 || codes->padded_dim > 4096)
+            return fail(GOFANN_ERR_UNSUPPORTED, "beam_search: padded_dim %u unsupported", codes->padded_dim);
+    } else {
+        return fail(GOFANN_ERR_INVALID, "beam_search: unknown scorer %d", p.scorer);
+    }
+    if (routes->n_routes == 0) return GOFANN_OK;
+
+    BeamArgs args{};
+    args.graph = *graph;
+    if (attrs) {
+        args.attrs.indptr = attrs->label_indptr;
+        args.attrs.indices = attrs->label_indices;
+        args.attrs.ranges = attrs->range_values;
+        args.attrs.n_samples = attrs->n_samples;
+        args.attrs.range_count = attrs->range_count;
+    }
+    args.codes = *codes;
+    args.prep = *prep;
+    args.routes = *routes;
+    args.p = p;
+    args.out = *out;
+    args.status = out->status;
+    const SmemLayout L = smem_layout(p, *codes, lut_shared);
+    args.warp_smem = L.total;
+    constexpr size_t kMaxSmem = 227 * 1024;
+    int wpb = kWarpsPerBlock;
+    while (wpb > 1 && static_cast<size_t>(L.total) * wpb > kMaxSmem) --wpb;
+    const size_t smem = static_cast<size_t>(L.total) * wpb;
+    if (smem > kMaxSmem)
+        return fail(GOFANN_ERR_UNSUPPORTED, "beam_search: %zu bytes of shared memory per warp exceed 227 KB", smem);
+    const bool bias = p.predicate_bias != 0;
+    const KernelFn kern = pick_kernel(p.scorer, bias, lut_shared);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_status(e, "beam_search: shared memory attribute");
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, wpb * 32, smem);
+    if (e != cudaSuccess) return cuda_status(e, "beam_search: occupancy query");
+    if (per_sm <= 0) return fail(GOFANN_ERR_UNSUPPORTED, "beam_search: kernel does not fit on an SM");
+    const uint32_t blocks = grid_blocks(routes->n_routes, wpb, per_sm);
+    const size_t need = kCounterBytes + static_cast<size_t>(blocks) * wpb * kHashCap * sizeof(uint32_t);
+    if (scratch_bytes < need)
+        return fail(GOFANN_ERR_CAPACITY, "beam_search: scratch of %zu bytes, %zu needed", scratch_bytes, need);
+    args.route_counter = static_cast<uint32_t*>(scratch);
+    args.hash = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(scratch) + kCounterBytes);
+    cudaStream_t s = as_stream(stream);
+    e = cudaMemsetAsync(scratch, 0, sizeof(uint32_t), s);
+    if (e != cudaSuccess) return cuda_status(e, "beam_search: counter reset");
+    kern<<<blocks, wpb * 32, smem, s>>>(args);
+    GOFANN_CHECK_LAUNCH("beam_search_kernel");
+    return GOFANN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,324 @@
+// common.cuh — shared device helpers of the B200 filtered-ANN search path.
+//
+// Host side: thread-local error string + status helpers used by every C-ABI
+// entry point.  Device side: the data-structure algorithms whose exact
+// behaviour decides which ids a traversal returns (visited hash, symmetric
+// min-max frontier, binary result heaps, (dist,id) ordering), the DNF
+// predicate, and the warp-order replays of the reference's float reductions.
+#pragma once
+
+#include <cfloat>
+#include <cstdint>
+#include <cstdio>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/gofann.h"
+
+namespace gofann {
+
+// ----------------------------------------------------------------- host
+void set_error(const char* fmt, ...);
+int fail(int status, const char* fmt, ...);
+int cuda_status(cudaError_t err, const char* what);
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+int sm_count();
+
+#define GOFANN_CHECK_LAUNCH(what)                                      \
+    do {                                                               \
+        cudaError_t _e = cudaGetLastError();                           \
+        if (_e != cudaSuccess) return ::gofann::cuda_status(_e, what); \
+    } while (0)
+
+constexpr uint32_t kU32Max = 0xffffffffu;
+constexpr uint32_t kPoolUsed = 0x80000000u;
+constexpr int kWarp = 32;
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kHashCap = GOFANN_HASH_CAPACITY;
+
+// --------------------------------------------------- float order helpers
+// Lane-0 value of `v += __shfl_xor_sync(v, off)` for off = 16..1, replayed
+// inside one thread from the 32 lane partials (backend_pq.cu:4716-4721).
+// Float addition is commutative, so lane i's step v[i] + v[i^off] equals
+// v[i] + v[i+off] for the lanes (i < off) that lane 0 depends on.
+__device__ __forceinline__ float butterfly_sum32(float (&v)[32])
+{
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+        for (int i = 0; i < off; ++i) v[i] = __fadd_rn(v[i], v[i + off]);
+    }
+    return v[0];
+}
+
+// ------------------------------------------------------------ visited hash
+// native_visited_hash.cuh:11-61: multiplicative mix modulo 4096, linear
+// probing, UINT32_MAX = empty, a full table silently drops the insert.
+__device__ __forceinline__ uint32_t hash_code(uint32_t v)
+{
+    const uint64_t mixed = static_cast<uint64_t>(v) ^
+                           (static_cast<uint64_t>(v >> 16) * 0x4bcb391f924ed183ULL) ^
+                           0xa0ab69ccd854fc0aULL;
+    return static_cast<uint32_t>(mixed % kHashCap);
+}
+__device__ __forceinline__ bool hash_test(const uint32_t* t, uint32_t v)
+{
+    uint32_t s = hash_code(v);
+    for (int p = 0; p < kHashCap; ++p) {
+        const uint32_t x = t[s];
+        if (x == kU32Max) return false;
+        if (x == v) return true;
+        s = (s + 1) & (kHashCap - 1);
+    }
+    return false;
+}
+__device__ __forceinline__ void hash_add(uint32_t* t, uint32_t v)
+{
+    uint32_t s = hash_code(v);
+    for (int p = 0; p < kHashCap; ++p) {
+        const uint32_t x = t[s];
+        if (x == v) return;
+        if (x == kU32Max) { t[s] = v; return; }
+        s = (s + 1) & (kHashCap - 1);
+    }
+}
+
+// ---------------------------------------------------------------- frontier
+// Frontier entry: priority, local row | used bit, unbiased score
+// (gpu_predicate::BiasedPair, gpu_predicate_index.cuh:137-144).
+struct FPair {
+    float first;
+    uint32_t second;
+    float base;
+};
+
+__device__ __forceinline__ void fswap(FPair& a, FPair& b) { FPair t = a; a = b; b = t; }
+
+// Symmetric min-max heap, include/smmh2.h:8-148 (index 0 unused, 1 = min,
+// 2 = max; entries compare by `first`).
+__device__ __forceinline__ int smmh_adjust_sibling(FPair* h, int y, int size)
+{
+    if (y & 1) {
+        const int s = y + 1;
+        if (s >= size) return y;
+        if (h[y].first > h[s].first) { fswap(h[y], h[s]); return s; }
+    } else {
+        const int s = y - 1;
+        if (h[y].first < h[s].first) { fswap(h[y], h[s]); return s; }
+    }
+    return y;
+}
+__device__ __forceinline__ int smmh_adjust_grandparent(FPair* h, int y)
+{
+    if (y <= 2) return y;
+    const int g = (y - 3) >> 2;
+    const int gl = 2 * g + 1, gr = 2 * g + 2;
+    if (h[gl].first > h[y].first) { fswap(h[gl], h[y]); return gl; }
+    if (h[gr].first < h[y].first) { fswap(h[gr], h[y]); return gr; }
+    return y;
+}
+__device__ __forceinline__ void smmh_insert(FPair* h, int& size, const FPair& e)
+{
+    int y = size;
+    h[size++] = e;
+    for (;;) {
+        y = smmh_adjust_sibling(h, y, size);
+        const int x = smmh_adjust_grandparent(h, y);
+        if (x == y) break;
+        y = x;
+    }
+}
+__device__ __forceinline__ int smmh_adjust_grandchild(FPair* h, int y, int size)
+{
+    if (y & 1) {
+        if (2 * y + 1 >= size) return y;
+        const int cl = 2 * y + 1, cr = 2 * (y + 1) + 1;
+        int c = cl;
+        if (cr < size && h[cr].first < h[cl].first) c = cr;
+        if (h[c].first < h[y].first) { fswap(h[c], h[y]); return c; }
+    } else {
+        const int cl = 2 * (y - 1) + 2, cr = 2 * y + 2;
+        if (cl >= size) return y;
+        int c = cl;
+        if (cr < size && h[cr].first > h[cl].first) c = cr;
+        if (h[c].first > h[y].first) { fswap(h[c], h[y]); return c; }
+    }
+    return y;
+}
+__device__ __forceinline__ void smmh_pop_max(FPair* h, int& size)
+{
+    h[2] = h[--size];
+    int y = 2;
+    for (;;) {
+        smmh_adjust_sibling(h, y, size);
+        const int x = smmh_adjust_grandchild(h, y, size);
+        if (x == y) break;
+        y = x;
+    }
+}
+
+// -------------------------------------------------------- binary max heaps
+// include/bin_heap.h:6-66 over entries with a float key `first`.
+template <class T>
+__device__ __forceinline__ void bheap_push(T* b, int n)
+{
+    int now = n - 1;
+    int parent = (now - 1) / 2;
+    while (now > 0 && b[parent].first < b[now].first) {
+        T t = b[now]; b[now] = b[parent]; b[parent] = t;
+        now = parent;
+        parent = (now - 1) / 2;
+    }
+}
+template <class T>
+__device__ __forceinline__ T bheap_pop(T* b, int n)
+{
+    T ret = b[0];
+    const int len = n - 1;
+    if (len <= 0) return ret;
+    b[0] = b[n - 1];
+    int now = 0;
+    while (now * 2 + 1 < len) {
+        const int l = now * 2 + 1, r = now * 2 + 2;
+        int nx = l;
+        if (r < len && b[l].first < b[r].first) nx = r;
+        if (!(b[now].first < b[nx].first)) break;
+        T t = b[now]; b[now] = b[nx]; b[nx] = t;
+        now = nx;
+    }
+    return ret;
+}
+struct RPair { float first; uint32_t second; };             // ResultPair
+struct SPair { float first; uint32_t pad; uint64_t second; }; // stop top-k entry
+
+// (dist, id) lexicographic order of posting_shortlist_heap.cuh:14-20.
+__device__ __forceinline__ bool pair_less(float ld, uint32_t li, float rd, uint32_t ri)
+{
+    return ld < rd || (ld == rd && li < ri);
+}
+
+// ---------------------------------------------------------------- filters
+struct AttrView {
+    const uint64_t* indptr;
+    const uint32_t* indices;
+    const float* ranges;
+    uint32_t n_samples;
+    uint32_t range_count;
+};
+
+__device__ __forceinline__ bool csr_contains(const AttrView& a, uint32_t sample, uint32_t label)
+{
+    uint64_t lo = a.indptr[sample], hi = a.indptr[sample + 1];
+    while (lo < hi) {
+        const uint64_t mid = lo + ((hi - lo) >> 1);
+        const uint32_t v = a.indices[mid];
+        if (v < label) lo = mid + 1; else hi = mid;
+    }
+    return lo < a.indptr[sample + 1] && a.indices[lo] == label;
+}
+__device__ __forceinline__ bool range_match(uint32_t mode, float lo, float hi, float v)
+{
+    switch (mode) {
+    case 0: return true;
+    case 1: return v > lo;
+    case 2: return v < hi;
+    case 3: return v >= lo && v < hi;
+    default: return false;
+    }
+}
+__device__ __forceinline__ bool pred_enabled(const gofann_routes& r, uint32_t route)
+{
+    if (!r.pred_offsets) return false;
+    return r.pred_enabled ? r.pred_enabled[route] != 0 : true;
+}
+// gpu_predicate::matches with clauses (gpu_predicate_index.cuh:109-136).
+__device__ __forceinline__ bool pred_matches(const gofann_routes& r, const AttrView& a,
+                                             uint32_t route, uint32_t sample)
+{
+    if (sample >= a.n_samples) return false;
+    const uint32_t e = r.pred_offsets[route + 1];
+    for (uint32_t i = r.pred_offsets[route]; i < e; ++i) {
+        const gofann_clause c = r.clauses[i];
+        bool pass = true;
+        for (uint32_t j = c.label_begin; pass && j < c.label_end; ++j)
+            pass = csr_contains(a, sample, r.pred_handles[j]);
+        for (uint32_t j = c.range_begin; pass && j < c.range_end; ++j) {
+            const gofann_range_atom at = r.pred_ranges[j];
+            pass = a.ranges != nullptr && at.dimension < a.range_count &&
+                   range_match(at.mode, at.lower, at.upper,
+                               a.ranges[static_cast<uint64_t>(sample) * a.range_count + at.dimension]);
+        }
+        if (pass) return true;
+    }
+    return false;
+}
+// resident_pq_labels_match (backend_pq.cu:3934-3965): every query label but
+// the route's primary one must be in the sample's row.
+__device__ __forceinline__ bool labels_match(const gofann_routes& r, const AttrView& a,
+                                             uint32_t route, uint32_t sample)
+{
+    if (!r.qlabel_indptr) return true;
+    const uint32_t primary = r.primary_label ? r.primary_label[route] : kU32Max;
+    const uint64_t e = r.qlabel_indptr[route + 1];
+    for (uint64_t p = r.qlabel_indptr[route]; p < e; ++p) {
+        const uint32_t l = r.qlabel_indices[p];
+        if (l == primary) continue;
+        if (!csr_contains(a, sample, l)) return false;
+    }
+    return true;
+}
+// gpu_predicate::priority (gpu_predicate_index.cuh:161-166).
+__device__ __forceinline__ float pred_priority(float base, float penalty, bool pass)
+{
+    if (pass || penalty == 0.0f || !isfinite(base) || base == FLT_MAX) return base;
+    if (base > FLT_MAX - penalty) return FLT_MAX;
+    return __fadd_rn(base, penalty);
+}
+
+// ------------------------------------------------------------ warp top-k
+// Smallest (dist, id) pairs with unique ids among `n` entries, selected by
+// `k` rounds of warp argmin.  An entry whose id was already taken is
+// skipped: an id's first selection carries its minimum distance, so the
+// result equals "dedup by id keeping the minimum distance, sort by
+// (dist, id), truncate to k" (rabitq_lowfreq_merge.h:773-813).  `get(i, d,
+// id)` loads entry i from any memory.  Lane 0 writes the k outputs.
+template <int kMaxK, class Get>
+__device__ __forceinline__ void warp_select_topk(int n, int k, Get get, uint32_t* out_ids, float* out_d,
+                                                 int lane)
+{
+    uint32_t sel[kMaxK];
+#pragma unroll
+    for (int r = 0; r < kMaxK; ++r) sel[r] = kU32Max;
+    for (int r = 0; r < k; ++r) {
+        float bd = FLT_MAX;
+        uint32_t bi = kU32Max;
+        int found = 0;
+        for (int i = lane; i < n; i += kWarp) {
+            float x;
+            uint32_t y;
+            get(i, x, y);
+            if (y == kU32Max) continue;
+            bool taken = false;
+#pragma unroll
+            for (int t = 0; t < kMaxK; ++t) taken |= (t < r) && sel[t] == y;
+            if (taken) continue;
+            if (!found || pair_less(x, y, bd, bi)) { bd = x; bi = y; found = 1; }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float od = __shfl_xor_sync(kFull, bd, off);
+            const uint32_t oi = __shfl_xor_sync(kFull, bi, off);
+            const int of = __shfl_xor_sync(kFull, found, off);
+            if (of && (!found || pair_less(od, oi, bd, bi))) { bd = od; bi = oi; found = 1; }
+        }
+        if (lane == 0) {
+            out_ids[r] = found ? bi : kU32Max;
+            out_d[r] = found ? bd : FLT_MAX;
+        }
+#pragma unroll
+        for (int t = 0; t < kMaxK; ++t)
+            if (t == r) sel[t] = found ? bi : kU32Max;
+    }
+}
+
+}  // namespace gofann

@@ -1,0 +1,91 @@
+// rq_device.cuh — device-side 1-bit RaBitQ estimator.
+//
+// The integer inner product sum_{d: bit(d)} q8[d] is computed from 8 bit
+// planes of u = q8 + 127 (0..254):  ip = sum_b 2^b popc(code & plane_b)
+// - 127 popc(code).  Integer sums are exact, so this equals the reference's
+// dp4a nibble-mask form (backend_rabitq.cu:3070-3098) bit for bit, with one
+// popc per plane per 32 dimensions instead of 8 dp4a + 8 table loads.
+// Code bit layout: dimension d is bit 31-(d%32) of little-endian word d/32.
+#pragma once
+
+#include "common.cuh"
+
+namespace gofann {
+
+constexpr int kMaxRqWords = 4096 / 32;  // padded_dim <= 4096
+
+// Builds the 8 bit planes [8][words] of one query into shared memory.
+// Cooperative over `nthreads` threads starting at `tid`.
+__device__ __forceinline__ void rq_build_planes(const int8_t* __restrict__ q8, int padded_dim,
+                                                uint32_t* planes, int tid, int nthreads)
+{
+    const int words = padded_dim / 32;
+    for (int w = tid; w < words; w += nthreads) {
+        uint32_t p[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int k = 0; k < 32; ++k) {
+            const uint32_t u = static_cast<uint32_t>(static_cast<int>(q8[w * 32 + k]) + 127);
+#pragma unroll
+            for (int b = 0; b < 8; ++b) p[b] |= ((u >> b) & 1u) << (31 - k);
+        }
+#pragma unroll
+        for (int b = 0; b < 8; ++b) planes[b * words + w] = p[b];
+    }
+}
+
+__device__ __forceinline__ int32_t rq_word_ip(uint32_t code_w, const uint32_t* planes, int words, int w)
+{
+    int32_t acc = 0;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) acc += __popc(code_w & planes[b * words + w]) << b;
+    return acc - 127 * __popc(code_w);
+}
+
+// Whole-code inner product by one thread (codes 16-byte aligned when
+// code_bytes % 16 == 0).
+__device__ __forceinline__ int32_t rq_ip_thread(const uint8_t* __restrict__ code, const uint32_t* planes,
+                                                int words)
+{
+    int32_t acc = 0;
+    if ((words & 3) == 0 && (reinterpret_cast<uintptr_t>(code) & 15) == 0) {
+        const uint4* p = reinterpret_cast<const uint4*>(code);
+        for (int i = 0; i < words / 4; ++i) {
+            const uint4 x = __ldg(p + i);
+            acc += rq_word_ip(x.x, planes, words, 4 * i + 0);
+            acc += rq_word_ip(x.y, planes, words, 4 * i + 1);
+            acc += rq_word_ip(x.z, planes, words, 4 * i + 2);
+            acc += rq_word_ip(x.w, planes, words, 4 * i + 3);
+        }
+    } else {
+        const uint32_t* p = reinterpret_cast<const uint32_t*>(code);
+        for (int i = 0; i < words; ++i) acc += rq_word_ip(__ldg(p + i), planes, words, i);
+    }
+    return acc;
+}
+
+// Combine of score_rabitq_code_device (backend_rabitq.cu:3185-3192), pinned
+// as fma(f_rescale, fma(float(ip), scale, k1xsumq), f_add + gdist).
+__device__ __forceinline__ float rq_combine(int32_t ip, float scale, float k1, float f_add,
+                                            float f_rescale, float gdist)
+{
+    const float t = __fmaf_rn(static_cast<float>(ip), scale, k1);
+    return __fmaf_rn(f_rescale, t, __fadd_rn(f_add, gdist));
+}
+
+struct RqQueryView {
+    const uint32_t* planes;  // [8][words] (shared memory)
+    float scale, k1;
+    const float* gdist;      // [num_anchors] of this query row
+};
+
+__device__ __forceinline__ float rq_estimate(const gofann_codes& c, const RqQueryView& q, uint32_t sample)
+{
+    const int words = static_cast<int>(c.padded_dim / 32);
+    const int32_t ip = rq_ip_thread(c.rq_codes + static_cast<size_t>(sample) * (c.padded_dim / 8), q.planes,
+                                    words);
+    const float f_add = __ldg(c.rq_factors + static_cast<size_t>(sample) * 3);
+    const float f_rescale = __ldg(c.rq_factors + static_cast<size_t>(sample) * 3 + 1);
+    const uint32_t anchor = __ldg(c.rq_anchor_ids + sample);
+    return rq_combine(ip, q.scale, q.k1, f_add, f_rescale, __ldg(q.gdist + anchor));
+}
+
+}  // namespace gofann

@@ -1,0 +1,131 @@
+"""Route planning: labelled queries -> graph routes and posting routes.
+
+Mirrors the reference's categorical routing (validate_and_prepare_queries,
+src/data/dataloader.cpp:10972; routing mode greedy_min_posting,
+dataloader.cpp:7833-7836) and its compiled predicate
+(route_predicate::compile, src/planning/route_predicate_plan.h:175-315):
+  * an AND query picks the label with the smallest posting as its route;
+  * a label with a graph group becomes a graph route seeded at the group's
+    seed row; otherwise the label's posting list is scanned;
+  * the full conjunction is compiled as one DNF clause and enabled whenever
+    it says more than the route's own label (a residual).
+Route tables are returned as numpy arrays in the gofann_routes layout.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _abi as A
+
+
+@dataclass
+class Plan:
+    graph_routes: dict           # gofann_routes arrays for the beam search
+    graph_query: np.ndarray      # [n_graph_routes] original query index
+    posting_routes: dict         # gofann_routes arrays for the posting scan
+    posting_query: np.ndarray
+    posting_begin: np.ndarray    # [n_posting_routes] u64 offsets into posting_ids
+    posting_count: np.ndarray    # [n_posting_routes] u32
+    n_queries: int
+
+    @property
+    def n_routes(self) -> int:
+        return int(self.graph_query.shape[0] + self.posting_query.shape[0])
+
+    def merge_tables(self):
+        """CSR of routes per original query over the concatenation
+        [graph routes ; posting routes] (route_to_original_query)."""
+        r2q = np.concatenate([self.graph_query, self.posting_query]).astype(np.int64)
+        order = np.argsort(r2q, kind="stable").astype(np.uint32)
+        counts = np.bincount(r2q, minlength=self.n_queries)
+        qoff = np.zeros(self.n_queries + 1, np.uint32)
+        qoff[1:] = np.cumsum(counts)
+        return qoff, order
+
+
+def _route_tables(qidx, labels_of, primary, group, start):
+    n = len(qidx)
+    indptr = np.zeros(n + 1, np.uint64)
+    lab = [labels_of[q] for q in qidx]
+    indptr[1:] = np.cumsum([len(x) for x in lab], dtype=np.uint64)
+    indices = np.concatenate(lab).astype(np.uint32) if n else np.zeros(0, np.uint32)
+    # one clause per route holding all query labels; enabled for residuals
+    clauses = np.zeros(n, A.CLAUSE_DTYPE)
+    clauses["label_begin"] = indptr[:-1].astype(np.uint32)
+    clauses["label_end"] = indptr[1:].astype(np.uint32)
+    pred_offsets = np.arange(n + 1, dtype=np.uint32)
+    enabled = np.array([len(x) > 1 for x in lab], np.uint8)
+    return {
+        "query_row": np.asarray(qidx, np.uint32),
+        "group_id": np.asarray(group, np.uint32),
+        "start_local": np.asarray(start, np.uint32),
+        "qlabel_indptr": indptr,
+        "qlabel_indices": indices,
+        "primary_label": np.asarray(primary, np.uint32),
+        "pred_offsets": pred_offsets,
+        "clauses": clauses,
+        "pred_handles": indices.copy(),
+        "pred_enabled": enabled,
+    }
+
+
+def plan_queries(index, query_labels: list) -> Plan:
+    """greedy_min_posting routing of AND-of-labels queries."""
+    card = index.posting_count
+    g_q, g_p, g_grp, g_start = [], [], [], []
+    p_q, p_p, p_b, p_c = [], [], [], []
+    for qi, labs in enumerate(query_labels):
+        labs = np.asarray(labs, np.uint32)
+        lab = int(labs[np.argmin(card[labs])])
+        grp = int(index.label_group[lab])
+        if grp >= 0:
+            g_q.append(qi); g_p.append(lab); g_grp.append(grp); g_start.append(int(index.seeds[grp]))
+        else:
+            p_q.append(qi); p_p.append(lab)
+            p_b.append(int(index.posting_begin[lab])); p_c.append(int(index.posting_count[lab]))
+    labels_of = [np.asarray(x, np.uint32) for x in query_labels]
+    graph = _route_tables(g_q, labels_of, g_p, g_grp, g_start)
+    post = _route_tables(p_q, labels_of, p_p, np.zeros(len(p_q), np.uint32), np.zeros(len(p_q), np.uint32))
+    return Plan(graph, np.asarray(g_q, np.uint32), post, np.asarray(p_q, np.uint32),
+                np.asarray(p_b, np.uint64), np.asarray(p_c, np.uint32), len(query_labels))
+
+
+def subset_routes(routes: dict, sel: np.ndarray) -> dict:
+    """Route tables restricted to the routes `sel` (label CSR re-based)."""
+    sel = np.asarray(sel, np.int64)
+    out = {}
+    for k in ("query_row", "group_id", "start_local", "primary_label", "pred_enabled"):
+        out[k] = np.ascontiguousarray(routes[k][sel])
+    ip = routes["qlabel_indptr"]
+    lab = [routes["qlabel_indices"][ip[i]:ip[i + 1]] for i in sel]
+    n = len(sel)
+    indptr = np.zeros(n + 1, np.uint64)
+    indptr[1:] = np.cumsum([len(x) for x in lab], dtype=np.uint64)
+    indices = np.concatenate(lab).astype(np.uint32) if n else np.zeros(0, np.uint32)
+    clauses = np.zeros(n, A.CLAUSE_DTYPE)
+    clauses["label_begin"] = indptr[:-1].astype(np.uint32)
+    clauses["label_end"] = indptr[1:].astype(np.uint32)
+    out.update(qlabel_indptr=indptr, qlabel_indices=indices, pred_offsets=np.arange(n + 1, dtype=np.uint32),
+               clauses=clauses, pred_handles=indices.copy())
+    return out
+
+
+def concat_routes(a: dict, b: dict) -> dict:
+    """Route tables of `a` followed by those of `b`."""
+    na, nb = a["query_row"].shape[0], b["query_row"].shape[0]
+    both = subset_routes(a, np.arange(na))
+    sb = subset_routes(b, np.arange(nb))
+    out = {}
+    for k in ("query_row", "group_id", "start_local", "primary_label", "pred_enabled"):
+        out[k] = np.concatenate([both[k], sb[k]])
+    ip = np.concatenate([both["qlabel_indptr"], sb["qlabel_indptr"][1:] + both["qlabel_indptr"][-1]])
+    ind = np.concatenate([both["qlabel_indices"], sb["qlabel_indices"]]).astype(np.uint32)
+    n = na + nb
+    clauses = np.zeros(n, A.CLAUSE_DTYPE)
+    clauses["label_begin"] = ip[:-1].astype(np.uint32)
+    clauses["label_end"] = ip[1:].astype(np.uint32)
+    out.update(qlabel_indptr=ip.astype(np.uint64), qlabel_indices=ind, pred_offsets=np.arange(n + 1, dtype=np.uint32),
+               clauses=clauses, pred_handles=ind.copy())
+    return out

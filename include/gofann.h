@@ -1,0 +1,286 @@
+/*
+ * gofann.h — C ABI of the B200 filtered-ANN search path.
+ *
+ * Every entry point takes plain pointers, sizes and a CUDA stream passed as
+ * `void*` (NULL = legacy default stream).  Pointers documented as "device"
+ * must be device-resident (cudaMalloc / torch CUDA storage); pointers
+ * documented as "host" are ordinary host memory.  No entry point throws; each
+ * returns a gofann_status (0 = success, negative = error) and records a
+ * message readable through gofann_last_error() on the calling thread.
+ *
+ * The interfaces replace, one for one, the device halves of the reference's
+ * search backends (putatio13/GO-FANN):
+ *   gofann_pq_build_lut       computePQTable          src/search/pq/backend_pq.cu:1999-2022
+ *   gofann_pq_adc             PQ neighbour scoring    src/search/pq/backend_pq.cu:4711-4725
+ *   gofann_pq_encode          pq::transform (encode)  tools/quantization/pq_builder.cu:125-151
+ *   gofann_rabitq_quantize    quantize_rabitq_queries_int8_kernel + compute_rabitq_query_factors_kernel
+ *                                                     src/search/rabitq/backend_rabitq.cu:2898-2964
+ *   gofann_rabitq_score       score_rabitq_code_device<kUseInt8Score=true>
+ *                                                     src/search/rabitq/backend_rabitq.cu:3100-3200
+ *   gofann_beam_search        native_warp_independent_search_kernel_impl (device-resident)
+ *                                                     src/search/pq/backend_pq.cu:3988-5199,
+ *                             native_rabitq_search_kernel src/search/rabitq/backend_rabitq.cu:3496-4299
+ *   gofann_posting_scan       lowfreq_pq_scan_kernel  src/search/pq/backend_pq.cu:2046-2185,
+ *                             lowfreq_rabitq_scan_kernel src/search/rabitq/backend_rabitq.cu:5396-5751
+ *   gofann_rerank             resident_pq_batch_exact_rerank_kernel src/search/pq/backend_pq.cu:5201-5310,
+ *                             highfreq_float_gpu_l2/topk_kernel src/search/rabitq/backend_rabitq.cu:6173-6270,
+ *                             highfreq_host_batch_rerank_range src/search/pq/backend_pq.cu:2479-2592
+ *   gofann_route_merge        merge_route_results_to_original src/search/rabitq/rabitq_lowfreq_merge.h:710-815
+ *   gofann_shard_merge        (no reference counterpart: the reference is single-GPU; the merge
+ *                             order is the (dist, id) rule of rabitq_lowfreq_merge.h:800-806)
+ */
+#ifndef GOFANN_H
+#define GOFANN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GOFANN_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define GOFANN_API __attribute__((visibility("default")))
+#else
+#define GOFANN_API
+#endif
+
+typedef enum gofann_status {
+    GOFANN_OK = 0,
+    GOFANN_ERR_INVALID = -1,     /* bad argument / shape / null pointer */
+    GOFANN_ERR_CUDA = -2,        /* a CUDA runtime call failed */
+    GOFANN_ERR_UNSUPPORTED = -3, /* shape outside the compiled limits */
+    GOFANN_ERR_CAPACITY = -4,    /* a device capacity was exceeded */
+    GOFANN_ERR_TIMEOUT = -5      /* a bounded device wait ran out */
+} gofann_status;
+
+/* Compiled limits (backend_pq.cu:66-75, runtime_defaults.h:30-52). */
+#define GOFANN_MAX_DEGREE 64
+#define GOFANN_MAX_QUEUE 512
+#define GOFANN_MAX_TOPK 10
+#define GOFANN_MAX_RESULT_WIDTH 512
+#define GOFANN_MAX_SHORTLIST 400
+#define GOFANN_PQ_CENTROIDS 256
+#define GOFANN_HASH_CAPACITY 4096
+
+enum { GOFANN_EARLY_STOP_FIXED = 0, GOFANN_EARLY_STOP_OFF = 1, GOFANN_EARLY_STOP_ADAPTIVE = 2 };
+enum { GOFANN_SCORER_PQ = 0, GOFANN_SCORER_RABITQ = 1 };
+enum { GOFANN_DTYPE_U8 = 0, GOFANN_DTYPE_F32 = 1, GOFANN_DTYPE_F16 = 2 };
+
+/* DNF clause over label handles and range atoms (gpu_predicate_index.cuh:24-25). */
+typedef struct gofann_clause {
+    uint32_t label_begin, label_end, range_begin, range_end;
+} gofann_clause;
+
+/* Range atom: mode 0 any, 1 v>lower, 2 v<upper, 3 lower<=v<upper (range_filter.cuh:28-45). */
+typedef struct gofann_range_atom {
+    uint32_t dimension, mode;
+    float lower, upper;
+} gofann_range_atom;
+
+/* Concatenated per-label graphs: row = label_offset[group] + local_row
+ * (GraphRuntime::graph + GraphMetadata, dataloader.h:583-602,753-836). */
+typedef struct gofann_graph {
+    const uint32_t* adjacency;       /* device [total_rows][degree], UINT32_MAX padding */
+    const uint32_t* row_to_sample;   /* device [total_rows] */
+    const uint64_t* row_filter_mask; /* device [total_rows], or NULL = implicit all-ones */
+    const uint32_t* label_offset;    /* device [group_count] */
+    uint32_t total_rows;
+    uint32_t degree;
+    uint32_t group_count;
+    uint32_t reserved;
+} gofann_graph;
+
+/* Per-sample attributes: sample-major label CSR (sorted, unique per row) and
+ * float range values (SparseLabelMatrix / base_range_values). */
+typedef struct gofann_attrs {
+    const uint64_t* label_indptr;  /* device [n_samples+1] */
+    const uint32_t* label_indices; /* device [nnz] */
+    const float* range_values;     /* device [n_samples][range_count] or NULL */
+    uint32_t n_samples;
+    uint32_t range_count;
+} gofann_attrs;
+
+/* Navigation codes.  PQ: uint8 [n][pq_dim] (pq.codes.bin rows).  RaBitQ:
+ * 1-bit codes [n][padded_dim/8] stored as little-endian uint32 words with
+ * dimension d at bit 31-(d%32) of word d/32, factors [n][3] = (f_add,
+ * f_rescale, f_err), anchor ids [n] (RabitqArtifactHeader v2 payload). */
+typedef struct gofann_codes {
+    const uint8_t* pq_codes;
+    uint32_t pq_dim;
+    uint32_t n_samples;
+    const uint8_t* rq_codes;
+    const float* rq_factors;
+    const uint32_t* rq_anchor_ids;
+    uint32_t padded_dim;
+    uint32_t num_anchors;
+} gofann_codes;
+
+/* Per-query prepared state.  PQ: lut [n_rows][pq_dim][256].  RaBitQ: int8
+ * query [n_rows][padded_dim], scale [n_rows], k1xsumq [n_rows], centroid
+ * distances [n_rows][num_anchors]. */
+typedef struct gofann_prepared {
+    const float* pq_lut;
+    const int8_t* rq_q8;
+    const float* rq_scale;
+    const float* rq_k1xsumq;
+    const float* rq_centroid_dist;
+    uint32_t n_rows;
+    uint32_t reserved;
+} gofann_prepared;
+
+/* Routed queries (GraphRuntime route tables + gpu_predicate::View).  Every
+ * per-route pointer except query_row, group_id and start_local may be NULL. */
+typedef struct gofann_routes {
+    uint32_t n_routes;
+    uint32_t range_count;
+    const uint32_t* query_row;   /* route -> row of gofann_prepared */
+    const uint32_t* group_id;    /* route -> graph group (query_group_ids) */
+    const uint32_t* start_local; /* route -> seed local row (start_local_ids) */
+    const uint64_t* filter_bits; /* route -> query_filter_bits; NULL = always match */
+    const uint8_t* range_modes;  /* [n_routes][range_count] */
+    const float* range_lower;
+    const float* range_upper;
+    /* residual label check (resident_pq_labels_match, backend_pq.cu:3934-3965) */
+    const uint64_t* qlabel_indptr;  /* [n_routes+1] */
+    const uint32_t* qlabel_indices; /* labels every result must carry */
+    const uint32_t* primary_label;  /* [n_routes] label covered by the route itself */
+    /* compiled DNF predicate (gpu_predicate::View with clauses) */
+    const uint32_t* pred_offsets;   /* [n_routes+1] into clauses, or NULL = no predicate */
+    const gofann_clause* clauses;
+    const uint32_t* pred_handles;
+    const gofann_range_atom* pred_ranges;
+    const uint8_t* pred_enabled;    /* [n_routes] or NULL = enabled iff pred_offsets */
+    const uint8_t* route_compiled;  /* [n_routes] or NULL */
+} gofann_routes;
+
+typedef struct gofann_search_params {
+    int32_t queue_size;      /* beam / search_queue_size, 1..512 */
+    int32_t stop_width;      /* topk used by the stop rule, 1..10 */
+    int32_t result_width;    /* shortlist emitted per route, 1..512 */
+    int32_t finish_limit;    /* search_finish_count (fixed mode) */
+    int32_t early_stop_mode; /* GOFANN_EARLY_STOP_* */
+    int32_t max_steps;       /* 0 = unlimited */
+    int32_t scorer;          /* GOFANN_SCORER_* */
+    int32_t predicate_bias;  /* 1 = penalise frontier entries failing the DNF */
+    float alpha;             /* predicate_bias_alpha */
+    int32_t pending_base_stop;
+    int32_t full_label_check;     /* 1 = resident residual label check on expansion */
+    int32_t lut_in_shared;        /* PQ: 1 = stage the LUT in shared memory */
+} gofann_search_params;
+
+/* Per-route device counters written by gofann_beam_search (may be NULL):
+ * [n_routes][4] = expanded nodes, distance evaluations, predicate probes,
+ * frontier admissions. */
+typedef struct gofann_search_out {
+    uint32_t* ids;      /* device [n_routes][result_width], UINT32_MAX fill */
+    float* dists;       /* device [n_routes][result_width], FLT_MAX fill */
+    int32_t* steps;     /* device [n_routes] or NULL */
+    uint32_t* counters; /* device [n_routes][4] or NULL */
+    int32_t* status;    /* device [1] error word or NULL */
+} gofann_search_out;
+
+/* ---------------------------------------------------------------- basics */
+GOFANN_API int gofann_abi_version(void);
+GOFANN_API const char* gofann_last_error(void);
+/* Number of streaming multiprocessors of the current device (0 on error). */
+GOFANN_API int gofann_device_sm_count(void);
+
+/* ------------------------------------------------------------- PQ stages */
+/* LUT [n][pq_dim][256]: sum over the subvector of fma(diff, diff, acc) with
+ * diff = q - c, sequential in d (computePQTable, backend_pq.cu:1999-2022).
+ * queries: device [n][dim] of dtype u8 or f32; centroids: device [256][dim]
+ * (pivots + mean, backend_pq.cu:1812-1815). */
+GOFANN_API int gofann_pq_build_lut(const void* queries, int query_dtype, uint32_t n, uint32_t dim,
+                        const float* centroids, uint32_t pq_dim, float* lut_out, void* stream);
+
+/* ADC for n_pairs (query row, sample) pairs with the reference's warp order:
+ * lane j sums subspaces j, j+32 sequentially, then an xor butterfly
+ * 16,8,4,2,1 (backend_pq.cu:4711-4725). */
+GOFANN_API int gofann_pq_adc(const float* lut, uint32_t pq_dim, const uint8_t* codes,
+                  const uint32_t* pair_row, const uint32_t* pair_sample, uint32_t n_pairs,
+                  float* dist_out, void* stream);
+
+/* Nearest-centroid PQ encoding (argmin, lowest centroid index on ties). */
+GOFANN_API int gofann_pq_encode(const void* vectors, int dtype, uint32_t n, uint32_t dim,
+                     const float* centroids, uint32_t pq_dim, uint8_t* codes_out, void* stream);
+
+/* --------------------------------------------------------- RaBitQ stages */
+/* From rotated queries [n][padded_dim] (f32): int8 query, scale =
+ * max|q|/127 (1 if 0), q8 = clamp(rint(q/scale), -127, 127), k1xsumq =
+ * -0.5*sum(q) (backend_rabitq.cu:2898-2964). */
+GOFANN_API int gofann_rabitq_quantize(const float* rotated, uint32_t n, uint32_t padded_dim,
+                           int8_t* q8_out, float* scale_out, float* k1xsumq_out, void* stream);
+
+/* gdist[q][a] = max(0, |q|^2 + |c_a|^2 - 2 q.c_a) (rabitq_query_rotation.cuh:89-113). */
+GOFANN_API int gofann_rabitq_centroid_dist(const float* rotated, uint32_t n, const float* anchors,
+                                uint32_t num_anchors, uint32_t padded_dim, float* gdist_out,
+                                void* stream);
+
+/* 1-bit int8 estimator for pairs (backend_rabitq.cu:3100-3200):
+ * est = (f_add + gdist) + f_rescale * (float(ip_int) * scale + k1xsumq). */
+GOFANN_API int gofann_rabitq_score(const gofann_codes* codes, const gofann_prepared* prep,
+                        const uint32_t* pair_row, const uint32_t* pair_sample, uint32_t n_pairs,
+                        float* dist_out, int32_t* ip_int_out, void* stream);
+
+/* ----------------------------------------------------------- traversal */
+/* Bytes of device scratch gofann_beam_search needs for n_routes routes
+ * (one 4096-slot visited table per resident warp). */
+GOFANN_API size_t gofann_beam_search_scratch_bytes(uint32_t n_routes);
+
+/* Filtered graph beam search, one warp per route (backend_pq.cu:3988-5013). */
+GOFANN_API int gofann_beam_search(const gofann_graph* graph, const gofann_attrs* attrs,
+                       const gofann_codes* codes, const gofann_prepared* prep,
+                       const gofann_routes* routes, const gofann_search_params* params,
+                       const gofann_search_out* out, void* scratch, size_t scratch_bytes,
+                       void* stream);
+
+/* ------------------------------------------------------- posting scans */
+/* Brute-force scan of each route's posting slice [begin, begin+count) of
+ * posting_ids, DNF filter (before scoring, or after a can-enter test when
+ * score_first), top-shortlist_k by (dist, id) (backend_pq.cu:2046-2134). PQ
+ * distances are sequential sums over subspaces (backend_pq.cu:2101-2104). */
+GOFANN_API int gofann_posting_scan(const gofann_codes* codes, const gofann_prepared* prep,
+                        const gofann_attrs* attrs, const gofann_routes* routes, int scorer,
+                        const uint32_t* posting_ids, const uint64_t* route_begin,
+                        const uint32_t* route_count, int32_t shortlist_k, int32_t score_first,
+                        uint32_t* out_ids, float* out_dists, void* stream);
+
+/* ---------------------------------------------------------- exact rerank */
+/* Exact L2 of each candidate against its query row, residual label check
+ * (every label of qlabel_indices except primary_label), duplicates dropped,
+ * top-k ascending by (dist, id) (backend_pq.cu:2479-2592, 5201-5310).
+ * base: device [n_samples][dim] of dtype; queries: device [n_rows][dim],
+ * u8 for a u8 base, f32 otherwise. routes supplies query_row and the residual
+ * label tables (may be NULL for no check). */
+GOFANN_API int gofann_rerank(const void* base, int dtype, uint32_t n_samples, uint32_t dim,
+                  const void* queries, const gofann_attrs* attrs, const gofann_routes* routes,
+                  const uint32_t* cand_ids, uint32_t width, int32_t topk,
+                  uint32_t* out_ids, float* out_dists, void* stream);
+
+/* --------------------------------------------------------------- merges */
+/* Route -> original query merge: dedup by id keeping the min distance, sort
+ * by (dist, id), truncate to topk, UINT32_MAX / FLT_MAX fill
+ * (rabitq_lowfreq_merge.h:710-815). query_route_offsets [n_queries+1] and
+ * query_routes list the routes of each original query. */
+GOFANN_API int gofann_route_merge(const uint32_t* route_ids, const float* route_dists, uint32_t width,
+                       const uint32_t* query_route_offsets, const uint32_t* query_routes,
+                       uint32_t n_queries, int32_t topk, uint32_t* out_ids, float* out_dists,
+                       void* stream);
+
+/* Shard merge: per query, n_shards sorted top-k lists (ids already global)
+ * laid out [n_shards][n_queries][k] -> top-k by (dist, id). */
+GOFANN_API int gofann_shard_merge(const uint32_t* shard_ids, const float* shard_dists, uint32_t n_shards,
+                       uint32_t n_queries, int32_t topk, uint32_t* out_ids, float* out_dists,
+                       void* stream);
+
+/* Adds base to every id that is not UINT32_MAX (local -> global shard ids). */
+GOFANN_API int gofann_offset_ids(uint32_t* ids, size_t n, uint32_t base, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GOFANN_H */

@@ -1,0 +1,416 @@
+"""GPU parity: every CUDA stage against the CPU oracle on the same seeded
+inputs, called through the C ABI (libgofann_b200.so).
+
+Bit-exact: PQ LUT / ADC / codes, RaBitQ int8 query, scale, k1xsumq, integer
+inner products and estimates, traversal ids + distances + steps + counters,
+posting shortlists, uint8 rerank, merges.  Tolerance: f32 rerank 1e-5
+relative, f16 rerank 1e-3 relative (ids compared up to ties within that
+tolerance), centroid distances 1e-3 + 2e-5 x against FP64
+(rabitq_query_rotation_test.cu:48-50).
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from fixtures import cfg1_small, cfg2_small, dev, dev_dict, fbits, host, rabitq_artifacts
+from gofann import _abi as A
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def L():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return A.lib()
+
+
+def stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+# ------------------------------------------------------------------ PQ stages
+@pytest.mark.parametrize("dim,pq_dim,qdtype", [(128, 32, "f32"), (192, 48, "u8"), (96, 16, "f32"), (64, 64, "u8"),
+                                               (256, 128, "f32")])
+def test_pq_lut_bitexact(L, dim, pq_dim, qdtype):
+    rng = np.random.default_rng(dim + pq_dim)
+    n = 37
+    if qdtype == "u8":
+        q = rng.integers(0, 256, size=(n, dim)).astype(np.uint8)
+        cent = rng.uniform(0, 255, size=(256, dim)).astype(np.float32)
+    else:
+        q = rng.standard_normal((n, dim)).astype(np.float32)
+        cent = rng.standard_normal((256, dim)).astype(np.float32)
+    want = O.pq_build_lut(q.astype(np.float32), cent, pq_dim)
+    lut = torch.empty((n, pq_dim, 256), dtype=torch.float32, device="cuda")
+    A.check(L.gofann_pq_build_lut(A.ptr(dev(q)), A.DTYPE_U8 if qdtype == "u8" else A.DTYPE_F32, n, dim,
+                                  A.ptr(dev(cent)), pq_dim, A.ptr(lut), stream()), "lut")
+    torch.cuda.synchronize()
+    assert np.array_equal(fbits(lut.cpu().numpy()), fbits(want))
+
+
+@pytest.mark.parametrize("pq_dim", [16, 24, 32, 48, 64, 96, 128])
+def test_pq_adc_bitexact(L, pq_dim):
+    rng = np.random.default_rng(pq_dim)
+    n_rows, n_samples, n_pairs = 11, 500, 4000
+    lut = rng.uniform(0, 100, size=(n_rows, pq_dim, 256)).astype(np.float32)
+    codes = rng.integers(0, 256, size=(n_samples, pq_dim)).astype(np.uint8)
+    pr = rng.integers(0, n_rows, size=n_pairs).astype(np.uint32)
+    ps = rng.integers(0, n_samples, size=n_pairs).astype(np.uint32)
+    want = O.pq_adc(lut, codes, pr, ps)
+    out = torch.empty(n_pairs, dtype=torch.float32, device="cuda")
+    A.check(L.gofann_pq_adc(A.ptr(dev(lut)), pq_dim, A.ptr(dev(codes)), A.ptr(dev(pr)), A.ptr(dev(ps)), n_pairs,
+                            A.ptr(out), stream()), "adc")
+    assert np.array_equal(fbits(out.cpu().numpy()), fbits(want))
+
+
+@pytest.mark.parametrize("dim,pq_dim,dtype", [(128, 32, "f32"), (192, 48, "u8")])
+def test_pq_encode_bitexact(L, dim, pq_dim, dtype):
+    rng = np.random.default_rng(7)
+    n = 3000
+    x = (rng.integers(0, 256, size=(n, dim)).astype(np.uint8) if dtype == "u8"
+         else rng.standard_normal((n, dim)).astype(np.float32))
+    cent = x[rng.choice(n, 256, replace=False)].astype(np.float32)
+    want = O.pq_encode(x.astype(np.float32), cent, pq_dim)
+    out = torch.empty((n, pq_dim), dtype=torch.uint8, device="cuda")
+    A.check(L.gofann_pq_encode(A.ptr(dev(x)), A.DTYPE_U8 if dtype == "u8" else A.DTYPE_F32, n, dim,
+                               A.ptr(dev(cent)), pq_dim, A.ptr(out), stream()), "encode")
+    assert np.array_equal(out.cpu().numpy(), want)
+
+
+# -------------------------------------------------------------- RaBitQ
+@pytest.mark.parametrize("pd", [64, 512, 4096])
+def test_rabitq_quantize_bitexact(L, pd):
+    rng = np.random.default_rng(pd)
+    n = 29
+    r = rng.standard_normal((n, pd)).astype(np.float32)
+    r[3] = 0.0  # zero query -> scale 1
+    r[4, :5] = [127.5, -127.5, 0.5, -0.5, 1.5]
+    q8, scale, k1 = O.rabitq_quantize(r)
+    gq8 = torch.empty((n, pd), dtype=torch.int8, device="cuda")
+    gs = torch.empty(n, dtype=torch.float32, device="cuda")
+    gk = torch.empty(n, dtype=torch.float32, device="cuda")
+    A.check(L.gofann_rabitq_quantize(A.ptr(dev(r)), n, pd, A.ptr(gq8), A.ptr(gs), A.ptr(gk), stream()), "quantize")
+    assert np.array_equal(gq8.cpu().numpy(), q8)
+    assert np.array_equal(fbits(gs.cpu().numpy()), fbits(scale))
+    assert np.array_equal(fbits(gk.cpu().numpy()), fbits(k1))
+
+
+def test_rabitq_centroid_dist_tolerance(L):
+    rng = np.random.default_rng(5)
+    n, a, pd = 17, 33, 512
+    q = rng.standard_normal((n, pd)).astype(np.float32)
+    c = rng.standard_normal((a, pd)).astype(np.float32)
+    want = ((q[:, None, :].astype(np.float64) - c[None].astype(np.float64)) ** 2).sum(-1)
+    out = torch.empty((n, a), dtype=torch.float32, device="cuda")
+    A.check(L.gofann_rabitq_centroid_dist(A.ptr(dev(q)), n, A.ptr(dev(c)), a, pd, A.ptr(out), stream()), "gdist")
+    got = out.cpu().numpy().astype(np.float64)
+    assert np.all(np.abs(got - want) <= 1e-3 + 2e-5 * np.abs(want))
+
+
+def _rq_prepared(L, qr, anchors):
+    n, pd = qr.shape
+    gq8 = torch.empty((n, pd), dtype=torch.int8, device="cuda")
+    gs = torch.empty(n, dtype=torch.float32, device="cuda")
+    gk = torch.empty(n, dtype=torch.float32, device="cuda")
+    gd = torch.empty((n, anchors.shape[0]), dtype=torch.float32, device="cuda")
+    A.check(L.gofann_rabitq_quantize(A.ptr(dev(qr)), n, pd, A.ptr(gq8), A.ptr(gs), A.ptr(gk), stream()), "quantize")
+    A.check(L.gofann_rabitq_centroid_dist(A.ptr(dev(qr)), n, A.ptr(dev(anchors)), anchors.shape[0], pd, A.ptr(gd),
+                                          stream()), "gdist")
+    torch.cuda.synchronize()
+    dprep = {"rq_q8": gq8, "rq_scale": gs, "rq_k1xsumq": gk, "rq_centroid_dist": gd}
+    hprep = {"rq_q8": gq8.cpu().numpy(), "rq_scale": gs.cpu().numpy(), "rq_k1xsumq": gk.cpu().numpy(),
+             "rq_centroid_dist": gd.cpu().numpy()}
+    return dprep, hprep
+
+
+def test_rabitq_score_bitexact(L):
+    w, idx, plan, rq, anchors, qr = rabitq_artifacts()
+    dprep, hprep = _rq_prepared(L, qr, anchors)
+    rng = np.random.default_rng(11)
+    n_pairs = 5000
+    pr = rng.integers(0, qr.shape[0], size=n_pairs).astype(np.uint32)
+    ps = rng.integers(0, w.n, size=n_pairs).astype(np.uint32)
+    want, want_ip = O.rabitq_score(rq, hprep, pr, ps)
+    dcodes = dev_dict(rq)
+    cs, pp = A.fill_codes(dcodes), A.fill_prepared(dprep)
+    out = torch.empty(n_pairs, dtype=torch.float32, device="cuda")
+    ip = torch.empty(n_pairs, dtype=torch.int32, device="cuda")
+    A.check(L.gofann_rabitq_score(C.byref(cs), C.byref(pp), A.ptr(dev(pr)), A.ptr(dev(ps)), n_pairs, A.ptr(out),
+                                  A.ptr(ip), stream()), "rq score")
+    assert np.array_equal(ip.cpu().numpy(), want_ip)
+    assert np.array_equal(fbits(out.cpu().numpy()), fbits(want))
+
+
+# ----------------------------------------------------------- traversal
+def run_gpu_beam(L, graph, attrs, codes, prep, routes, **params):
+    dg, da, dc, dp, dr = dev_dict(graph), dev_dict(attrs), dev_dict(codes), prep, dev_dict(routes)
+    gs, at, cs, ps, rs = A.fill_graph(dg), A.fill_attrs(da), A.fill_codes(dc), A.fill_prepared(dp), A.fill_routes(dr)
+    sp = A.fill_params(**params)
+    n, rw = rs.n_routes, sp.result_width
+    ids = torch.empty((n, rw), dtype=torch.int32, device="cuda")
+    d = torch.empty((n, rw), dtype=torch.float32, device="cuda")
+    steps = torch.empty(n, dtype=torch.int32, device="cuda")
+    cnt = torch.empty((n, 4), dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = A.SearchOut(ids=A.ptr(ids), dists=A.ptr(d), steps=A.ptr(steps), counters=A.ptr(cnt), status=A.ptr(status))
+    nbytes = L.gofann_beam_search_scratch_bytes(n)
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    A.check(L.gofann_beam_search(C.byref(gs), C.byref(at), C.byref(cs), C.byref(ps), C.byref(rs), C.byref(sp),
+                                 C.byref(out), A.ptr(scratch), nbytes, stream()), "beam_search")
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    return host(ids, np.uint32), d.cpu().numpy(), steps.cpu().numpy(), host(cnt, np.uint32)
+
+
+BEAM_VARIANTS = [
+    dict(queue_size=64, predicate_bias=1, early_stop_mode=A.EARLY_STOP_ADAPTIVE, result_width=100),
+    dict(queue_size=16, predicate_bias=0, early_stop_mode=A.EARLY_STOP_FIXED, finish_limit=20, result_width=50),
+    dict(queue_size=200, predicate_bias=1, early_stop_mode=A.EARLY_STOP_FIXED, finish_limit=100, result_width=512,
+         lut_in_shared=1),
+    dict(queue_size=512, predicate_bias=0, early_stop_mode=A.EARLY_STOP_OFF, max_steps=300, result_width=100,
+         lut_in_shared=1),
+    dict(queue_size=2, predicate_bias=1, early_stop_mode=A.EARLY_STOP_ADAPTIVE, stop_width=1, result_width=1),
+    dict(queue_size=96, predicate_bias=1, early_stop_mode=A.EARLY_STOP_ADAPTIVE, pending_base_stop=1,
+         full_label_check=1, alpha=0.3),
+]
+
+
+@pytest.mark.parametrize("wl", ["cfg1", "cfg2"])
+@pytest.mark.parametrize("vi", range(len(BEAM_VARIANTS)))
+def test_beam_search_pq_bitexact(L, wl, vi):
+    w, idx, plan = cfg1_small() if wl == "cfg1" else cfg2_small()
+    params = dict(BEAM_VARIANTS[vi], scorer=A.SCORER_PQ)
+    lut = O.pq_build_lut(w.queries.astype(np.float32), idx.pq_centroids, idx.pq_codes.shape[1])
+    want = O.beam_search(idx.graph(), idx.attrs(), idx.codes(), {"pq_lut": lut}, plan.graph_routes, threads=8,
+                         **params)
+    got = run_gpu_beam(L, idx.graph(), idx.attrs(), idx.codes(), {"pq_lut": dev(lut)}, plan.graph_routes, **params)
+    for name, g, o in zip(("ids", "dists", "steps", "counters"), got, want):
+        if name == "dists":
+            g, o = fbits(g), fbits(o)
+        assert np.array_equal(g, o), f"{name} differ in {np.count_nonzero(np.any(np.atleast_2d(g != o), axis=-1))} routes"
+
+
+@pytest.mark.parametrize("vi", [0, 1, 3])
+def test_beam_search_rabitq_bitexact(L, vi):
+    w, idx, plan, rq, anchors, qr = rabitq_artifacts()
+    dprep, hprep = _rq_prepared(L, qr, anchors)
+    params = dict(BEAM_VARIANTS[vi], scorer=A.SCORER_RABITQ, lut_in_shared=0)
+    want = O.beam_search(idx.graph(), idx.attrs(), rq, hprep, plan.graph_routes, threads=8, **params)
+    got = run_gpu_beam(L, idx.graph(), idx.attrs(), rq, dprep, plan.graph_routes, **params)
+    for name, g, o in zip(("ids", "dists", "steps", "counters"), got, want):
+        if name == "dists":
+            g, o = fbits(g), fbits(o)
+        assert np.array_equal(g, o), name
+
+
+def test_beam_search_edge_cases(L):
+    """Seed-only graphs (all neighbours padding), a seed whose neighbours are
+    all visited, and a zero-route batch."""
+    w, idx, plan = cfg1_small()
+    g = idx.graph()
+    adj = g["adjacency"].copy()
+    adj[: adj.shape[0] // 2] = A.U32MAX
+    g = dict(g, adjacency=adj)
+    lut = O.pq_build_lut(w.queries, idx.pq_centroids, idx.pq_codes.shape[1])
+    params = dict(queue_size=32, predicate_bias=1)
+    want = O.beam_search(g, idx.attrs(), idx.codes(), {"pq_lut": lut}, plan.graph_routes, **params)
+    got = run_gpu_beam(L, g, idx.attrs(), idx.codes(), {"pq_lut": dev(lut)}, plan.graph_routes, **params)
+    assert np.array_equal(got[0], want[0]) and np.array_equal(got[2], want[2])
+    empty = {k: v[:0] if k not in ("qlabel_indptr", "pred_offsets") else v[:1] for k, v in plan.graph_routes.items()}
+    gs, at, cs = A.fill_graph(dev_dict(idx.graph())), A.fill_attrs(dev_dict(idx.attrs())), A.fill_codes(dev_dict(idx.codes()))
+    rs = A.fill_routes(dev_dict({k: v if v.size else np.zeros(1, v.dtype) for k, v in empty.items()}))
+    rs.n_routes = 0
+    ps = A.fill_prepared({"pq_lut": dev(lut)})
+    sp = A.fill_params(**params)
+    buf = torch.empty(16, dtype=torch.int32, device="cuda")
+    out = A.SearchOut(ids=A.ptr(buf), dists=A.ptr(buf))
+    assert L.gofann_beam_search(C.byref(gs), C.byref(at), C.byref(cs), C.byref(ps), C.byref(rs), C.byref(sp),
+                                C.byref(out), A.ptr(buf), 64, stream()) == 0
+
+
+# ----------------------------------------------------------- postings
+def run_gpu_posting(L, codes, prep, attrs, routes, scorer, pids, begin, count, k):
+    dc, da, dr = dev_dict(codes), dev_dict(attrs), dev_dict(routes)
+    cs, pp, at, rs = A.fill_codes(dc), A.fill_prepared(prep), A.fill_attrs(da), A.fill_routes(dr)
+    n = rs.n_routes
+    ids = torch.empty((n, k), dtype=torch.int32, device="cuda")
+    d = torch.empty((n, k), dtype=torch.float32, device="cuda")
+    A.check(L.gofann_posting_scan(C.byref(cs), C.byref(pp), C.byref(at), C.byref(rs), scorer, A.ptr(dev(pids)),
+                                  A.ptr(dev(begin)), A.ptr(dev(count)), k, 1, A.ptr(ids), A.ptr(d), stream()), "posting")
+    torch.cuda.synchronize()
+    return host(ids, np.uint32), d.cpu().numpy()
+
+
+@pytest.mark.parametrize("k", [1, 10, 100, 400])
+def test_posting_scan_pq_bitexact(L, k):
+    from gofann.planner import concat_routes, subset_routes
+    w, idx, plan = cfg2_small()
+    lut = O.pq_build_lut(w.queries.astype(np.float32), idx.pq_centroids, idx.pq_codes.shape[1])
+    # the planner's low-frequency routes, plus scans of the three largest
+    # postings (several sort rounds) and one empty posting
+    big = np.argsort(idx.posting_count)[-3:]
+    extra = subset_routes(plan.graph_routes, np.arange(4))
+    routes = concat_routes(plan.posting_routes, extra)
+    begin = np.concatenate([plan.posting_begin, idx.posting_begin[big], [0]]).astype(np.uint64)
+    count = np.concatenate([plan.posting_count, idx.posting_count[big], [0]]).astype(np.uint32)
+    want = O.posting_scan(idx.codes(), {"pq_lut": lut}, idx.attrs(), routes, A.SCORER_PQ, idx.posting_ids, begin,
+                          count, k)
+    got = run_gpu_posting(L, idx.codes(), {"pq_lut": dev(lut)}, idx.attrs(), routes, A.SCORER_PQ, idx.posting_ids,
+                          begin, count, k)
+    assert np.array_equal(got[0], want[0])
+    assert np.array_equal(fbits(got[1]), fbits(want[1]))
+
+
+def test_posting_scan_rabitq_bitexact(L):
+    w, idx, plan, rq, anchors, qr = rabitq_artifacts()
+    dprep, hprep = _rq_prepared(L, qr, anchors)
+    routes = plan.graph_routes  # scan each graph route's label posting
+    lab = routes["primary_label"]
+    begin, count = idx.posting_begin[lab], idx.posting_count[lab]
+    want = O.posting_scan(rq, hprep, idx.attrs(), routes, A.SCORER_RABITQ, idx.posting_ids, begin, count, 100)
+    got = run_gpu_posting(L, rq, dprep, idx.attrs(), routes, A.SCORER_RABITQ,
+                          idx.posting_ids, begin, count, 100)
+    assert np.array_equal(got[0], want[0])
+    assert np.array_equal(fbits(got[1]), fbits(want[1]))
+
+
+# --------------------------------------------------------------- rerank
+def _ties_equivalent(gi, gd, wi, wd, rtol):
+    """Ids equal, or differing only inside a run of distances equal within rtol."""
+    if np.array_equal(gi, wi):
+        return True
+    for r in range(gi.shape[0]):
+        if np.array_equal(gi[r], wi[r]):
+            continue
+        if not np.allclose(gd[r], wd[r], rtol=rtol, atol=0):
+            return False
+        for j in np.nonzero(gi[r] != wi[r])[0]:
+            near = np.abs(wd[r] - gd[r, j]) <= rtol * np.abs(gd[r, j])
+            if gi[r, j] not in wi[r][near] and gi[r, j] != A.U32MAX:
+                return False
+    return True
+
+
+@pytest.mark.parametrize("dtype", ["u8", "f32", "f16"])
+def test_rerank(L, dtype):
+    if dtype == "u8":
+        w, idx, plan = cfg2_small()
+        base, queries = w.base, w.queries
+    else:
+        w, idx, plan = cfg1_small()
+        base = w.base if dtype == "f32" else w.base.astype(np.float16)
+        queries = w.queries
+    dt = {"u8": A.DTYPE_U8, "f32": A.DTYPE_F32, "f16": A.DTYPE_F16}[dtype]
+    rng = np.random.default_rng(3)
+    routes = plan.graph_routes
+    n = routes["query_row"].shape[0]
+    width = 100
+    cand = rng.integers(0, w.n, size=(n, width)).astype(np.uint32)
+    cand[:, 5] = cand[:, 3]  # duplicates
+    cand[rng.random(cand.shape) < 0.05] = A.U32MAX
+    cand[0, :] = A.U32MAX    # empty shortlist
+    cand[1, 7] = w.n + 5     # out of range id
+    want_i, want_d = O.rerank(base, dt, queries, idx.attrs(), routes, cand, 10)
+    bt = dev(base.view(np.uint16) if dtype == "f16" else base)
+    ids = torch.empty((n, 10), dtype=torch.int32, device="cuda")
+    d = torch.empty((n, 10), dtype=torch.float32, device="cuda")
+    at, rs = A.fill_attrs(dev_dict(idx.attrs())), A.fill_routes(dev_dict(routes))
+    A.check(L.gofann_rerank(A.ptr(bt), dt, w.n, w.dim, A.ptr(dev(queries)), C.byref(at), C.byref(rs),
+                            A.ptr(dev(cand)), width, 10, A.ptr(ids), A.ptr(d), stream()), "rerank")
+    gi, gd = host(ids, np.uint32), d.cpu().numpy()
+    if dtype == "u8":
+        assert np.array_equal(gi, want_i) and np.array_equal(fbits(gd), fbits(want_d))
+    else:
+        rtol = 1e-5 if dtype == "f32" else 1e-3
+        valid = want_i != A.U32MAX
+        assert np.array_equal(gi == A.U32MAX, ~valid)
+        assert np.all(np.abs(gd[valid] - want_d[valid]) <= rtol * np.abs(want_d[valid]))
+        assert _ties_equivalent(gi, gd, want_i, want_d, rtol)
+
+
+# --------------------------------------------------------------- merges
+def test_route_merge_bitexact(L):
+    rng = np.random.default_rng(9)
+    n_routes, n_q, width = 700, 300, 10
+    r2q = rng.integers(0, n_q, size=n_routes)
+    ids = rng.integers(0, 500, size=(n_routes, width)).astype(np.uint32)
+    ids[rng.random(ids.shape) < 0.1] = A.U32MAX
+    d = rng.integers(0, 50, size=(n_routes, width)).astype(np.float32)
+    order = np.argsort(r2q, kind="stable").astype(np.uint32)
+    qoff = np.zeros(n_q + 1, np.uint32)
+    qoff[1:] = np.cumsum(np.bincount(r2q, minlength=n_q))
+    wi, wd = O.route_merge(ids, d, qoff, order, 10)
+    oi = torch.empty((n_q, 10), dtype=torch.int32, device="cuda")
+    od = torch.empty((n_q, 10), dtype=torch.float32, device="cuda")
+    A.check(L.gofann_route_merge(A.ptr(dev(ids)), A.ptr(dev(d)), width, A.ptr(dev(qoff)), A.ptr(dev(order)), n_q, 10,
+                                 A.ptr(oi), A.ptr(od), stream()), "route merge")
+    assert np.array_equal(host(oi, np.uint32), wi) and np.array_equal(fbits(od.cpu().numpy()), fbits(wd))
+
+
+@pytest.mark.parametrize("shards", [1, 2, 8])
+def test_shard_merge_bitexact(L, shards):
+    rng = np.random.default_rng(shards)
+    nq, k = 257, 10
+    ids = np.empty((shards, nq, k), np.uint32)
+    d = np.empty((shards, nq, k), np.float32)
+    for s in range(shards):
+        dd = np.sort(rng.integers(0, 30, size=(nq, k)).astype(np.float32), axis=1)
+        ids[s] = s * 1000 + rng.integers(0, 1000, size=(nq, k))
+        d[s] = dd
+    ids[0, 0, 5:] = A.U32MAX
+    d[0, 0, 5:] = A.FLT_MAX
+    wi, wd = O.shard_merge(ids, d, k)
+    oi = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+    od = torch.empty((nq, k), dtype=torch.float32, device="cuda")
+    A.check(L.gofann_shard_merge(A.ptr(dev(ids)), A.ptr(dev(d)), shards, nq, k, A.ptr(oi), A.ptr(od), stream()), "shard")
+    assert np.array_equal(host(oi, np.uint32), wi) and np.array_equal(fbits(od.cpu().numpy()), fbits(wd))
+
+
+def test_offset_ids(L):
+    x = np.array([0, 5, A.U32MAX, 7], np.uint32)
+    t = dev(x)
+    A.check(L.gofann_offset_ids(A.ptr(t), 4, 100, stream()), "offset")
+    assert np.array_equal(host(t, np.uint32), np.array([100, 105, A.U32MAX, 107], np.uint32))
+
+
+# ------------------------------------------------------------ end to end
+@pytest.mark.parametrize("wl", ["cfg1", "cfg2"])
+def test_pipeline_matches_oracle_and_recall(L, wl):
+    from gofann.engine import DeviceIndex, DevicePlan, Pipeline, SearchConfig
+    w, idx, plan = cfg1_small() if wl == "cfg1" else cfg2_small()
+    cfg = SearchConfig(queue_size=64, result_width=100)
+    pipe = Pipeline(DeviceIndex(idx), DevicePlan(plan, "cuda"), cfg)
+    q = dev(w.queries)
+    gi, gd = pipe.run(q)
+    torch.cuda.synchronize()
+    gi = host(gi, np.uint32)
+    # oracle pipeline on the same inputs
+    dt = A.DTYPE_U8 if w.dtype == "u8" else A.DTYPE_F32
+    lut = O.pq_build_lut(w.queries.astype(np.float32), idx.pq_centroids, idx.pq_codes.shape[1])
+    bi, _, _, _ = O.beam_search(idx.graph(), idx.attrs(), idx.codes(), {"pq_lut": lut}, plan.graph_routes, threads=8,
+                                **{k: getattr(cfg, k) for k in ("queue_size", "stop_width", "result_width",
+                                                                "finish_limit", "early_stop_mode", "predicate_bias",
+                                                                "alpha")})
+    ri, rd = O.rerank(w.base, dt, w.queries, idx.attrs(), plan.graph_routes, bi, 10)
+    pi, _ = O.posting_scan(idx.codes(), {"pq_lut": lut}, idx.attrs(), plan.posting_routes, A.SCORER_PQ,
+                           idx.posting_ids, plan.posting_begin, plan.posting_count, cfg.lowfreq_shortlist)
+    rpi, rpd = O.rerank(w.base, dt, w.queries, idx.attrs(), plan.posting_routes, pi, 10)
+    qoff, order = plan.merge_tables()
+    wi, wd = O.route_merge(np.concatenate([ri, rpi]), np.concatenate([rd, rpd]), qoff, order, 10)
+    if w.dtype == "u8":
+        assert np.array_equal(gi, wi)
+    else:
+        assert _ties_equivalent(gi, gd.cpu().numpy(), wi, wd, 1e-5)
+    # recall against exhaustive filtered top-k (FP64)
+    from gofann.planner import _route_tables
+    labs = [np.asarray(x, np.uint32) for x in w.query_labels]
+    gt_routes = _route_tables(list(range(len(labs))), labs, [x[0] for x in labs], [0] * len(labs), [0] * len(labs))
+    gt_routes["pred_enabled"][:] = 1
+    ti, _ = O.filtered_topk(w.base, dt, w.queries, idx.attrs(), gt_routes, 10)
+    rec = np.mean([len((set(gi[i].tolist()) & set(ti[i].tolist())) - {A.U32MAX}) /
+                   max(1, len(set(ti[i].tolist()) - {A.U32MAX})) for i in range(gi.shape[0])])
+    assert rec >= 0.95, rec
