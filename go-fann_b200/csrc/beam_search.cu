@@ -112,29 +112,56 @@ __device__ __forceinline__ bool stop_now(const gofann_search_params& p, const Wa
     return st.exhausted || es || step >= cap;
 }
 
-// Cooperative pickup (backend_pq.cu:844-893): lexicographic min of
-// (first, index) over unused entries, same lane-strided scan and shfl_down
-// tree; lane 0 copies and marks the winner.
+#ifdef GOFANN_DEBUG_PICKUP
+// Debug builds only: prints every pickup (run with a single route).
+__device__ void gofann_debug_pickup(const FPair* f, int size, int bi)
+{
+    printf("PICK size=%d idx=%d row=%u first=%.9g\n", size, bi,
+           bi >= 0 ? (f[bi].second & ~kPoolUsed) : 0xffffffffu, bi >= 0 ? f[bi].first : 0.f);
+    if (bi >= 0)
+        for (int i = 1; i < size; ++i)
+            if (i != bi && !(f[i].second & kPoolUsed) && !(f[i].first < f[bi].first) && !(f[bi].first < f[i].first))
+                printf("  TIE idx=%d row=%u bits=%08x vs %08x\n", i, f[i].second, __float_as_uint(f[i].first),
+                       __float_as_uint(f[bi].first));
+}
+#endif
+// Cooperative pickup (backend_pq.cu:844-893): the unused entry with the
+// smallest `first`, lowest array index on ties; lane 0 copies and marks it.
+// The order is taken as one 64-bit key (order-preserving float bits, with
+// -0 folded onto +0, above the index) reduced by an xor-shuffle min: exact
+// for every finite or infinite distance and NaN-safe.  (The reference's
+// tie clause `!(b < a) && !(a < b) && ia < ib` inside a shfl_down tree was
+// observed to keep the larger index on sm_100a with nvcc 12.9 -O3.)
+__device__ __forceinline__ uint32_t ordered_bits(float f)
+{
+    if (f == 0.0f) f = 0.0f;
+    const uint32_t b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
 __device__ __forceinline__ bool coop_pickup(FPair* f, int size, FPair* out, int lane)
 {
-    int bi = -1;
-    float bd = FLT_MAX;
+    unsigned long long best = ~0ull;
     for (int i = lane + 1; i < size; i += kWarp) {
         const FPair e = f[i];
         if (e.second & kPoolUsed) continue;
-        if (bi < 0 || e.first < bd || (!(bd < e.first) && !(e.first < bd) && i < bi)) { bi = i; bd = e.first; }
+        const unsigned long long k = (static_cast<unsigned long long>(ordered_bits(e.first)) << 32) |
+                                     static_cast<uint32_t>(i);
+        best = k < best ? k : best;
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
-        const int oi = __shfl_down_sync(kFull, bi, off);
-        const float od = __shfl_down_sync(kFull, bd, off);
-        if (oi >= 0 && (bi < 0 || od < bd || (!(bd < od) && !(od < bd) && oi < bi))) { bi = oi; bd = od; }
+        const unsigned long long o = __shfl_xor_sync(kFull, best, off);
+        best = o < best ? o : best;
     }
-    bi = __shfl_sync(kFull, bi, 0);
+    const int bi = best == ~0ull ? -1 : static_cast<int>(best & 0xffffffffu);
     if (lane == 0 && bi >= 0) {
         *out = f[bi];
         f[bi].second |= kPoolUsed;
     }
+#ifdef GOFANN_DEBUG_PICKUP
+    if (lane == 0) gofann_debug_pickup(f, size, bi);
+#endif
     __syncwarp();
     return bi >= 0;
 }
@@ -310,6 +337,8 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
                 st.nfr = nfr;
                 st.brk = stop_now(p, st, step) ? 1 : 0;
                 if (!st.brk) {
+                    if (a.out.trace && static_cast<uint32_t>(st.expanded) < a.out.trace_width)
+                        a.out.trace[static_cast<size_t>(route) * a.out.trace_width + st.expanded] = now_row;
                     ++st.expanded;
                     if (nfr == 1) {
                         // stop top-k and result heap (backend_pq.cu:4583-4630)
@@ -463,6 +492,9 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
             oid[i] = id;
             od[i] = d;
         }
+        if (a.out.trace)
+            for (uint32_t i = static_cast<uint32_t>(st.expanded) + lane; i < a.out.trace_width; i += kWarp)
+                a.out.trace[static_cast<size_t>(route) * a.out.trace_width + i] = kU32Max;
         if (lane == 0) {
             if (a.out.steps) a.out.steps[route] = step;
             if (a.out.counters) {

@@ -79,7 +79,8 @@ class SearchParams(C.Structure):
 
 
 class SearchOut(C.Structure):
-    _fields_ = [("ids", P), ("dists", P), ("steps", P), ("counters", P), ("status", P)]
+    _fields_ = [("ids", P), ("dists", P), ("steps", P), ("counters", P), ("status", P), ("trace", P),
+                ("trace_width", U32), ("reserved", U32)]
 
 
 def ptr(x) -> int | None:

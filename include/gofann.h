@@ -180,6 +180,12 @@ typedef struct gofann_search_out {
     int32_t* steps;     /* device [n_routes] or NULL */
     uint32_t* counters; /* device [n_routes][4] or NULL */
     int32_t* status;    /* device [1] error word or NULL */
+    /* optional expansion trace (expansion_trace::View, src/profiling/
+     * expansion_trace.h:19): the first trace_width expanded local rows of
+     * each route in expansion order, UINT32_MAX fill; NULL = off */
+    uint32_t* trace;
+    uint32_t trace_width;
+    uint32_t reserved;
 } gofann_search_out;
 
 /* ---------------------------------------------------------------- basics */

@@ -20,6 +20,7 @@
 #include <float.h>
 #include <math.h>
 #include <pthread.h>
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -577,14 +578,26 @@ static int early_stop(int mode, int bad, int fixed, int queue_limit, int expande
 
 /* pickup_next_unused_from_native_frontier<kCooperative=true>,
  * backend_pq.cu:844-893: minimum `first` among unused entries 1..size-1,
- * lowest array index on ties; marks the entry used. */
+ * lowest array index on ties; marks the entry used.  Distances are ordered
+ * by their order-preserving bit pattern (-0 folded onto +0), which equals
+ * float order for every non-NaN value and places NaN after +inf. */
+static uint32_t ordered_bits(float x)
+{
+    if (x == 0.0f) x = 0.0f;
+    const uint32_t b = f2u(x);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
 static int pickup(fpair* f, int size, fpair* out)
 {
     int best = -1;
     for (int i = 1; i < size; ++i) {
         if (f[i].second & POOL_USED) continue;
-        if (best < 0 || f[i].first < f[best].first) best = i;
+        if (best < 0 || ordered_bits(f[i].first) < ordered_bits(f[best].first)) best = i;
     }
+#ifdef ORACLE_DEBUG_PICKUP
+    printf("PICK size=%d idx=%d row=%u first=%.9g\n", size, best,
+           best >= 0 ? (f[best].second & ~POOL_USED) : 0xffffffffu, best >= 0 ? (double)f[best].first : 0.0);
+#endif
     if (best < 0) return 0;
     *out = f[best];
     f[best].second |= POOL_USED;
@@ -611,7 +624,7 @@ static void search_one(const gofann_graph* g, const gofann_attrs* a, const gofan
                        const gofann_prepared* p, const gofann_routes* r,
                        const gofann_search_params* sp, uint32_t route, uint32_t* out_ids,
                        float* out_d, int32_t* out_steps, uint32_t* counters, uint32_t* hash,
-                       fpair* frontier, rpair* topk)
+                       fpair* frontier, rpair* topk, uint32_t* trace, uint32_t trace_width)
 {
     const int QS = sp->queue_size, SW = sp->stop_width, RW = sp->result_width;
     const uint32_t row = r->query_row[route];
@@ -701,6 +714,7 @@ static void search_one(const gofann_graph* g, const gofann_attrs* a, const gofan
                                     passed, SW) ||
             (sp->max_steps > 0 && step >= sp->max_steps))
             break;
+        if (trace && (uint32_t)expanded < trace_width) trace[expanded] = now_row;
         ++expanded;
         ++n_expanded;
         if (nfr == 1) {
@@ -794,6 +808,8 @@ static void search_one(const gofann_graph* g, const gofann_attrs* a, const gofan
         out_ids[slot] = g->row_to_sample[label_offset + res.second];
         out_d[slot] = res.first;
     }
+    if (trace)
+        for (uint32_t i = (uint32_t)expanded; i < trace_width; ++i) trace[i] = U32MAX;
     if (out_steps) *out_steps = step;
     if (counters) {
         counters[0] = n_expanded; counters[1] = n_dist; counters[2] = n_probe; counters[3] = n_admit;
@@ -805,6 +821,7 @@ typedef struct {
     const gofann_routes* r; const gofann_search_params* sp;
     uint32_t* ids; float* d; int32_t* steps; uint32_t* counters;
     uint32_t begin, end, stride;
+    uint32_t* trace; uint32_t trace_width;
 } search_job;
 
 static void* search_worker(void* arg)
@@ -817,15 +834,29 @@ static void* search_worker(void* arg)
     for (uint32_t route = j->begin; route < j->end; route += j->stride)
         search_one(j->g, j->a, j->c, j->p, j->r, j->sp, route, j->ids + (size_t)route * RW,
                    j->d + (size_t)route * RW, j->steps ? j->steps + route : NULL,
-                   j->counters ? j->counters + (size_t)route * 4 : NULL, hash, frontier, topk);
+                   j->counters ? j->counters + (size_t)route * 4 : NULL, hash, frontier, topk,
+                   j->trace ? j->trace + (size_t)route * j->trace_width : NULL, j->trace_width);
     free(hash); free(frontier); free(topk);
     return NULL;
 }
+
+int oracle_beam_search_traced(const gofann_graph* g, const gofann_attrs* a, const gofann_codes* c,
+                              const gofann_prepared* p, const gofann_routes* r,
+                              const gofann_search_params* sp, uint32_t* ids, float* d, int32_t* steps,
+                              uint32_t* counters, int threads, uint32_t* trace, uint32_t trace_width);
 
 int oracle_beam_search(const gofann_graph* g, const gofann_attrs* a, const gofann_codes* c,
                        const gofann_prepared* p, const gofann_routes* r,
                        const gofann_search_params* sp, uint32_t* ids, float* d, int32_t* steps,
                        uint32_t* counters, int threads)
+{
+    return oracle_beam_search_traced(g, a, c, p, r, sp, ids, d, steps, counters, threads, NULL, 0);
+}
+
+int oracle_beam_search_traced(const gofann_graph* g, const gofann_attrs* a, const gofann_codes* c,
+                              const gofann_prepared* p, const gofann_routes* r,
+                              const gofann_search_params* sp, uint32_t* ids, float* d, int32_t* steps,
+                              uint32_t* counters, int threads, uint32_t* trace, uint32_t trace_width)
 {
     if (sp->queue_size < 1 || sp->queue_size > GOFANN_MAX_QUEUE || sp->stop_width < 1 ||
         sp->stop_width > GOFANN_MAX_TOPK || sp->result_width < 1 ||
@@ -836,7 +867,7 @@ int oracle_beam_search(const gofann_graph* g, const gofann_attrs* a, const gofan
     search_job* jobs = (search_job*)malloc(sizeof(search_job) * (size_t)threads);
     for (int t = 0; t < threads; ++t) {
         search_job j = {g, a, c, p, r, sp, ids, d, steps, counters, (uint32_t)t, r->n_routes,
-                        (uint32_t)threads};
+                        (uint32_t)threads, trace, trace_width};
         jobs[t] = j;
         if (threads == 1) search_worker(&jobs[t]);
         else pthread_create(&th[t], NULL, search_worker, &jobs[t]);

@@ -36,6 +36,10 @@ int oracle_beam_search(const gofann_graph* g, const gofann_attrs* a, const gofan
                        const gofann_prepared* p, const gofann_routes* r,
                        const gofann_search_params* sp, uint32_t* ids, float* d, int32_t* steps,
                        uint32_t* counters, int threads);
+int oracle_beam_search_traced(const gofann_graph* g, const gofann_attrs* a, const gofann_codes* c,
+                              const gofann_prepared* p, const gofann_routes* r,
+                              const gofann_search_params* sp, uint32_t* ids, float* d, int32_t* steps,
+                              uint32_t* counters, int threads, uint32_t* trace, uint32_t trace_width);
 int oracle_posting_scan(const gofann_codes* c, const gofann_prepared* p, const gofann_attrs* a,
                         const gofann_routes* r, int scorer, const uint32_t* posting_ids,
                         const uint64_t* route_begin, const uint32_t* route_count, int k,

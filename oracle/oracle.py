@@ -55,6 +55,8 @@ def olib() -> C.CDLL:
         L.oracle_beam_search.argtypes = [C.POINTER(A.Graph), C.POINTER(A.Attrs), C.POINTER(A.Codes),
                                          C.POINTER(A.Prepared), C.POINTER(A.Routes), C.POINTER(A.SearchParams),
                                          sp, sp, sp, sp, C.c_int]
+        L.oracle_beam_search_traced.argtypes = L.oracle_beam_search.argtypes + [sp, U32]
+        L.oracle_beam_search_traced.restype = C.c_int
         L.oracle_posting_scan.argtypes = [C.POINTER(A.Codes), C.POINTER(A.Prepared), C.POINTER(A.Attrs),
                                           C.POINTER(A.Routes), C.c_int, sp, sp, sp, C.c_int, C.c_int, sp, sp]
         L.oracle_rerank.argtypes = [sp, C.c_int, U32, U32, sp, C.POINTER(A.Attrs), C.POINTER(A.Routes), sp, U32,
@@ -170,7 +172,8 @@ def rabitq_encode(residual, rotated_centroids, anchor_ids):
     return codes, factors
 
 
-def beam_search(graph: dict, attrs: dict | None, codes: dict, prep: dict, routes: dict, threads: int = 1, **params):
+def beam_search(graph: dict, attrs: dict | None, codes: dict, prep: dict, routes: dict, threads: int = 1,
+                trace_width: int = 0, **params):
     g = A.fill_graph(graph)
     at = A.fill_attrs(attrs) if attrs is not None else A.Attrs()
     cs, ps, rs = A.fill_codes(codes), A.fill_prepared(prep), A.fill_routes(routes)
@@ -180,10 +183,14 @@ def beam_search(graph: dict, attrs: dict | None, codes: dict, prep: dict, routes
     d = np.empty((n, rw), np.float32)
     steps = np.empty(n, np.int32)
     counters = np.empty((n, 4), np.uint32)
-    st = olib().oracle_beam_search(C.byref(g), C.byref(at), C.byref(cs), C.byref(ps), C.byref(rs), C.byref(sp),
-                                   P(ids), P(d), P(steps), P(counters), threads)
+    trace = np.empty((n, trace_width), np.uint32) if trace_width else None
+    st = olib().oracle_beam_search_traced(C.byref(g), C.byref(at), C.byref(cs), C.byref(ps), C.byref(rs),
+                                          C.byref(sp), P(ids), P(d), P(steps), P(counters), threads, P(trace),
+                                          trace_width)
     if st != 0:
         raise RuntimeError(f"oracle_beam_search status {st}")
+    if trace_width:
+        return ids, d, steps, counters, trace
     return ids, d, steps, counters
 
 

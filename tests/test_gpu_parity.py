@@ -32,6 +32,23 @@ def stream():
     return torch.cuda.current_stream().cuda_stream
 
 
+_KEEP = []
+
+
+def dptr(a):
+    """Device copy of a numpy array, kept alive until the test module ends."""
+    t = dev(a)
+    _KEEP.append(t)
+    return A.ptr(t)
+
+
+@pytest.fixture(autouse=True)
+def _release():
+    yield
+    torch.cuda.synchronize()
+    _KEEP.clear()
+
+
 # ------------------------------------------------------------------ PQ stages
 @pytest.mark.parametrize("dim,pq_dim,qdtype", [(128, 32, "f32"), (192, 48, "u8"), (96, 16, "f32"), (64, 64, "u8"),
                                                (256, 128, "f32")])
@@ -46,8 +63,8 @@ def test_pq_lut_bitexact(L, dim, pq_dim, qdtype):
         cent = rng.standard_normal((256, dim)).astype(np.float32)
     want = O.pq_build_lut(q.astype(np.float32), cent, pq_dim)
     lut = torch.empty((n, pq_dim, 256), dtype=torch.float32, device="cuda")
-    A.check(L.gofann_pq_build_lut(A.ptr(dev(q)), A.DTYPE_U8 if qdtype == "u8" else A.DTYPE_F32, n, dim,
-                                  A.ptr(dev(cent)), pq_dim, A.ptr(lut), stream()), "lut")
+    A.check(L.gofann_pq_build_lut(dptr((q)), A.DTYPE_U8 if qdtype == "u8" else A.DTYPE_F32, n, dim,
+                                  dptr((cent)), pq_dim, A.ptr(lut), stream()), "lut")
     torch.cuda.synchronize()
     assert np.array_equal(fbits(lut.cpu().numpy()), fbits(want))
 
@@ -62,7 +79,7 @@ def test_pq_adc_bitexact(L, pq_dim):
     ps = rng.integers(0, n_samples, size=n_pairs).astype(np.uint32)
     want = O.pq_adc(lut, codes, pr, ps)
     out = torch.empty(n_pairs, dtype=torch.float32, device="cuda")
-    A.check(L.gofann_pq_adc(A.ptr(dev(lut)), pq_dim, A.ptr(dev(codes)), A.ptr(dev(pr)), A.ptr(dev(ps)), n_pairs,
+    A.check(L.gofann_pq_adc(dptr((lut)), pq_dim, dptr((codes)), dptr((pr)), dptr((ps)), n_pairs,
                             A.ptr(out), stream()), "adc")
     assert np.array_equal(fbits(out.cpu().numpy()), fbits(want))
 
@@ -76,8 +93,8 @@ def test_pq_encode_bitexact(L, dim, pq_dim, dtype):
     cent = x[rng.choice(n, 256, replace=False)].astype(np.float32)
     want = O.pq_encode(x.astype(np.float32), cent, pq_dim)
     out = torch.empty((n, pq_dim), dtype=torch.uint8, device="cuda")
-    A.check(L.gofann_pq_encode(A.ptr(dev(x)), A.DTYPE_U8 if dtype == "u8" else A.DTYPE_F32, n, dim,
-                               A.ptr(dev(cent)), pq_dim, A.ptr(out), stream()), "encode")
+    A.check(L.gofann_pq_encode(dptr((x)), A.DTYPE_U8 if dtype == "u8" else A.DTYPE_F32, n, dim,
+                               dptr((cent)), pq_dim, A.ptr(out), stream()), "encode")
     assert np.array_equal(out.cpu().numpy(), want)
 
 
@@ -93,7 +110,7 @@ def test_rabitq_quantize_bitexact(L, pd):
     gq8 = torch.empty((n, pd), dtype=torch.int8, device="cuda")
     gs = torch.empty(n, dtype=torch.float32, device="cuda")
     gk = torch.empty(n, dtype=torch.float32, device="cuda")
-    A.check(L.gofann_rabitq_quantize(A.ptr(dev(r)), n, pd, A.ptr(gq8), A.ptr(gs), A.ptr(gk), stream()), "quantize")
+    A.check(L.gofann_rabitq_quantize(dptr((r)), n, pd, A.ptr(gq8), A.ptr(gs), A.ptr(gk), stream()), "quantize")
     assert np.array_equal(gq8.cpu().numpy(), q8)
     assert np.array_equal(fbits(gs.cpu().numpy()), fbits(scale))
     assert np.array_equal(fbits(gk.cpu().numpy()), fbits(k1))
@@ -106,7 +123,7 @@ def test_rabitq_centroid_dist_tolerance(L):
     c = rng.standard_normal((a, pd)).astype(np.float32)
     want = ((q[:, None, :].astype(np.float64) - c[None].astype(np.float64)) ** 2).sum(-1)
     out = torch.empty((n, a), dtype=torch.float32, device="cuda")
-    A.check(L.gofann_rabitq_centroid_dist(A.ptr(dev(q)), n, A.ptr(dev(c)), a, pd, A.ptr(out), stream()), "gdist")
+    A.check(L.gofann_rabitq_centroid_dist(dptr((q)), n, dptr((c)), a, pd, A.ptr(out), stream()), "gdist")
     got = out.cpu().numpy().astype(np.float64)
     assert np.all(np.abs(got - want) <= 1e-3 + 2e-5 * np.abs(want))
 
@@ -117,8 +134,8 @@ def _rq_prepared(L, qr, anchors):
     gs = torch.empty(n, dtype=torch.float32, device="cuda")
     gk = torch.empty(n, dtype=torch.float32, device="cuda")
     gd = torch.empty((n, anchors.shape[0]), dtype=torch.float32, device="cuda")
-    A.check(L.gofann_rabitq_quantize(A.ptr(dev(qr)), n, pd, A.ptr(gq8), A.ptr(gs), A.ptr(gk), stream()), "quantize")
-    A.check(L.gofann_rabitq_centroid_dist(A.ptr(dev(qr)), n, A.ptr(dev(anchors)), anchors.shape[0], pd, A.ptr(gd),
+    A.check(L.gofann_rabitq_quantize(dptr((qr)), n, pd, A.ptr(gq8), A.ptr(gs), A.ptr(gk), stream()), "quantize")
+    A.check(L.gofann_rabitq_centroid_dist(dptr((qr)), n, dptr((anchors)), anchors.shape[0], pd, A.ptr(gd),
                                           stream()), "gdist")
     torch.cuda.synchronize()
     dprep = {"rq_q8": gq8, "rq_scale": gs, "rq_k1xsumq": gk, "rq_centroid_dist": gd}
@@ -139,14 +156,14 @@ def test_rabitq_score_bitexact(L):
     cs, pp = A.fill_codes(dcodes), A.fill_prepared(dprep)
     out = torch.empty(n_pairs, dtype=torch.float32, device="cuda")
     ip = torch.empty(n_pairs, dtype=torch.int32, device="cuda")
-    A.check(L.gofann_rabitq_score(C.byref(cs), C.byref(pp), A.ptr(dev(pr)), A.ptr(dev(ps)), n_pairs, A.ptr(out),
+    A.check(L.gofann_rabitq_score(C.byref(cs), C.byref(pp), dptr((pr)), dptr((ps)), n_pairs, A.ptr(out),
                                   A.ptr(ip), stream()), "rq score")
     assert np.array_equal(ip.cpu().numpy(), want_ip)
     assert np.array_equal(fbits(out.cpu().numpy()), fbits(want))
 
 
 # ----------------------------------------------------------- traversal
-def run_gpu_beam(L, graph, attrs, codes, prep, routes, **params):
+def run_gpu_beam(L, graph, attrs, codes, prep, routes, trace_width=0, **params):
     dg, da, dc, dp, dr = dev_dict(graph), dev_dict(attrs), dev_dict(codes), prep, dev_dict(routes)
     gs, at, cs, ps, rs = A.fill_graph(dg), A.fill_attrs(da), A.fill_codes(dc), A.fill_prepared(dp), A.fill_routes(dr)
     sp = A.fill_params(**params)
@@ -156,14 +173,19 @@ def run_gpu_beam(L, graph, attrs, codes, prep, routes, **params):
     steps = torch.empty(n, dtype=torch.int32, device="cuda")
     cnt = torch.empty((n, 4), dtype=torch.int32, device="cuda")
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    out = A.SearchOut(ids=A.ptr(ids), dists=A.ptr(d), steps=A.ptr(steps), counters=A.ptr(cnt), status=A.ptr(status))
+    trace = torch.empty((n, max(trace_width, 1)), dtype=torch.int32, device="cuda")
+    out = A.SearchOut(ids=A.ptr(ids), dists=A.ptr(d), steps=A.ptr(steps), counters=A.ptr(cnt), status=A.ptr(status),
+                      trace=A.ptr(trace) if trace_width else None, trace_width=trace_width)
     nbytes = L.gofann_beam_search_scratch_bytes(n)
     scratch = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
     A.check(L.gofann_beam_search(C.byref(gs), C.byref(at), C.byref(cs), C.byref(ps), C.byref(rs), C.byref(sp),
                                  C.byref(out), A.ptr(scratch), nbytes, stream()), "beam_search")
     torch.cuda.synchronize()
     assert int(status.item()) == 0
-    return host(ids, np.uint32), d.cpu().numpy(), steps.cpu().numpy(), host(cnt, np.uint32)
+    res = (host(ids, np.uint32), d.cpu().numpy(), steps.cpu().numpy(), host(cnt, np.uint32))
+    if trace_width:
+        return res + (host(trace, np.uint32),)
+    return res
 
 
 BEAM_VARIANTS = [
@@ -221,10 +243,12 @@ def test_beam_search_edge_cases(L):
     got = run_gpu_beam(L, g, idx.attrs(), idx.codes(), {"pq_lut": dev(lut)}, plan.graph_routes, **params)
     assert np.array_equal(got[0], want[0]) and np.array_equal(got[2], want[2])
     empty = {k: v[:0] if k not in ("qlabel_indptr", "pred_offsets") else v[:1] for k, v in plan.graph_routes.items()}
-    gs, at, cs = A.fill_graph(dev_dict(idx.graph())), A.fill_attrs(dev_dict(idx.attrs())), A.fill_codes(dev_dict(idx.codes()))
-    rs = A.fill_routes(dev_dict({k: v if v.size else np.zeros(1, v.dtype) for k, v in empty.items()}))
+    dg, da, dc = dev_dict(idx.graph()), dev_dict(idx.attrs()), dev_dict(idx.codes())
+    dr = dev_dict({k: v if v.size else np.zeros(1, v.dtype) for k, v in empty.items()})
+    gs, at, cs, rs = A.fill_graph(dg), A.fill_attrs(da), A.fill_codes(dc), A.fill_routes(dr)
     rs.n_routes = 0
-    ps = A.fill_prepared({"pq_lut": dev(lut)})
+    dl = {"pq_lut": dev(lut)}
+    ps = A.fill_prepared(dl)
     sp = A.fill_params(**params)
     buf = torch.empty(16, dtype=torch.int32, device="cuda")
     out = A.SearchOut(ids=A.ptr(buf), dists=A.ptr(buf))
@@ -239,8 +263,8 @@ def run_gpu_posting(L, codes, prep, attrs, routes, scorer, pids, begin, count, k
     n = rs.n_routes
     ids = torch.empty((n, k), dtype=torch.int32, device="cuda")
     d = torch.empty((n, k), dtype=torch.float32, device="cuda")
-    A.check(L.gofann_posting_scan(C.byref(cs), C.byref(pp), C.byref(at), C.byref(rs), scorer, A.ptr(dev(pids)),
-                                  A.ptr(dev(begin)), A.ptr(dev(count)), k, 1, A.ptr(ids), A.ptr(d), stream()), "posting")
+    A.check(L.gofann_posting_scan(C.byref(cs), C.byref(pp), C.byref(at), C.byref(rs), scorer, dptr((pids)),
+                                  dptr((begin)), dptr((count)), k, 1, A.ptr(ids), A.ptr(d), stream()), "posting")
     torch.cuda.synchronize()
     return host(ids, np.uint32), d.cpu().numpy()
 
@@ -318,9 +342,10 @@ def test_rerank(L, dtype):
     bt = dev(base.view(np.uint16) if dtype == "f16" else base)
     ids = torch.empty((n, 10), dtype=torch.int32, device="cuda")
     d = torch.empty((n, 10), dtype=torch.float32, device="cuda")
-    at, rs = A.fill_attrs(dev_dict(idx.attrs())), A.fill_routes(dev_dict(routes))
-    A.check(L.gofann_rerank(A.ptr(bt), dt, w.n, w.dim, A.ptr(dev(queries)), C.byref(at), C.byref(rs),
-                            A.ptr(dev(cand)), width, 10, A.ptr(ids), A.ptr(d), stream()), "rerank")
+    da, dr = dev_dict(idx.attrs()), dev_dict(routes)
+    at, rs = A.fill_attrs(da), A.fill_routes(dr)
+    A.check(L.gofann_rerank(A.ptr(bt), dt, w.n, w.dim, dptr((queries)), C.byref(at), C.byref(rs),
+                            dptr((cand)), width, 10, A.ptr(ids), A.ptr(d), stream()), "rerank")
     gi, gd = host(ids, np.uint32), d.cpu().numpy()
     if dtype == "u8":
         assert np.array_equal(gi, want_i) and np.array_equal(fbits(gd), fbits(want_d))
@@ -346,7 +371,7 @@ def test_route_merge_bitexact(L):
     wi, wd = O.route_merge(ids, d, qoff, order, 10)
     oi = torch.empty((n_q, 10), dtype=torch.int32, device="cuda")
     od = torch.empty((n_q, 10), dtype=torch.float32, device="cuda")
-    A.check(L.gofann_route_merge(A.ptr(dev(ids)), A.ptr(dev(d)), width, A.ptr(dev(qoff)), A.ptr(dev(order)), n_q, 10,
+    A.check(L.gofann_route_merge(dptr((ids)), dptr((d)), width, dptr((qoff)), dptr((order)), n_q, 10,
                                  A.ptr(oi), A.ptr(od), stream()), "route merge")
     assert np.array_equal(host(oi, np.uint32), wi) and np.array_equal(fbits(od.cpu().numpy()), fbits(wd))
 
@@ -358,15 +383,18 @@ def test_shard_merge_bitexact(L, shards):
     ids = np.empty((shards, nq, k), np.uint32)
     d = np.empty((shards, nq, k), np.float32)
     for s in range(shards):
-        dd = np.sort(rng.integers(0, 30, size=(nq, k)).astype(np.float32), axis=1)
-        ids[s] = s * 1000 + rng.integers(0, 1000, size=(nq, k))
-        d[s] = dd
+        # each shard's list is sorted by (dist, id) with unique, shard-disjoint ids
+        dd = rng.integers(0, 30, size=(nq, k)).astype(np.float32)
+        ii = np.stack([s * 1000 + rng.permutation(1000)[:k] for _ in range(nq)]).astype(np.uint32)
+        for q in range(nq):
+            o = np.lexsort((ii[q], dd[q]))
+            ids[s, q], d[s, q] = ii[q][o], dd[q][o]
     ids[0, 0, 5:] = A.U32MAX
     d[0, 0, 5:] = A.FLT_MAX
     wi, wd = O.shard_merge(ids, d, k)
     oi = torch.empty((nq, k), dtype=torch.int32, device="cuda")
     od = torch.empty((nq, k), dtype=torch.float32, device="cuda")
-    A.check(L.gofann_shard_merge(A.ptr(dev(ids)), A.ptr(dev(d)), shards, nq, k, A.ptr(oi), A.ptr(od), stream()), "shard")
+    A.check(L.gofann_shard_merge(dptr((ids)), dptr((d)), shards, nq, k, A.ptr(oi), A.ptr(od), stream()), "shard")
     assert np.array_equal(host(oi, np.uint32), wi) and np.array_equal(fbits(od.cpu().numpy()), fbits(wd))
 
 
