@@ -1,0 +1,490 @@
+#!/usr/bin/env python
+"""Filtered-ANN benchmark: QPS at recall@10 >= 0.95 on BASELINE config 2.
+
+One step = one batch of 100k routed queries through the hot path on every
+rank: PQ LUT build -> filtered graph beam search -> low-frequency posting
+scans -> exact uint8 rerank -> route merge (-> NCCL all-gather of the
+per-shard top-10 and the shard merge when N > 1).  The queue size is the
+smallest of the reference's sweep (16..512) whose recall@10 on a 2,000-query
+exact-ground-truth sample reaches 0.95.
+
+Multi-GPU: the base set is sharded by contiguous id range, queries are
+replicated, each rank searches its shard and the per-shard top-10 lists are
+all-gathered and merged (total work fixed: "scaling": "strong").
+
+`--impl reference` times the reference's search restated on the CPU
+(oracle/, all host threads) on a bounded query sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for p in (str(ROOT), str(ROOT / "go-fann_b200")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import numpy as np  # noqa: E402
+
+QUEUE_SWEEP = [16, 32, 48, 64, 96, 128, 192, 256, 384, 512]  # configs/yfcc10m/categorical.json
+METRIC = "filtered QPS @ recall@10=0.95"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="gofann", choices=["gofann", "reference"])
+    ap.add_argument("--n", type=int, default=10_000_000, help="base vectors (config 2: 10M)")
+    ap.add_argument("--queries", type=int, default=100_000)
+    ap.add_argument("--eval", type=int, default=2000, help="queries with exact ground truth")
+    ap.add_argument("--queue-size", type=int, default=0, help="fixed queue size (0 = sweep)")
+    ap.add_argument("--recall", type=float, default=0.95)
+    ap.add_argument("--lut-shared", type=int, default=0)
+    ap.add_argument("--cpu-sample", type=int, default=0, help="queries in the CPU baseline sample (0 = auto)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seed", type=int, default=0)
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------ utilities
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except FileNotFoundError:
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()) | {"source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def profiled_traffic() -> dict | None:
+    p = ROOT / "profiles" / "beam_search_config2_traffic.json"
+    return json.loads(p.read_text()) if p.exists() else None
+
+
+# ------------------------------------------------------------ workload
+def build_workload(args, rank, world, device, t0):
+    import torch
+    from gofann import workload_gpu as W
+    data = W.generate(device=device, seed=args.seed, n=args.n, n_queries=args.queries, t0=t0)
+    n = args.n
+    lo, hi = rank * n // world, (rank + 1) * n // world
+    gt = None
+    eval_idx = np.arange(min(args.eval, args.queries))
+    if rank == 0:
+        gt = W.ground_truth(data, data["queries"], eval_idx)
+        W._log(f"ground truth for {len(eval_idx)} queries", t0)
+    shard = data
+    if world > 1:
+        shard = shard_data(data, lo, hi, device)
+    idx = W.build_index(shard, seed=args.seed, t0=t0)
+    return data, idx, gt, eval_idx, lo
+
+
+def shard_data(data, lo, hi, device):
+    """Rows [lo, hi) of the base set with their labels and postings (local ids)."""
+    import torch
+    ip = data["label_indptr"]
+    a, b = int(ip[lo]), int(ip[hi])
+    indptr = ip[lo:hi + 1] - a
+    indices = data["label_indices"][a:b]
+    base = data["base"][lo:hi]
+    vocab = data["vocab"]
+    rows = torch.repeat_interleave(torch.arange(hi - lo, device=device, dtype=torch.int64), indptr[1:] - indptr[:-1])
+    key = torch.sort((indices.to(torch.int64) << 24) | rows).values
+    pid = (key & ((1 << 24) - 1)).to(torch.int32)
+    card = torch.bincount(indices, minlength=vocab).cpu().numpy().astype(np.int64)
+    begin = np.zeros(vocab, np.int64)
+    begin[1:] = np.cumsum(card)[:-1]
+    return dict(base=base, label_indptr=indptr, label_indices=indices, posting_ids=pid, card=card, begin=begin,
+                queries=data["queries"], vocab=vocab, dim=data["dim"], n=hi - lo)
+
+
+def beam_bytes(counters: np.ndarray, n_routes: int, degree: int, pq_dim: int, avg_labels: float,
+               result_width: int) -> float:
+    """Algorithmic HBM bytes of one beam-search launch: per expansion the
+    adjacency row and its row->sample entry; per distance evaluation the
+    row->sample entry and the code row; per predicate probe the CSR offsets
+    and the sample's label row; per route its LUT row once and its shortlist
+    output.  Cache hits are not discounted, nothing is counted twice."""
+    e, v, p = counters[:, 0].sum(), counters[:, 1].sum(), counters[:, 2].sum()
+    return float(e * (degree * 4 + 4) + v * (4 + pq_dim) + p * (16 + 4 * avg_labels) +
+                 n_routes * (pq_dim * 256 * 4 + result_width * 8))
+
+
+# ------------------------------------------------------------ GPU arm
+def run_gofann(args):
+    import torch
+    import torch.distributed as dist
+    from gofann import _abi as A, planner, workload_gpu as W
+    from gofann.engine import DeviceIndex, DevicePlan, Pipeline, SearchConfig, stream_handle
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=600))
+    t0 = time.time()
+    data, idx, gt, eval_idx, shard_base = build_workload(args, rank, world, device, t0)
+    q = data["queries"]
+    plan = planner.plan_queries(idx, q.labels)
+    dplan = DevicePlan(plan, device)
+    dindex = DeviceIndex(idx, device)
+    L = A.lib()
+    nq = len(q.labels)
+    k = 10
+
+    def make_pipe(qs):
+        cfg = SearchConfig(queue_size=qs, result_width=100, lut_in_shared=args.lut_shared)
+        return Pipeline(dindex, dplan, cfg)
+
+    gath_ids = torch.empty((world, nq, k), dtype=torch.int32, device=device) if world > 1 else None
+    gath_d = torch.empty((world, nq, k), dtype=torch.float32, device=device) if world > 1 else None
+    fin_ids = torch.empty((nq, k), dtype=torch.int32, device=device)
+    fin_d = torch.empty((nq, k), dtype=torch.float32, device=device)
+
+    def step(pipe, queries):
+        ids, d = pipe.run(queries)
+        if world == 1:
+            return ids, d
+        s = stream_handle()
+        A.check(L.gofann_offset_ids(A.ptr(ids), ids.numel(), shard_base, s), "offset_ids")
+        dist.all_gather_into_tensor(gath_ids.view(-1), ids.reshape(-1))
+        dist.all_gather_into_tensor(gath_d.view(-1), d.reshape(-1))
+        A.check(L.gofann_shard_merge(A.ptr(gath_ids), A.ptr(gath_d), world, nq, k, A.ptr(fin_ids), A.ptr(fin_d), s),
+                "shard_merge")
+        return fin_ids, fin_d
+
+    # queue-size sweep on the eval sample (every rank runs the same steps)
+    sweep = [args.queue_size] if args.queue_size else QUEUE_SWEEP
+    chosen, recalls = None, {}
+    for qs in sweep:
+        pipe = make_pipe(qs)
+        ids, _ = step(pipe, q.vectors)
+        torch.cuda.synchronize()
+        r = None
+        if rank == 0:
+            pred = ids[torch.from_numpy(eval_idx).to(device)].cpu().numpy().view(np.uint32)
+            r = W.recall_at_k(pred, gt, k)
+        rr = torch.tensor([r if r is not None else 0.0], device=device)
+        if world > 1:
+            dist.broadcast(rr, 0)
+        recalls[qs] = round(float(rr.item()), 4)
+        W._log(f"queue {qs}: recall@10 {recalls[qs]}", t0)
+        if recalls[qs] >= args.recall:
+            chosen = qs
+            break
+    if chosen is None:
+        chosen = max(recalls, key=lambda x: recalls[x])
+    pipe = make_pipe(chosen)
+
+    # ---- device-resident timing (value)
+    stream = torch.cuda.current_stream()
+    beam_ev = []
+    for _ in range(args.warmup):
+        step(pipe, q.vectors)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start.record(stream)
+    for _ in range(args.steps):
+        pipe.build_lut(q.vectors)
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record(stream)
+        pipe.beam_search()
+        b1.record(stream)
+        beam_ev.append((b0, b1))
+        pipe.posting_scan()
+        pipe.rerank(q.vectors)
+        pipe.merge()
+        if world > 1:
+            s = stream_handle()
+            A.check(L.gofann_offset_ids(A.ptr(pipe.out_ids), pipe.out_ids.numel(), shard_base, s), "offset_ids")
+            dist.all_gather_into_tensor(gath_ids.view(-1), pipe.out_ids.reshape(-1))
+            dist.all_gather_into_tensor(gath_d.view(-1), pipe.out_d.reshape(-1))
+            A.check(L.gofann_shard_merge(A.ptr(gath_ids), A.ptr(gath_d), world, nq, k, A.ptr(fin_ids),
+                                         A.ptr(fin_d), s), "shard_merge")
+    end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = start.elapsed_time(end) / args.steps
+    beam_ms = float(np.mean([a.elapsed_time(b) for a, b in beam_ev]))
+    t = torch.tensor([ms, beam_ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, beam_ms = float(t[0]), float(t[1])
+    value = nq / (ms / 1e3)
+
+    # ---- end to end through host buffers (pinned), copies inside the timed region
+    hq = q.vectors.cpu().pin_memory()
+    hid = torch.empty((nq, k), dtype=torch.int32).pin_memory()
+    hd = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+    # per-step inputs: query vectors and every route table (graph + posting routes)
+    dev_tables = [v for v in dplan.graph.values()] + [v for v in dplan.post.values()] + \
+        [dplan.post_begin, dplan.post_count, dplan.qoff, dplan.qroutes]
+    host_tables = [v.cpu().pin_memory() for v in dev_tables]
+    h2d = hq.numel() + sum(v.numel() * v.element_size() for v in host_tables)
+    dq = torch.empty_like(q.vectors)
+    for _ in range(2):
+        dq.copy_(hq, non_blocking=True)
+        ids, d = step(pipe, dq)
+        hid.copy_(ids, non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_steps = max(3, args.steps // 2)
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(e_steps):
+        dq.copy_(hq, non_blocking=True)
+        for tgt, src in zip(dev_tables, host_tables):
+            tgt.copy_(src, non_blocking=True)
+        ids, d = step(pipe, dq)
+        hid.copy_(ids, non_blocking=True)
+        hd.copy_(d, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = max(e0.elapsed_time(e1), (time.perf_counter() - wall0) * 1e3) / e_steps
+    te = torch.tensor([e_ms], device=device)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e_ms = float(te[0])
+    final_pred = hid[torch.from_numpy(eval_idx)].numpy().view(np.uint32) if rank == 0 else None
+
+    # ---- roofline of the beam-search kernel (counters of the last launch)
+    cnt = pipe.g_counters[:dplan.n_graph].cpu().numpy().view(np.uint32).astype(np.int64)
+    avg_labels = float(idx.label_indices.numel()) / max(1, idx.n)
+    bytes_launch = beam_bytes(cnt, dplan.n_graph, idx.degree, dindex.pq_dim, avg_labels, 100)
+    peaks = measured_peaks()
+    achieved = bytes_launch / (beam_ms / 1e3) / 1e9
+    prof = profiled_traffic()
+    traffic = None
+    if prof and prof.get("workload") == f"config2_n{args.n}_q{args.queries}" and prof.get("queue_size") == chosen:
+        traffic = prof.get("bytes_per_launch")
+
+    if rank == 0:
+        final_recall = W.recall_at_k(final_pred, gt, k)
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": {"workload": "config2: 10M x 192 u8, 200k-tag Zipf(1.1), AND of 1-2 tags, PQ 48x256, "
+                                   "degree 64, exact u8 rerank", "n_base": args.n, "n_queries": nq,
+                       "queue_size": chosen, "recall_at_10": round(final_recall, 4), "recall_sweep": recalls,
+                       "graph_routes": dplan.n_graph, "posting_routes": dplan.n_post,
+                       "graph_rows": idx.stats.get("graph_rows"), "label_graphs": idx.stats.get("groups"),
+                       "l2_flush": "inputs larger than L2 (index ~25 GB, LUTs 4.9 GB per batch)",
+                       "parallelism": f"shard{world}" if world > 1 else "single"},
+            "e2e": {"value": round(nq / (e_ms / 1e3), 1), "unit": "queries/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(nq * k * 8)},
+            "gpu_launches": int(pipe.launches_per_run * args.steps + (2 * args.steps if world > 1 else 0)),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                         "kernel": "beam_search_kernel", "kernel_ms": round(beam_ms, 3),
+                         "algorithmic_bytes_per_launch": int(bytes_launch), "peak_source": peaks["source"]},
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args, data, idx, plan, chosen, t0)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------ CPU legs
+def host_index(idx):
+    """Index arrays copied to host memory for the CPU restatement."""
+    def h(t, dt):
+        return t.cpu().numpy().view(dt) if hasattr(t, "cpu") else np.asarray(t)
+    return dict(
+        graph={"adjacency": h(idx.adjacency, np.uint32), "row_to_sample": h(idx.row_to_sample, np.uint32),
+               "label_offset": idx.label_offset},
+        attrs={"label_indptr": h(idx.label_indptr, np.uint64), "label_indices": h(idx.label_indices, np.uint32)},
+        codes={"pq_codes": h(idx.pq_codes, np.uint8)},
+        base=h(idx.base, np.uint8), centroids=h(idx.pq_centroids, np.float32),
+        posting_ids=h(idx.posting_ids, np.uint32))
+
+
+def cpu_search(hidx, plan, qv, sel, qs, threads):
+    """The reference's path on host cores for the queries `sel`: LUT build,
+    traversal, posting scans, exact rerank (oracle restatement).  Route
+    tables are re-based onto the compact query sample."""
+    from gofann.planner import subset_routes
+    from oracle import oracle as O
+    from gofann import _abi as A
+    pos = np.full(qv.shape[0], -1, np.int64)
+    pos[sel] = np.arange(len(sel))
+    gsel = np.nonzero(pos[plan.graph_query] >= 0)[0]
+    psel = np.nonzero(pos[plan.posting_query] >= 0)[0]
+    qs_v = np.ascontiguousarray(qv[sel])
+    lut = O.pq_build_lut(qs_v.astype(np.float32), hidx["centroids"], hidx["codes"]["pq_codes"].shape[1])
+    gr = subset_routes(plan.graph_routes, gsel)
+    gr["query_row"] = pos[plan.graph_query[gsel]].astype(np.uint32)
+    pr = subset_routes(plan.posting_routes, psel)
+    pr["query_row"] = pos[plan.posting_query[psel]].astype(np.uint32)
+    ids, _, _, _ = O.beam_search(hidx["graph"], hidx["attrs"], hidx["codes"], {"pq_lut": lut}, gr, threads=threads,
+                                 queue_size=qs, result_width=100, predicate_bias=1, alpha=0.15,
+                                 early_stop_mode=A.EARLY_STOP_ADAPTIVE)
+    ri, rd = O.rerank(hidx["base"], A.DTYPE_U8, qs_v, hidx["attrs"], gr, ids, 10)
+    pi, _ = O.posting_scan(hidx["codes"], {"pq_lut": lut}, hidx["attrs"], pr, A.SCORER_PQ, hidx["posting_ids"],
+                           plan.posting_begin[psel], plan.posting_count[psel], 100)
+    pri, prd = O.rerank(hidx["base"], A.DTYPE_U8, qs_v, hidx["attrs"], pr, pi, 10)
+    return ri, pri
+
+
+def sized_sample(hidx, plan, qv, qs, threads, target_s=12.0, first=400, seed=1):
+    """Query sample whose CPU search takes about target_s seconds."""
+    rng = np.random.default_rng(seed)
+    sel = np.sort(rng.choice(qv.shape[0], size=min(first, qv.shape[0]), replace=False))
+    tt = time.perf_counter()
+    cpu_search(hidx, plan, qv, sel, qs, threads)
+    el = time.perf_counter() - tt
+    n = int(min(qv.shape[0], max(first, first * target_s / max(el, 1e-3))))
+    return np.sort(rng.choice(qv.shape[0], size=n, replace=False))
+
+
+def cpu_baseline(args, data, idx, plan, qs, t0):
+    """Oracle restatement of the reference path, timed on this box's host
+    cores over a query sample sized to ~12 s of CPU work."""
+    from oracle import oracle as O
+    from gofann import workload_gpu as W
+    threads = O.cpu_count()
+    hidx = host_index(idx)
+    W._log("index copied to host for the CPU baseline", t0)
+    qv = data["queries"].vectors.cpu().numpy()
+    sel = (np.sort(np.random.default_rng(1).choice(qv.shape[0], args.cpu_sample, replace=False))
+           if args.cpu_sample else sized_sample(hidx, plan, qv, qs, threads))
+    tt = time.perf_counter()
+    cpu_search(hidx, plan, qv, sel, qs, threads)
+    el = time.perf_counter() - tt
+    W._log(f"CPU baseline: {len(sel)} queries in {el:.1f} s", t0)
+    return {"value": round(len(sel) / el, 1), "unit": "queries/s", "cores": threads, "kind": "port",
+            "sample": f"{len(sel)} of {qv.shape[0]} config-2 queries, queue {qs}; LUT build + traversal + "
+                      f"posting scans + exact rerank, {el:.1f} s on {threads} threads"}
+
+
+def run_reference(args):
+    """--impl reference: the reference's search path restated on the CPU
+    (oracle/, all host threads), on bounded samples of the same workload."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+    from gofann import planner, workload_gpu as W
+    from oracle import oracle as O
+    t0 = time.time()
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))) if torch.cuda.is_available() else "cpu"
+    data = W.generate(device=device, seed=args.seed, n=args.n, n_queries=args.queries, t0=t0)
+    # input artefacts only (the reference builds them with cuVS); PQ codes by torch, not this library
+    idx = W.build_index(data, seed=args.seed, t0=t0, torch_encode=True)
+    plan = planner.plan_queries(idx, data["queries"].labels)
+    qs = args.queue_size or 128
+    hidx = host_index(idx)
+    qv = data["queries"].vectors.cpu().numpy()
+    threads = O.cpu_count()
+    rng = np.random.default_rng(2)
+    # each step a bounded sample: the whole timed run targets ~60 s of CPU work
+    per_step = args.cpu_sample or len(sized_sample(hidx, plan, qv, qs, threads, target_s=60.0 / max(1, args.steps)))
+    for _ in range(args.warmup):
+        cpu_search(hidx, plan, qv, np.sort(rng.choice(qv.shape[0], 100, replace=False)), qs, threads)
+    tt = time.perf_counter()
+    for _ in range(args.steps):
+        sel = np.sort(rng.choice(qv.shape[0], per_step, replace=False))
+        cpu_search(hidx, plan, qv, sel, qs, threads)
+    el = time.perf_counter() - tt
+    v = per_step * args.steps / el
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 1), "unit": "queries/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": {"workload": "config2: 10M x 192 u8, 200k-tag Zipf(1.1), AND of 1-2 tags, PQ 48x256, "
+                                   "degree 64, exact u8 rerank", "queue_size": qs, "n_queries_per_step": per_step},
+            "cpu_baseline": {"value": round(v, 1), "unit": "queries/s", "cores": threads, "kind": "port",
+                             "sample": f"{per_step} random queries per step of 100k"},
+            "e2e": {"value": round(v, 1), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gofann(args)
+
+
+if __name__ == "__main__":
+    main()
