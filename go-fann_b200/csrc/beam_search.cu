@@ -23,6 +23,8 @@
 #include "pq_device.cuh"
 #include "rq_device.cuh"
 
+#include <mutex>
+
 namespace gofann {
 namespace {
 
@@ -635,6 +637,173 @@ int gofann_beam_search(const gofann_graph* graph, const gofann_attrs* attrs, con
     if (e != cudaSuccess) return cuda_status(e, "beam_search: counter reset");
     kern<<<blocks, wpb * 32, smem, s>>>(args);
     GOFANN_CHECK_LAUNCH("beam_search_kernel");
+    return GOFANN_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free traversal entry point.
+//
+// Some callers cannot allocate device memory at all: a host process whose
+// device memory is owned by another allocator (a database or JVM/Go runtime
+// embedding this library and handing it only pre-sized buffers), code that
+// must not call cudaMalloc while another library is capturing its stream
+// into a CUDA graph, or latency-critical serving paths where an allocation
+// (and the device synchronisation cudaFree implies) is not acceptable.  For
+// them the traversal's scratch -- the route counter and one 4096-slot
+// visited table per resident warp -- lives in the file-scope device array
+// below instead of a caller-supplied buffer.
+//
+// Limits and sharing: the array holds kNoAllocTables (1,024) visited tables,
+// 16 MiB + 256 B, allocated once per device by the CUDA runtime when this
+// library is loaded and held until the process exits.  At most 1,024 warps
+// run at once in this mode (the grid is capped to that; any number of routes
+// is still processed, since warps pull routes from the counter).  Every call
+// on a device uses the same array, which keeps the previous call's contents:
+// the counter is cleared before each launch and each warp clears its visited
+// table per route, so nothing stale is read.  Calls whose kernels overlap on
+// the GPU (different streams, or different host threads) race on the array
+// and must be serialised by the caller.
+namespace gofann {
+namespace {
+constexpr int kNoAllocTables = 1024;
+constexpr size_t kNoAllocBytes = kCounterBytes + static_cast<size_t>(kNoAllocTables) * kHashCap * sizeof(uint32_t);
+}  // namespace
+}  // namespace gofann
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[gofann::kNoAllocBytes];
+
+namespace gofann {
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_address[kNoAllocMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device.  Host code may
+// not pass the symbol itself to a kernel (in host code it names a host-side
+// stand-in), so the address is looked up once per device, with that device
+// current, on the first call.
+int noalloc_scratch_address(void** out)
+{
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_status(e, "beam_search_noalloc: cudaGetDevice");
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        return fail(GOFANN_ERR_UNSUPPORTED, "beam_search_noalloc: device %d outside 0..%d", dev, kNoAllocMaxDevices - 1);
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_address[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_status(e, "beam_search_noalloc: cudaGetSymbolAddress");
+        g_noalloc_address[dev] = p;
+    }
+    *out = g_noalloc_address[dev];
+    return GOFANN_OK;
+}
+
+}  // namespace
+}  // namespace gofann
+
+extern "C" {
+
+int gofann_beam_search_noalloc(const gofann_graph* graph, const gofann_attrs* attrs, const gofann_codes* codes,
+                               const gofann_prepared* prep, const gofann_routes* routes,
+                               const gofann_search_params* params, const gofann_search_out* out, void* stream)
+{
+    if (!graph || !codes || !prep || !routes || !params || !out)
+        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: null argument");
+    const gofann_search_params& p = *params;
+    if (p.queue_size < 2 || p.queue_size > GOFANN_MAX_QUEUE)
+        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: queue_size %d outside 2..%d", p.queue_size,
+                    GOFANN_MAX_QUEUE);
+    if (p.stop_width < 1 || p.stop_width > GOFANN_MAX_TOPK)
+        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: stop_width %d outside 1..%d", p.stop_width,
+                    GOFANN_MAX_TOPK);
+    if (p.result_width < 1 || p.result_width > GOFANN_MAX_RESULT_WIDTH)
+        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: result_width %d outside 1..%d", p.result_width,
+                    GOFANN_MAX_RESULT_WIDTH);
+    if (p.early_stop_mode < 0 || p.early_stop_mode > 2)
+        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: unknown early_stop_mode %d", p.early_stop_mode);
+    if (!graph->adjacency || !graph->row_to_sample || !graph->label_offset || graph->degree == 0)
+        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: graph arrays missing");
+    if (!routes->query_row || !routes->group_id || !routes->start_local || !out->ids || !out->dists)
+        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: route or output arrays missing");
+    const bool needs_attrs = routes->pred_offsets != nullptr || p.full_label_check != 0 ||
+                             routes->range_modes != nullptr;
+    if (needs_attrs && (!attrs || !attrs->label_indptr || !attrs->label_indices))
+        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: predicates need the sample label CSR");
+    if (routes->pred_offsets && (!routes->clauses || !routes->pred_handles))
+        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: predicate clause arrays missing");
+    bool lut_shared = false;
+    if (p.scorer == GOFANN_SCORER_PQ) {
+        if (!codes->pq_codes || !prep->pq_lut)
+            return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: PQ arrays missing");
+        if (codes->pq_dim == 0 || codes->pq_dim > static_cast<uint32_t>(kMaxPqDim))
+            return fail(GOFANN_ERR_UNSUPPORTED, "beam_search_noalloc: pq_dim %u outside 1..%d", codes->pq_dim,
+                        kMaxPqDim);
+        lut_shared = p.lut_in_shared != 0;
+    } else if (p.scorer == GOFANN_SCORER_RABITQ) {
+        if (!codes->rq_codes || !codes->rq_factors || !codes->rq_anchor_ids || !prep->rq_q8 || !prep->rq_scale ||
+            !prep->rq_k1xsumq || !prep->rq_centroid_dist)
+            return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: RaBitQ arrays missing");
+        if (codes->padded_dim == 0 || codes->padded_dim % 64 != 0 || codes->padded_dim > 4096)
+            return fail(GOFANN_ERR_UNSUPPORTED, "beam_search_noalloc: padded_dim %u unsupported", codes->padded_dim);
+    } else {
+        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: unknown scorer %d", p.scorer);
+    }
+    void* scratch = nullptr;
+    const int st = noalloc_scratch_address(&scratch);
+    if (st != GOFANN_OK) return st;
+    if (routes->n_routes == 0) return GOFANN_OK;
+
+    BeamArgs args{};
+    args.graph = *graph;
+    if (attrs) {
+        args.attrs.indptr = attrs->label_indptr;
+        args.attrs.indices = attrs->label_indices;
+        args.attrs.ranges = attrs->range_values;
+        args.attrs.n_samples = attrs->n_samples;
+        args.attrs.range_count = attrs->range_count;
+    }
+    args.codes = *codes;
+    args.prep = *prep;
+    args.routes = *routes;
+    args.p = p;
+    args.out = *out;
+    args.status = out->status;
+    const SmemLayout L = smem_layout(p, *codes, lut_shared);
+    args.warp_smem = L.total;
+    constexpr size_t kMaxSmem = 227 * 1024;
+    int wpb = kWarpsPerBlock;
+    while (wpb > 1 && static_cast<size_t>(L.total) * wpb > kMaxSmem) --wpb;
+    const size_t smem = static_cast<size_t>(L.total) * wpb;
+    if (smem > kMaxSmem)
+        return fail(GOFANN_ERR_UNSUPPORTED, "beam_search_noalloc: %zu bytes of shared memory per warp exceed 227 KB",
+                    smem);
+    const KernelFn kern = pick_kernel(p.scorer, p.predicate_bias != 0, lut_shared);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_status(e, "beam_search_noalloc: shared memory attribute");
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, wpb * 32, smem);
+    if (e != cudaSuccess) return cuda_status(e, "beam_search_noalloc: occupancy query");
+    if (per_sm <= 0) return fail(GOFANN_ERR_UNSUPPORTED, "beam_search_noalloc: kernel does not fit on an SM");
+    uint32_t blocks = grid_blocks(routes->n_routes, wpb, per_sm);
+    const uint32_t max_blocks = static_cast<uint32_t>(kNoAllocTables / wpb);
+    if (blocks > max_blocks) blocks = max_blocks;
+    const size_t need = kCounterBytes + static_cast<size_t>(blocks) * wpb * kHashCap * sizeof(uint32_t);
+    if (blocks == 0 || need > kNoAllocBytes)
+        return fail(GOFANN_ERR_CAPACITY,
+                    "beam_search_noalloc: %zu bytes of scratch needed, the static scratch holds %zu (%d visited tables)",
+                    need, kNoAllocBytes, kNoAllocTables);
+    args.route_counter = static_cast<uint32_t*>(scratch);
+    args.hash = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(scratch) + kCounterBytes);
+    cudaStream_t s = as_stream(stream);
+    e = cudaMemsetAsync(scratch, 0, sizeof(uint32_t), s);
+    if (e != cudaSuccess) return cuda_status(e, "beam_search_noalloc: counter reset");
+    kern<<<blocks, wpb * 32, smem, s>>>(args);
+    GOFANN_CHECK_LAUNCH("beam_search_kernel (no-alloc)");
     return GOFANN_OK;
 }
 

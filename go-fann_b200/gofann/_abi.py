@@ -205,6 +205,8 @@ def lib() -> C.CDLL:
         "gofann_beam_search": [C.POINTER(Graph), C.POINTER(Attrs), C.POINTER(Codes), C.POINTER(Prepared),
                                C.POINTER(Routes), C.POINTER(SearchParams), C.POINTER(SearchOut), sp, C.c_size_t,
                                sp],
+        "gofann_beam_search_noalloc": [C.POINTER(Graph), C.POINTER(Attrs), C.POINTER(Codes), C.POINTER(Prepared),
+                                       C.POINTER(Routes), C.POINTER(SearchParams), C.POINTER(SearchOut), sp],
         "gofann_posting_scan": [C.POINTER(Codes), C.POINTER(Prepared), C.POINTER(Attrs), C.POINTER(Routes),
                                 C.c_int, sp, sp, sp, I32, I32, sp, sp, sp],
         "gofann_rerank": [sp, C.c_int, U32, U32, sp, C.POINTER(Attrs), C.POINTER(Routes), sp, U32, I32, sp, sp,
@@ -238,6 +240,7 @@ def check(status: int, where: str) -> None:
 EXPORTED = ("gofann_abi_version", "gofann_last_error", "gofann_device_sm_count", "gofann_pq_build_lut",
             "gofann_pq_adc", "gofann_pq_encode", "gofann_rabitq_quantize", "gofann_rabitq_centroid_dist",
             "gofann_rabitq_score", "gofann_beam_search_scratch_bytes", "gofann_beam_search",
+            "gofann_beam_search_noalloc",
             "gofann_posting_scan", "gofann_rerank", "gofann_route_merge", "gofann_shard_merge",
             "gofann_offset_ids")
 

@@ -243,6 +243,24 @@ GOFANN_API int gofann_beam_search(const gofann_graph* graph, const gofann_attrs*
                        const gofann_search_out* out, void* scratch, size_t scratch_bytes,
                        void* stream);
 
+/* Allocation-free variant of gofann_beam_search (no counterpart in the
+ * reference, which allocates its traversal scratch with cudaMalloc).  For
+ * callers that cannot allocate device memory themselves -- a host runtime or
+ * database whose allocator owns the device, code that must not allocate
+ * while a stream is being captured into a CUDA graph, latency-critical paths
+ * -- the visited tables and route counter live in a static device array of
+ * 16 MiB + 256 B inside the library (1,024 visited tables), held by every GPU
+ * that loads the library until the process exits.  At most 1,024 warps run
+ * at once; any number of routes is accepted.  The first call on each device
+ * looks up the array's device address (make it before any stream capture
+ * begins).  Calls share the array: calls whose kernels overlap on the GPU
+ * race and must be serialised by the caller.  Results equal
+ * gofann_beam_search's bit for bit. */
+GOFANN_API int gofann_beam_search_noalloc(const gofann_graph* graph, const gofann_attrs* attrs,
+                                          const gofann_codes* codes, const gofann_prepared* prep,
+                                          const gofann_routes* routes, const gofann_search_params* params,
+                                          const gofann_search_out* out, void* stream);
+
 /* ------------------------------------------------------- posting scans */
 /* Brute-force scan of each route's posting slice [begin, begin+count) of
  * posting_ids, DNF filter (before scoring, or after a can-enter test when
