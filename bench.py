@@ -49,7 +49,7 @@ def parse():
     ap.add_argument("--eval", type=int, default=2000, help="queries with exact ground truth")
     ap.add_argument("--queue-size", type=int, default=0, help="fixed queue size (0 = sweep)")
     ap.add_argument("--recall", type=float, default=0.95)
-    ap.add_argument("--lut-shared", type=int, default=0)
+    ap.add_argument("--pq-mode", type=int, default=0, help="0 LUT in global, 1 LUT in shared, 2 direct")
     ap.add_argument("--cpu-sample", type=int, default=0, help="queries in the CPU baseline sample (0 = auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
@@ -197,7 +197,7 @@ def run_gofann(args):
     k = 10
 
     def make_pipe(qs):
-        cfg = SearchConfig(queue_size=qs, result_width=100, lut_in_shared=args.lut_shared)
+        cfg = SearchConfig(queue_size=qs, result_width=100, pq_mode=args.pq_mode)
         return Pipeline(dindex, dplan, cfg)
 
     gath_ids = torch.empty((world, nq, k), dtype=torch.int32, device=device) if world > 1 else None

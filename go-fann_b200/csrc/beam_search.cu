@@ -29,6 +29,13 @@ namespace gofann {
 namespace {
 
 constexpr int kWarpsPerBlock = 4;
+// Frontier payload: local row in bits 0..29, bit 31 = expanded ("used",
+// backend_pq.cu:738-758), bit 30 = the row passed the route's DNF predicate
+// when it was admitted (recorded only with predicate bias, where the
+// predicate is evaluated at admission; the expansion then reuses it instead
+// of evaluating the same predicate on the same sample again).
+constexpr uint32_t kPassBit = 0x40000000u;
+constexpr uint32_t kRowMask = 0x3fffffffu;
 constexpr int kMaxSteps = 1 << 22;  // hard bound when max_steps == 0
 
 struct WarpState {
@@ -63,7 +70,7 @@ struct SmemLayout {
 __host__ __device__ inline uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
 
 __host__ __device__ inline SmemLayout smem_layout(const gofann_search_params& p, const gofann_codes& c,
-                                                  bool lut_shared)
+                                                  int pq_mode, uint32_t dim)
 {
     SmemLayout s;
     uint32_t o = 0;
@@ -77,7 +84,8 @@ __host__ __device__ inline SmemLayout smem_layout(const gofann_search_params& p,
     s.state = o; o = align16(o + sizeof(WarpState));
     s.table = o;
     if (p.scorer == GOFANN_SCORER_PQ) {
-        if (lut_shared) o = align16(o + c.pq_dim * GOFANN_PQ_CENTROIDS * 4);
+        if (pq_mode == GOFANN_PQ_LUT_SHARED) o = align16(o + c.pq_dim * GOFANN_PQ_CENTROIDS * 4);
+        if (pq_mode == GOFANN_PQ_DIRECT) o = align16(o + dim * 4);
     } else {
         o = align16(o + 8 * (c.padded_dim / 32) * 4);
     }
@@ -168,29 +176,37 @@ __device__ __forceinline__ bool coop_pickup(FPair* f, int size, FPair* out, int 
     return bi >= 0;
 }
 
-template <int kScorer, bool kLutShared>
+// kMode: PQ_LUT_GLOBAL / PQ_LUT_SHARED read a table row; PQ_DIRECT evaluates
+// entries from the query row (shared memory) and the codebook; kW is the
+// subvector width when it is 4 (vector loads), else 0; kMaxM bounds pq_dim.
+template <int kScorer, int kMode, int kW, int kMaxM>
 struct Scorer {
-    const float* lut_row;  // PQ
+    const float* lut_row;  // PQ table row, or the query row in PQ_DIRECT
+    const float* cent;     // PQ_DIRECT codebook
+    int dim;
     RqQueryView rq;        // RaBitQ
     __device__ __forceinline__ float operator()(const gofann_codes& c, uint32_t sample) const
     {
         if constexpr (kScorer == GOFANN_SCORER_PQ) {
-            return pq_adc_warp_order(lut_row, c.pq_codes + static_cast<size_t>(sample) * c.pq_dim,
-                                     static_cast<int>(c.pq_dim));
+            const uint8_t* code = c.pq_codes + static_cast<size_t>(sample) * c.pq_dim;
+            if constexpr (kMode == GOFANN_PQ_DIRECT)
+                return pq_adc_direct<kW, kMaxM>(lut_row, cent, dim, code, static_cast<int>(c.pq_dim));
+            else
+                return pq_adc_warp_order(lut_row, code, static_cast<int>(c.pq_dim));
         } else {
             return rq_estimate(c, rq, sample);
         }
     }
 };
 
-template <int kScorer, bool kBias, bool kLutShared>
+template <int kScorer, bool kBias, int kMode, int kW, int kMaxM>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamArgs a)
 {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const gofann_search_params& p = a.p;
-    const SmemLayout L = smem_layout(p, a.codes, kLutShared);
+    const SmemLayout L = smem_layout(p, a.codes, kMode, a.prep.dim);
     unsigned char* base = smem_raw + static_cast<size_t>(warp) * a.warp_smem;
     FPair* frontier = reinterpret_cast<FPair*>(base + L.frontier);
     RPair* topk = reinterpret_cast<RPair*>(base + L.topk);
@@ -224,17 +240,31 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
             const uint4 e = make_uint4(kU32Max, kU32Max, kU32Max, kU32Max);
             for (int i = lane; i < kHashCap / 4; i += kWarp) h4[i] = e;
         }
-        Scorer<kScorer, kLutShared> score;
+        Scorer<kScorer, kMode, kW, kMaxM> score;
         if constexpr (kScorer == GOFANN_SCORER_PQ) {
-            const float* g = a.prep.pq_lut + static_cast<size_t>(row) * a.codes.pq_dim * GOFANN_PQ_CENTROIDS;
-            if constexpr (kLutShared) {
-                const float4* s4 = reinterpret_cast<const float4*>(g);
-                float4* d4 = reinterpret_cast<float4*>(table);
-                const int n4 = static_cast<int>(a.codes.pq_dim) * GOFANN_PQ_CENTROIDS / 4;
-                for (int i = lane; i < n4; i += kWarp) d4[i] = __ldg(s4 + i);
+            if constexpr (kMode == GOFANN_PQ_DIRECT) {
+                const int dim = static_cast<int>(a.prep.dim);
+                if (a.prep.pq_query_dtype == GOFANN_DTYPE_U8) {
+                    const uint8_t* qr = static_cast<const uint8_t*>(a.prep.pq_query) + static_cast<size_t>(row) * dim;
+                    for (int i = lane; i < dim; i += kWarp) table[i] = static_cast<float>(qr[i]);
+                } else {
+                    const float* qr = static_cast<const float*>(a.prep.pq_query) + static_cast<size_t>(row) * dim;
+                    for (int i = lane; i < dim; i += kWarp) table[i] = qr[i];
+                }
                 score.lut_row = table;
+                score.cent = a.prep.pq_centroids;
+                score.dim = dim;
             } else {
-                score.lut_row = g;
+                const float* g = a.prep.pq_lut + static_cast<size_t>(row) * a.codes.pq_dim * GOFANN_PQ_CENTROIDS;
+                if constexpr (kMode == GOFANN_PQ_LUT_SHARED) {
+                    const float4* s4 = reinterpret_cast<const float4*>(g);
+                    float4* d4 = reinterpret_cast<float4*>(table);
+                    const int n4 = static_cast<int>(a.codes.pq_dim) * GOFANN_PQ_CENTROIDS / 4;
+                    for (int i = lane; i < n4; i += kWarp) d4[i] = __ldg(s4 + i);
+                    score.lut_row = table;
+                } else {
+                    score.lut_row = g;
+                }
             }
         } else {
             rq_build_planes(a.prep.rq_q8 + static_cast<size_t>(row) * a.codes.padded_dim,
@@ -272,6 +302,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
             kp.first = start;
             kp.second = begin_id;
             kp.base = start;
+            if (kBias && pred_on && pred_matches(a.routes, a.attrs, route, begin_sample)) kp.second |= kPassBit;
             smmh_insert(frontier, st.heap_size, kp);
             hash_add(hash, begin_id);
         }
@@ -306,7 +337,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
                 __syncwarp();
             }
             if (st.exhausted) break;
-            const uint32_t now_row = st.now.second & ~kPoolUsed;
+            const uint32_t now_row = st.now.second & kRowMask;
             const uint32_t grow = label_offset + now_row;
 
             if (lane == 0) {
@@ -331,7 +362,10 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
                 const bool exact_range = active == 0 || matched == active;
                 int nfr = (p.full_label_check == 0 || labels_match(a.routes, a.attrs, route, sample)) ? 1 : 2;
                 if (pred_on) {
-                    nfr = pred_matches(a.routes, a.attrs, route, sample) ? 1 : 2;
+                    if (kBias)
+                        nfr = (st.now.second & kPassBit) ? 1 : 2;
+                    else
+                        nfr = pred_matches(a.routes, a.attrs, route, sample) ? 1 : 2;
                     ++st.n_probe;
                 } else if (!a.routes.route_compiled || !a.routes.route_compiled[route]) {
                     nfr = (nfr == 1 && bit_match && exact_range) ? 1 : 2;
@@ -425,18 +459,22 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
 #pragma unroll
             for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
                 const int i = half * kWarp + lane;
-                bool reject = false;
+                bool reject = false, pass = false;
                 if (i < len) {
                     float pr = dist[i];
                     if (kBias && pred_on) {
-                        const bool pass = pred_matches(a.routes, a.attrs, route, slist[i]);
+                        pass = pred_matches(a.routes, a.attrs, route, slist[i]);
                         pr = pred_priority(dist[i], st.penalty, pass);
                     }
                     prio[i] = pr;
                     reject = full && maxv < pr;  // definitely rejected (max only decreases)
                 }
                 const unsigned m = __ballot_sync(kFull, reject);
-                if (lane == 0) st.rej[half] = m;
+                const unsigned pm = __ballot_sync(kFull, pass);
+                if (lane == 0) {
+                    st.rej[half] = m;
+                    st.pass[half] = pm;
+                }
             }
             __syncwarp();
             if (lane == 0) {
@@ -447,7 +485,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
                     FPair kp;
                     kp.first = prio[i];
                     kp.base = dist[i];
-                    kp.second = list[i];
+                    kp.second = list[i] | (((st.pass[i >> 5] >> (i & 31)) & 1u) ? kPassBit : 0u);
                     if (st.heap_size >= QS + 1 && frontier[2].first < kp.first) continue;
                     smmh_insert(frontier, st.heap_size, kp);
                     hash_add(hash, list[i]);
@@ -513,13 +551,48 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
 
 using KernelFn = void (*)(BeamArgs);
 
-KernelFn pick_kernel(int scorer, bool bias, bool lut_shared)
+template <bool kBias>
+KernelFn pick_pq(int mode, bool w4, bool small_m)
 {
-    if (scorer == GOFANN_SCORER_PQ) {
-        if (bias) return lut_shared ? beam_search_kernel<0, true, true> : beam_search_kernel<0, true, false>;
-        return lut_shared ? beam_search_kernel<0, false, true> : beam_search_kernel<0, false, false>;
+    if (mode == GOFANN_PQ_DIRECT) {
+        if (w4) return small_m ? beam_search_kernel<0, kBias, GOFANN_PQ_DIRECT, 4, 64>
+                               : beam_search_kernel<0, kBias, GOFANN_PQ_DIRECT, 4, 128>;
+        return small_m ? beam_search_kernel<0, kBias, GOFANN_PQ_DIRECT, 0, 64>
+                       : beam_search_kernel<0, kBias, GOFANN_PQ_DIRECT, 0, 128>;
     }
-    return bias ? beam_search_kernel<1, true, false> : beam_search_kernel<1, false, false>;
+    if (mode == GOFANN_PQ_LUT_SHARED) return beam_search_kernel<0, kBias, GOFANN_PQ_LUT_SHARED, 0, 128>;
+    return beam_search_kernel<0, kBias, GOFANN_PQ_LUT_GLOBAL, 0, 128>;
+}
+
+// w4: 4-wide subvectors with 16-byte aligned codebook rows (vector loads);
+// small_m: pq_dim <= 64 (a shorter unrolled subspace loop).
+KernelFn pick_kernel(int scorer, bool bias, int pq_mode, bool w4, bool small_m)
+{
+    if (scorer == GOFANN_SCORER_PQ)
+        return bias ? pick_pq<true>(pq_mode, w4, small_m) : pick_pq<false>(pq_mode, w4, small_m);
+    return bias ? beam_search_kernel<1, true, 0, 0, 64> : beam_search_kernel<1, false, 0, 0, 64>;
+}
+
+// Validates the PQ-mode specific inputs; sets w4 / small_m.
+int check_pq_mode(const gofann_search_params& p, const gofann_codes& c, const gofann_prepared& prep, bool& w4,
+                  bool& small_m, const char* who)
+{
+    w4 = false;
+    small_m = c.pq_dim <= 64;
+    if (p.pq_mode == GOFANN_PQ_DIRECT) {
+        if (!prep.pq_query || !prep.pq_centroids || prep.dim == 0 || prep.dim % c.pq_dim != 0)
+            return fail(GOFANN_ERR_INVALID, "%s: direct PQ scoring needs pq_query, pq_centroids and dim %% pq_dim == 0",
+                        who);
+        if (prep.pq_query_dtype != GOFANN_DTYPE_U8 && prep.pq_query_dtype != GOFANN_DTYPE_F32)
+            return fail(GOFANN_ERR_INVALID, "%s: pq_query_dtype must be u8 or f32", who);
+        if (prep.dim > 4096) return fail(GOFANN_ERR_UNSUPPORTED, "%s: dim %u above 4096", who, prep.dim);
+        w4 = prep.dim / c.pq_dim == 4 && (reinterpret_cast<uintptr_t>(prep.pq_centroids) & 15) == 0;
+        return GOFANN_OK;
+    }
+    if (p.pq_mode != GOFANN_PQ_LUT_GLOBAL && p.pq_mode != GOFANN_PQ_LUT_SHARED)
+        return fail(GOFANN_ERR_INVALID, "%s: unknown pq_mode %d", who, p.pq_mode);
+    if (!prep.pq_lut) return fail(GOFANN_ERR_INVALID, "%s: PQ lookup table missing", who);
+    return GOFANN_OK;
 }
 
 // Persistent grid: at most one warp per route, at most what fits resident.
@@ -578,12 +651,15 @@ int gofann_beam_search(const gofann_graph* graph, const gofann_attrs* attrs, con
         return fail(GOFANN_ERR_INVALID, "beam_search: predicates need the sample label CSR");
     if (routes->pred_offsets && (!routes->clauses || !routes->pred_handles))
         return fail(GOFANN_ERR_INVALID, "beam_search: predicate clause arrays missing");
-    bool lut_shared = false;
+    int pq_mode = GOFANN_PQ_LUT_GLOBAL;
+    bool w4 = false, small_m = true;
     if (p.scorer == GOFANN_SCORER_PQ) {
-        if (!codes->pq_codes || !prep->pq_lut) return fail(GOFANN_ERR_INVALID, "beam_search: PQ arrays missing");
+        if (!codes->pq_codes) return fail(GOFANN_ERR_INVALID, "beam_search: PQ codes missing");
         if (codes->pq_dim == 0 || codes->pq_dim > static_cast<uint32_t>(kMaxPqDim))
             return fail(GOFANN_ERR_UNSUPPORTED, "beam_search: pq_dim %u outside 1..%d", codes->pq_dim, kMaxPqDim);
-        lut_shared = p.lut_in_shared != 0;
+        const int st = check_pq_mode(p, *codes, *prep, w4, small_m, "beam_search");
+        if (st != GOFANN_OK) return st;
+        pq_mode = p.pq_mode;
     } else if (p.scorer == GOFANN_SCORER_RABITQ) {
         if (!codes->rq_codes || !codes->rq_factors || !codes->rq_anchor_ids || !prep->rq_q8 || !prep->rq_scale ||
             !prep->rq_k1xsumq || !prep->rq_centroid_dist)
@@ -610,7 +686,7 @@ int gofann_beam_search(const gofann_graph* graph, const gofann_attrs* attrs, con
     args.p = p;
     args.out = *out;
     args.status = out->status;
-    const SmemLayout L = smem_layout(p, *codes, lut_shared);
+    const SmemLayout L = smem_layout(p, *codes, pq_mode, prep->dim);
     args.warp_smem = L.total;
     constexpr size_t kMaxSmem = 227 * 1024;
     int wpb = kWarpsPerBlock;
@@ -619,7 +695,7 @@ int gofann_beam_search(const gofann_graph* graph, const gofann_attrs* attrs, con
     if (smem > kMaxSmem)
         return fail(GOFANN_ERR_UNSUPPORTED, "beam_search: %zu bytes of shared memory per warp exceed 227 KB", smem);
     const bool bias = p.predicate_bias != 0;
-    const KernelFn kern = pick_kernel(p.scorer, bias, lut_shared);
+    const KernelFn kern = pick_kernel(p.scorer, bias, pq_mode, w4, small_m);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return cuda_status(e, "beam_search: shared memory attribute");
     int per_sm = 0;
@@ -736,14 +812,16 @@ int gofann_beam_search_noalloc(const gofann_graph* graph, const gofann_attrs* at
         return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: predicates need the sample label CSR");
     if (routes->pred_offsets && (!routes->clauses || !routes->pred_handles))
         return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: predicate clause arrays missing");
-    bool lut_shared = false;
+    int pq_mode = GOFANN_PQ_LUT_GLOBAL;
+    bool w4 = false, small_m = true;
     if (p.scorer == GOFANN_SCORER_PQ) {
-        if (!codes->pq_codes || !prep->pq_lut)
-            return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: PQ arrays missing");
+        if (!codes->pq_codes) return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: PQ codes missing");
         if (codes->pq_dim == 0 || codes->pq_dim > static_cast<uint32_t>(kMaxPqDim))
             return fail(GOFANN_ERR_UNSUPPORTED, "beam_search_noalloc: pq_dim %u outside 1..%d", codes->pq_dim,
                         kMaxPqDim);
-        lut_shared = p.lut_in_shared != 0;
+        const int cst = check_pq_mode(p, *codes, *prep, w4, small_m, "beam_search_noalloc");
+        if (cst != GOFANN_OK) return cst;
+        pq_mode = p.pq_mode;
     } else if (p.scorer == GOFANN_SCORER_RABITQ) {
         if (!codes->rq_codes || !codes->rq_factors || !codes->rq_anchor_ids || !prep->rq_q8 || !prep->rq_scale ||
             !prep->rq_k1xsumq || !prep->rq_centroid_dist)
@@ -773,7 +851,7 @@ int gofann_beam_search_noalloc(const gofann_graph* graph, const gofann_attrs* at
     args.p = p;
     args.out = *out;
     args.status = out->status;
-    const SmemLayout L = smem_layout(p, *codes, lut_shared);
+    const SmemLayout L = smem_layout(p, *codes, pq_mode, prep->dim);
     args.warp_smem = L.total;
     constexpr size_t kMaxSmem = 227 * 1024;
     int wpb = kWarpsPerBlock;
@@ -782,7 +860,7 @@ int gofann_beam_search_noalloc(const gofann_graph* graph, const gofann_attrs* at
     if (smem > kMaxSmem)
         return fail(GOFANN_ERR_UNSUPPORTED, "beam_search_noalloc: %zu bytes of shared memory per warp exceed 227 KB",
                     smem);
-    const KernelFn kern = pick_kernel(p.scorer, p.predicate_bias != 0, lut_shared);
+    const KernelFn kern = pick_kernel(p.scorer, p.predicate_bias != 0, pq_mode, w4, small_m);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return cuda_status(e, "beam_search_noalloc: shared memory attribute");
     int per_sm = 0;

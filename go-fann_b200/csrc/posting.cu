@@ -57,11 +57,31 @@ __global__ void __launch_bounds__(kScanThreads) posting_scan_kernel(
 
     RqQueryView rq{};
     if constexpr (kScorer == GOFANN_SCORER_PQ) {
-        const float4* g = reinterpret_cast<const float4*>(prep.pq_lut + static_cast<size_t>(row) * codes.pq_dim *
-                                                                            GOFANN_PQ_CENTROIDS);
-        float4* t4 = reinterpret_cast<float4*>(table);
-        for (int i = tid; i < static_cast<int>(codes.pq_dim) * GOFANN_PQ_CENTROIDS / 4; i += kScanThreads)
-            t4[i] = __ldg(g + i);
+        if (prep.pq_lut) {
+            const float4* g = reinterpret_cast<const float4*>(prep.pq_lut + static_cast<size_t>(row) * codes.pq_dim *
+                                                                                GOFANN_PQ_CENTROIDS);
+            float4* t4 = reinterpret_cast<float4*>(table);
+            for (int i = tid; i < static_cast<int>(codes.pq_dim) * GOFANN_PQ_CENTROIDS / 4; i += kScanThreads)
+                t4[i] = __ldg(g + i);
+        } else {
+            // fused table build (computePQTable, backend_pq.cu:1999-2022, which
+            // the reference also runs inside its scan): query row to shared
+            // memory, then thread c evaluates column c of every subspace
+            const int dim = static_cast<int>(prep.dim);
+            float* q = table + codes.pq_dim * GOFANN_PQ_CENTROIDS;
+            if (prep.pq_query_dtype == GOFANN_DTYPE_U8) {
+                const uint8_t* qr = static_cast<const uint8_t*>(prep.pq_query) + static_cast<size_t>(row) * dim;
+                for (int i = tid; i < dim; i += kScanThreads) q[i] = static_cast<float>(qr[i]);
+            } else {
+                const float* qr = static_cast<const float*>(prep.pq_query) + static_cast<size_t>(row) * dim;
+                for (int i = tid; i < dim; i += kScanThreads) q[i] = qr[i];
+            }
+            __syncthreads();
+            const int w = dim / static_cast<int>(codes.pq_dim);
+            const float* crow = prep.pq_centroids + static_cast<size_t>(tid) * dim;  // kScanThreads == 256
+            for (int m = 0; m < static_cast<int>(codes.pq_dim); ++m)
+                table[m * GOFANN_PQ_CENTROIDS + tid] = pq_entry<0>(q + m * w, crow + m * w, w);
+        }
     } else {
         rq_build_planes(prep.rq_q8 + static_cast<size_t>(row) * codes.padded_dim, static_cast<int>(codes.padded_dim),
                         reinterpret_cast<uint32_t*>(table), tid, kScanThreads);
@@ -134,10 +154,16 @@ int gofann_posting_scan(const gofann_codes* codes, const gofann_prepared* prep, 
     }
     size_t table_bytes = 0;
     if (scorer == GOFANN_SCORER_PQ) {
-        if (!codes->pq_codes || !prep->pq_lut) return fail(GOFANN_ERR_INVALID, "posting_scan: PQ arrays missing");
+        if (!codes->pq_codes) return fail(GOFANN_ERR_INVALID, "posting_scan: PQ codes missing");
         if (codes->pq_dim == 0 || codes->pq_dim > static_cast<uint32_t>(kMaxPqDim))
             return fail(GOFANN_ERR_UNSUPPORTED, "posting_scan: pq_dim %u unsupported", codes->pq_dim);
         table_bytes = static_cast<size_t>(codes->pq_dim) * GOFANN_PQ_CENTROIDS * sizeof(float);
+        if (!prep->pq_lut) {
+            if (!prep->pq_query || !prep->pq_centroids || prep->dim == 0 || prep->dim % codes->pq_dim != 0 ||
+                prep->dim > 4096)
+                return fail(GOFANN_ERR_INVALID, "posting_scan: needs pq_lut, or pq_query + pq_centroids + dim");
+            table_bytes += static_cast<size_t>(prep->dim) * sizeof(float);
+        }
     } else if (scorer == GOFANN_SCORER_RABITQ) {
         if (!codes->rq_codes || !prep->rq_q8) return fail(GOFANN_ERR_INVALID, "posting_scan: RaBitQ arrays missing");
         if (codes->padded_dim == 0 || codes->padded_dim % 64 != 0 || codes->padded_dim > 4096)

@@ -64,6 +64,58 @@ __device__ __forceinline__ float pq_adc_warp_order(const float* lut_row, const u
     return pq_adc_words(lut_row, cw, pq_dim);
 }
 
+// Table entry (m, c) = sum over the subvector of fma(diff, diff, acc), diff =
+// q - c, sequential (computePQTable, backend_pq.cu:1999-2022).  `q` is the
+// query subvector (shared memory), `cr` the centroid subvector (global).
+template <int kW>
+__device__ __forceinline__ float pq_entry(const float* q, const float* __restrict__ cr, int w)
+{
+    float acc = 0.0f;
+    if constexpr (kW == 4) {
+        const float4 c = __ldg(reinterpret_cast<const float4*>(cr));
+        float d = __fsub_rn(q[0], c.x);
+        acc = __fmaf_rn(d, d, acc);
+        d = __fsub_rn(q[1], c.y);
+        acc = __fmaf_rn(d, d, acc);
+        d = __fsub_rn(q[2], c.z);
+        acc = __fmaf_rn(d, d, acc);
+        d = __fsub_rn(q[3], c.w);
+        acc = __fmaf_rn(d, d, acc);
+    } else {
+        for (int d = 0; d < w; ++d) {
+            const float diff = __fsub_rn(q[d], __ldg(cr + d));
+            acc = __fmaf_rn(diff, diff, acc);
+        }
+    }
+    return acc;
+}
+
+// ADC in the reference's warp order with every table entry evaluated from
+// the query (shared memory, [dim] floats) and the codebook ([256][dim],
+// global, L1/L2-resident since all routes share it) instead of read from a
+// per-query table: same operations in the same order, so the same bits, and
+// no 48 KB table per in-flight query.
+template <int kW, int kMaxM>
+__device__ __forceinline__ float pq_adc_direct(const float* q, const float* __restrict__ cent, int dim,
+                                               const uint8_t* code, int pq_dim)
+{
+    uint32_t cw[kMaxPqDim / 4];
+    load_code_words(code, pq_dim, cw);
+    const int w = dim / pq_dim;
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+#pragma unroll
+    for (int m = 0; m < kMaxM; ++m) {
+        if (m < pq_dim) {
+            const uint32_t c = code_byte(cw, m);
+            const float e = pq_entry<kW>(q + m * w, cent + static_cast<size_t>(c) * dim + m * w, w);
+            v[m & 31] = __fadd_rn(v[m & 31], e);
+        }
+    }
+    return butterfly_sum32(v);
+}
+
 // Posting-scan order: sequential over subspaces (backend_pq.cu:2101-2104).
 __device__ __forceinline__ float pq_adc_sequential(const float* lut_row, const uint8_t* code, int pq_dim)
 {

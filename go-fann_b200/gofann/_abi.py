@@ -21,6 +21,7 @@ ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_CAPACITY, ERR_TIMEOUT = -1, -2, -3, 
 EARLY_STOP_FIXED, EARLY_STOP_OFF, EARLY_STOP_ADAPTIVE = 0, 1, 2
 SCORER_PQ, SCORER_RABITQ = 0, 1
 DTYPE_U8, DTYPE_F32, DTYPE_F16 = 0, 1, 2
+PQ_LUT_GLOBAL, PQ_LUT_SHARED, PQ_DIRECT = 0, 1, 2
 MAX_DEGREE, MAX_QUEUE, MAX_TOPK, MAX_RESULT_WIDTH, MAX_SHORTLIST = 64, 512, 10, 512, 400
 PQ_CENTROIDS, HASH_CAPACITY = 256, 4096
 U32MAX = 0xFFFFFFFF
@@ -60,7 +61,8 @@ class Codes(C.Structure):
 
 class Prepared(C.Structure):
     _fields_ = [("pq_lut", P), ("rq_q8", P), ("rq_scale", P), ("rq_k1xsumq", P), ("rq_centroid_dist", P),
-                ("n_rows", U32), ("reserved", U32)]
+                ("n_rows", U32), ("reserved", U32), ("pq_query", P), ("pq_centroids", P), ("pq_query_dtype", I32),
+                ("dim", U32)]
 
 
 class Routes(C.Structure):
@@ -75,7 +77,7 @@ class SearchParams(C.Structure):
     _fields_ = [("queue_size", I32), ("stop_width", I32), ("result_width", I32), ("finish_limit", I32),
                 ("early_stop_mode", I32), ("max_steps", I32), ("scorer", I32), ("predicate_bias", I32),
                 ("alpha", C.c_float), ("pending_base_stop", I32), ("full_label_check", I32),
-                ("lut_in_shared", I32)]
+                ("pq_mode", I32)]
 
 
 class SearchOut(C.Structure):
@@ -148,7 +150,13 @@ def fill_prepared(p: dict) -> Prepared:
     s.rq_scale = ptr(p.get("rq_scale"))
     s.rq_k1xsumq = ptr(p.get("rq_k1xsumq"))
     s.rq_centroid_dist = ptr(p.get("rq_centroid_dist"))
-    for key in ("pq_lut", "rq_q8"):
+    q = p.get("pq_query")
+    if q is not None:
+        s.pq_query = ptr(q)
+        s.pq_centroids = ptr(p["pq_centroids"])
+        s.dim = int(q.shape[1])
+        s.pq_query_dtype = DTYPE_U8 if str(q.dtype).endswith("uint8") else DTYPE_F32
+    for key in ("pq_lut", "rq_q8", "pq_query"):
         if p.get(key) is not None:
             s.n_rows = int(p[key].shape[0])
     return s
@@ -173,7 +181,7 @@ def fill_params(**kw) -> SearchParams:
     s = SearchParams()
     defaults = dict(queue_size=64, stop_width=10, result_width=100, finish_limit=100,
                     early_stop_mode=EARLY_STOP_ADAPTIVE, max_steps=0, scorer=SCORER_PQ, predicate_bias=0,
-                    alpha=0.15, pending_base_stop=0, full_label_check=0, lut_in_shared=0)
+                    alpha=0.15, pending_base_stop=0, full_label_check=0, pq_mode=PQ_LUT_GLOBAL)
     defaults.update(kw)
     for k, v in defaults.items():
         setattr(s, k, v)

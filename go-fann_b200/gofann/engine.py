@@ -57,7 +57,7 @@ class SearchConfig:
     max_steps: int = 0
     predicate_bias: int = 1
     alpha: float = 0.15
-    lut_in_shared: int = 0
+    pq_mode: int = A.PQ_LUT_GLOBAL
     lowfreq_shortlist: int = 100
     topk: int = 10
 
@@ -65,7 +65,7 @@ class SearchConfig:
         return A.fill_params(queue_size=self.queue_size, stop_width=self.stop_width, result_width=self.result_width,
                              finish_limit=self.finish_limit, early_stop_mode=self.early_stop_mode,
                              max_steps=self.max_steps, scorer=scorer, predicate_bias=self.predicate_bias,
-                             alpha=self.alpha, lut_in_shared=self.lut_in_shared)
+                             alpha=self.alpha, pq_mode=self.pq_mode)
 
 
 class DeviceIndex:
@@ -123,7 +123,9 @@ class Pipeline:
         d = dindex.device
         nq, ng, npo = dplan.n_queries, dplan.n_graph, dplan.n_post
         rw, sl, k = cfg.result_width, cfg.lowfreq_shortlist, cfg.topk
-        self.lut = torch.empty((nq, dindex.pq_dim, A.PQ_CENTROIDS), dtype=torch.float32, device=d)
+        # a per-query table batch is only materialised for the table modes
+        self.lut = (torch.empty((nq, dindex.pq_dim, A.PQ_CENTROIDS), dtype=torch.float32, device=d)
+                    if cfg.pq_mode != A.PQ_DIRECT else None)
         self.g_ids = torch.empty((max(ng, 1), rw), dtype=torch.int32, device=d)
         self.g_d = torch.empty((max(ng, 1), rw), dtype=torch.float32, device=d)
         self.g_steps = torch.empty(max(ng, 1), dtype=torch.int32, device=d)
@@ -139,13 +141,30 @@ class Pipeline:
         self.scratch = torch.empty(self.scratch_bytes, dtype=torch.uint8, device=d)
         self.prep = {"pq_lut": self.lut}
         self.prep_s = A.fill_prepared(self.prep)
+        self.queries = None
         self.params = cfg.params(A.SCORER_PQ)
         self.out_s = A.SearchOut(ids=A.ptr(self.g_ids), dists=A.ptr(self.g_d), steps=A.ptr(self.g_steps),
                                  counters=A.ptr(self.g_counters), status=A.ptr(self.status))
-        self.launches_per_run = 1 + (1 if ng else 0) + (1 if npo else 0) + (1 if ng else 0) + (1 if npo else 0) + 2
+        self.launches_per_run = ((1 if cfg.pq_mode != A.PQ_DIRECT else 0) + 2 * (1 if ng else 0) +
+                                 2 * (1 if npo else 0) + 1)
 
     # -- individual stages (device pointers, current stream) --------------
+    def set_queries(self, queries: torch.Tensor):
+        """Points the prepared state at this batch's query rows."""
+        if queries is self.queries:
+            return
+        self.queries = queries
+        if self.cfg.pq_mode == A.PQ_DIRECT:
+            self.prep = {"pq_query": queries, "pq_centroids": self.di.pq_centroids}
+        else:
+            self.prep = {"pq_lut": self.lut}
+        self.prep_s = A.fill_prepared(self.prep)
+
     def build_lut(self, queries: torch.Tensor, stream=None):
+        """Table build for the table modes (a no-op in PQ_DIRECT)."""
+        self.set_queries(queries)
+        if self.lut is None:
+            return
         s = stream_handle(stream)
         dt = A.DTYPE_U8 if queries.dtype == torch.uint8 else A.DTYPE_F32
         A.check(self.L.gofann_pq_build_lut(A.ptr(queries), dt, queries.shape[0], queries.shape[1],

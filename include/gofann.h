@@ -68,6 +68,10 @@ typedef enum gofann_status {
 enum { GOFANN_EARLY_STOP_FIXED = 0, GOFANN_EARLY_STOP_OFF = 1, GOFANN_EARLY_STOP_ADAPTIVE = 2 };
 enum { GOFANN_SCORER_PQ = 0, GOFANN_SCORER_RABITQ = 1 };
 enum { GOFANN_DTYPE_U8 = 0, GOFANN_DTYPE_F32 = 1, GOFANN_DTYPE_F16 = 2 };
+/* PQ scoring inside the traversal: read a prebuilt LUT from global memory,
+ * stage it in shared memory per route, or evaluate each table entry from the
+ * query and the codebook where it is used (no per-query table at all). */
+enum { GOFANN_PQ_LUT_GLOBAL = 0, GOFANN_PQ_LUT_SHARED = 1, GOFANN_PQ_DIRECT = 2 };
 
 /* DNF clause over label handles and range atoms (gpu_predicate_index.cuh:24-25). */
 typedef struct gofann_clause {
@@ -118,9 +122,12 @@ typedef struct gofann_codes {
     uint32_t num_anchors;
 } gofann_codes;
 
-/* Per-query prepared state.  PQ: lut [n_rows][pq_dim][256].  RaBitQ: int8
- * query [n_rows][padded_dim], scale [n_rows], k1xsumq [n_rows], centroid
- * distances [n_rows][num_anchors]. */
+/* Per-query prepared state.  PQ: either the lookup tables lut
+ * [n_rows][pq_dim][256], or the raw query rows pq_query [n_rows][dim] (u8 or
+ * f32, pq_query_dtype) with the codebook pq_centroids [256][dim] -- then every
+ * table entry is evaluated where it is used, with the same fma order, which
+ * gives the same bits.  RaBitQ: int8 query [n_rows][padded_dim], scale
+ * [n_rows], k1xsumq [n_rows], centroid distances [n_rows][num_anchors]. */
 typedef struct gofann_prepared {
     const float* pq_lut;
     const int8_t* rq_q8;
@@ -129,6 +136,10 @@ typedef struct gofann_prepared {
     const float* rq_centroid_dist;
     uint32_t n_rows;
     uint32_t reserved;
+    const void* pq_query;
+    const float* pq_centroids;
+    int32_t pq_query_dtype; /* GOFANN_DTYPE_U8 or GOFANN_DTYPE_F32 */
+    uint32_t dim;
 } gofann_prepared;
 
 /* Routed queries (GraphRuntime route tables + gpu_predicate::View).  Every
@@ -168,7 +179,7 @@ typedef struct gofann_search_params {
     float alpha;             /* predicate_bias_alpha */
     int32_t pending_base_stop;
     int32_t full_label_check;     /* 1 = resident residual label check on expansion */
-    int32_t lut_in_shared;        /* PQ: 1 = stage the LUT in shared memory */
+    int32_t pq_mode;              /* PQ scoring: GOFANN_PQ_LUT_GLOBAL, _LUT_SHARED or _DIRECT */
 } gofann_search_params;
 
 /* Per-route device counters written by gofann_beam_search (may be NULL):

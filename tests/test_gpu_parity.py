@@ -189,16 +189,28 @@ def run_gpu_beam(L, graph, attrs, codes, prep, routes, trace_width=0, **params):
 
 
 BEAM_VARIANTS = [
-    dict(queue_size=64, predicate_bias=1, early_stop_mode=A.EARLY_STOP_ADAPTIVE, result_width=100),
-    dict(queue_size=16, predicate_bias=0, early_stop_mode=A.EARLY_STOP_FIXED, finish_limit=20, result_width=50),
+    dict(queue_size=64, predicate_bias=1, early_stop_mode=A.EARLY_STOP_ADAPTIVE, result_width=100,
+         pq_mode=A.PQ_DIRECT),
+    dict(queue_size=16, predicate_bias=0, early_stop_mode=A.EARLY_STOP_FIXED, finish_limit=20, result_width=50,
+         pq_mode=A.PQ_LUT_GLOBAL),
     dict(queue_size=200, predicate_bias=1, early_stop_mode=A.EARLY_STOP_FIXED, finish_limit=100, result_width=512,
-         lut_in_shared=1),
+         pq_mode=A.PQ_LUT_SHARED),
     dict(queue_size=512, predicate_bias=0, early_stop_mode=A.EARLY_STOP_OFF, max_steps=300, result_width=100,
-         lut_in_shared=1),
-    dict(queue_size=2, predicate_bias=1, early_stop_mode=A.EARLY_STOP_ADAPTIVE, stop_width=1, result_width=1),
+         pq_mode=A.PQ_DIRECT),
+    dict(queue_size=2, predicate_bias=1, early_stop_mode=A.EARLY_STOP_ADAPTIVE, stop_width=1, result_width=1,
+         pq_mode=A.PQ_DIRECT),
     dict(queue_size=96, predicate_bias=1, early_stop_mode=A.EARLY_STOP_ADAPTIVE, pending_base_stop=1,
-         full_label_check=1, alpha=0.3),
+         full_label_check=1, alpha=0.3, pq_mode=A.PQ_LUT_GLOBAL),
+    dict(queue_size=384, predicate_bias=1, early_stop_mode=A.EARLY_STOP_ADAPTIVE, result_width=100,
+         pq_mode=A.PQ_LUT_GLOBAL),
 ]
+
+
+def pq_prep(w, idx, mode):
+    """Device prepared state for a PQ mode: the LUT batch, or query rows + codebook."""
+    if mode == A.PQ_DIRECT:
+        return {"pq_query": dev(w.queries), "pq_centroids": dev(idx.pq_centroids)}
+    return {"pq_lut": dev(O.pq_build_lut(w.queries.astype(np.float32), idx.pq_centroids, idx.pq_codes.shape[1]))}
 
 
 @pytest.mark.parametrize("wl", ["cfg1", "cfg2"])
@@ -208,9 +220,10 @@ def test_beam_search_pq_bitexact(L, wl, vi):
     params = dict(BEAM_VARIANTS[vi], scorer=A.SCORER_PQ)
     lut = O.pq_build_lut(w.queries.astype(np.float32), idx.pq_centroids, idx.pq_codes.shape[1])
     want = O.beam_search(idx.graph(), idx.attrs(), idx.codes(), {"pq_lut": lut}, plan.graph_routes, threads=8,
-                         **params)
-    got = run_gpu_beam(L, idx.graph(), idx.attrs(), idx.codes(), {"pq_lut": dev(lut)}, plan.graph_routes, **params)
-    for name, g, o in zip(("ids", "dists", "steps", "counters"), got, want):
+                         trace_width=64, **params)
+    got = run_gpu_beam(L, idx.graph(), idx.attrs(), idx.codes(), pq_prep(w, idx, params["pq_mode"]),
+                       plan.graph_routes, trace_width=64, **params)
+    for name, g, o in zip(("ids", "dists", "steps", "counters", "trace"), got, want):
         if name == "dists":
             g, o = fbits(g), fbits(o)
         assert np.array_equal(g, o), f"{name} differ in {np.count_nonzero(np.any(np.atleast_2d(g != o), axis=-1))} routes"
@@ -220,7 +233,7 @@ def test_beam_search_pq_bitexact(L, wl, vi):
 def test_beam_search_rabitq_bitexact(L, vi):
     w, idx, plan, rq, anchors, qr = rabitq_artifacts()
     dprep, hprep = _rq_prepared(L, qr, anchors)
-    params = dict(BEAM_VARIANTS[vi], scorer=A.SCORER_RABITQ, lut_in_shared=0)
+    params = dict(BEAM_VARIANTS[vi], scorer=A.SCORER_RABITQ, pq_mode=A.PQ_LUT_GLOBAL)
     want = O.beam_search(idx.graph(), idx.attrs(), rq, hprep, plan.graph_routes, threads=8, **params)
     got = run_gpu_beam(L, idx.graph(), idx.attrs(), rq, dprep, plan.graph_routes, **params)
     for name, g, o in zip(("ids", "dists", "steps", "counters"), got, want):
@@ -269,8 +282,8 @@ def run_gpu_posting(L, codes, prep, attrs, routes, scorer, pids, begin, count, k
     return host(ids, np.uint32), d.cpu().numpy()
 
 
-@pytest.mark.parametrize("k", [1, 10, 100, 400])
-def test_posting_scan_pq_bitexact(L, k):
+@pytest.mark.parametrize("k,fused", [(1, False), (10, True), (100, False), (100, True), (400, True)])
+def test_posting_scan_pq_bitexact(L, k, fused):
     from gofann.planner import concat_routes, subset_routes
     w, idx, plan = cfg2_small()
     lut = O.pq_build_lut(w.queries.astype(np.float32), idx.pq_centroids, idx.pq_codes.shape[1])
@@ -283,8 +296,8 @@ def test_posting_scan_pq_bitexact(L, k):
     count = np.concatenate([plan.posting_count, idx.posting_count[big], [0]]).astype(np.uint32)
     want = O.posting_scan(idx.codes(), {"pq_lut": lut}, idx.attrs(), routes, A.SCORER_PQ, idx.posting_ids, begin,
                           count, k)
-    got = run_gpu_posting(L, idx.codes(), {"pq_lut": dev(lut)}, idx.attrs(), routes, A.SCORER_PQ, idx.posting_ids,
-                          begin, count, k)
+    prep = pq_prep(w, idx, A.PQ_DIRECT if fused else A.PQ_LUT_GLOBAL)  # fused: table built in the scan
+    got = run_gpu_posting(L, idx.codes(), prep, idx.attrs(), routes, A.SCORER_PQ, idx.posting_ids, begin, count, k)
     assert np.array_equal(got[0], want[0])
     assert np.array_equal(fbits(got[1]), fbits(want[1]))
 

@@ -56,7 +56,8 @@ def test_noalloc_matches_allocating_entry_point(tile):
     dg, da, dc, dr = dev_dict(idx.graph()), dev_dict(idx.attrs()), dev_dict(idx.codes()), dev_dict(routes)
     prep = {"pq_lut": lut}
     gs, at, cs, ps, rs = A.fill_graph(dg), A.fill_attrs(da), A.fill_codes(dc), A.fill_prepared(prep), A.fill_routes(dr)
-    sp = A.fill_params(queue_size=64, predicate_bias=1, early_stop_mode=A.EARLY_STOP_ADAPTIVE, result_width=100)
+    sp = A.fill_params(queue_size=64, predicate_bias=1, early_stop_mode=A.EARLY_STOP_ADAPTIVE, result_width=100,
+                       pq_mode=A.PQ_LUT_GLOBAL)
     n = rs.n_routes
     stream = torch.cuda.current_stream().cuda_stream
 
