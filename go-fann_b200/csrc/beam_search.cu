@@ -47,6 +47,11 @@ struct WarpState {
     uint32_t n_dist, n_probe, n_admit;
     uint32_t rej[2];
     uint32_t pass[2];
+    uint32_t adm[2];     // candidates admitted to the frontier this step
+    int hash_count;      // values in the visited table
+    int serial_hash;     // 1: this step's insertions could fill the table
+    uint32_t pf_row[2];  // local rows whose adjacency sits in the two prefetch slots
+    int pf_last;         // slot of the most recently issued prefetch (-1: none)
 };
 
 struct BeamArgs {
@@ -64,7 +69,7 @@ struct BeamArgs {
 };
 
 struct SmemLayout {
-    uint32_t frontier, topk, stop, list, sample, dist, prio, state, table, total;
+    uint32_t frontier, topk, stop, list, sample, dist, prio, state, nadj, table, total;
 };
 
 __host__ __device__ inline uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
@@ -82,6 +87,7 @@ __host__ __device__ inline SmemLayout smem_layout(const gofann_search_params& p,
     s.dist = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
     s.prio = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
     s.state = o; o = align16(o + sizeof(WarpState));
+    s.nadj = o; o = align16(o + 2 * GOFANN_MAX_DEGREE * 4);
     s.table = o;
     if (p.scorer == GOFANN_SCORER_PQ) {
         if (pq_mode == GOFANN_PQ_LUT_SHARED) o = align16(o + c.pq_dim * GOFANN_PQ_CENTROIDS * 4);
@@ -142,6 +148,43 @@ __device__ void gofann_debug_pickup(const FPair* f, int size, int bi)
 // for every finite or infinite distance and NaN-safe.  (The reference's
 // tie clause `!(b < a) && !(a < b) && ia < ib` inside a shfl_down tree was
 // observed to keep the larger index on sm_100a with nvcc 12.9 -O3.)
+// Asynchronous copy of the adjacency row at `src` into a prefetch slot.  The
+// node expanded next is fixed one step ahead (the reference picks `next`
+// before processing `now`, backend_pq.cu:4257-4278), so its row is in flight
+// while the current step scores and admits candidates.
+__device__ __forceinline__ void prefetch_row(uint32_t* dst, const uint32_t* src, uint32_t deg, int lane)
+{
+    const bool vec = (deg & 3u) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+    const uint32_t n = vec ? deg / 4 : deg;
+    for (uint32_t i = lane; i < n; i += kWarp) {
+        const uint32_t sa = static_cast<uint32_t>(__cvta_generic_to_shared(dst + (vec ? 4 * i : i)));
+        if (vec)
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(src + 4 * i));
+        else
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(sa), "l"(src + i));
+    }
+    asm volatile("cp.async.commit_group;\n" ::);
+}
+__device__ __forceinline__ void prefetch_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+__device__ __forceinline__ void prefetch_wait_older() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
+
+// Issues the prefetch of `row` into the slot not holding the row expanded
+// now (double buffering across steps).
+__device__ __forceinline__ void prefetch_next(WarpState& st, uint32_t* nadj, const uint32_t* adjacency,
+                                              uint32_t label_offset, uint32_t degree, uint32_t deg, uint32_t row,
+                                              int lane)
+{
+    const int slot = st.pf_last < 0 ? 0 : (st.pf_last ^ 1);
+    prefetch_row(nadj + slot * GOFANN_MAX_DEGREE, adjacency + static_cast<size_t>(label_offset + row) * degree, deg,
+                 lane);
+    __syncwarp();
+    if (lane == 0) {
+        st.pf_row[slot] = row;
+        st.pf_last = slot;
+    }
+    __syncwarp();
+}
+
 __device__ __forceinline__ uint32_t ordered_bits(float f)
 {
     if (f == 0.0f) f = 0.0f;
@@ -217,6 +260,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
     float* prio = reinterpret_cast<float*>(base + L.prio);
     WarpState& st = *reinterpret_cast<WarpState*>(base + L.state);
     float* table = reinterpret_cast<float*>(base + L.table);
+    uint32_t* nadj = reinterpret_cast<uint32_t*>(base + L.nadj);
     const uint32_t gwarp = blockIdx.x * (blockDim.x >> 5) + warp;
     uint32_t* hash = a.hash + static_cast<size_t>(gwarp) * kHashCap;
     const int QS = p.queue_size, SW = p.stop_width, RW = p.result_width;
@@ -305,6 +349,9 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
             if (kBias && pred_on && pred_matches(a.routes, a.attrs, route, begin_sample)) kp.second |= kPassBit;
             smmh_insert(frontier, st.heap_size, kp);
             hash_add(hash, begin_id);
+            st.hash_count = 1;
+            st.pf_row[0] = st.pf_row[1] = kU32Max;
+            st.pf_last = -1;
         }
         __syncwarp();
         coop_pickup(frontier, st.heap_size, &st.now, lane);
@@ -335,6 +382,9 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
                     }
                 }
                 __syncwarp();
+                if (found)
+                    prefetch_next(st, nadj, a.graph.adjacency, label_offset, a.graph.degree, deg,
+                                  st.next.second & kRowMask, lane);
             }
             if (st.exhausted) break;
             const uint32_t now_row = st.now.second & kRowMask;
@@ -344,7 +394,9 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
                 // filter verdict of the expanded node (backend_pq.cu:4394-4440)
                 const bool bit_match = a.graph.row_filter_mask ? (a.graph.row_filter_mask[grow] & qbit) != 0ull
                                                                : qbit != 0ull;
-                const uint32_t sample = a.graph.row_to_sample[grow];
+                const bool need_sample = a.routes.range_modes != nullptr || p.full_label_check != 0 ||
+                                         (pred_on && !kBias);
+                const uint32_t sample = need_sample ? a.graph.row_to_sample[grow] : 0u;
                 uint32_t active = 0, matched = 0;
                 if (a.routes.range_modes) {
                     for (uint32_t i = 0; i < a.routes.range_count; ++i) {
@@ -427,13 +479,21 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
             if (st.brk) break;
 
             // neighbour list: parallel read + visited test, in-order compaction
-            const uint32_t* adj = a.graph.adjacency + static_cast<size_t>(grow) * a.graph.degree;
+            const int pslot = st.pf_row[0] == now_row ? 0 : (st.pf_row[1] == now_row ? 1 : -1);
+            if (pslot >= 0) {
+                if (pslot == st.pf_last) prefetch_wait_all();
+                else prefetch_wait_older();  // the newer group (the next row) may stay in flight
+            }
+            __syncwarp();
+            const bool prefetched = pslot >= 0;
+            const uint32_t* adj = prefetched ? nadj + pslot * GOFANN_MAX_DEGREE
+                                             : a.graph.adjacency + static_cast<size_t>(grow) * a.graph.degree;
             int len = 0;
 #pragma unroll
             for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
                 const uint32_t i = half * kWarp + lane;
                 uint32_t idx = kU32Max;
-                if (i < deg) idx = __ldg(adj + i);
+                if (i < deg) idx = prefetched ? adj[i] : __ldg(adj + i);
                 const bool keep = idx != kU32Max && !hash_test(hash, idx);
                 const unsigned m = __ballot_sync(kFull, keep);
                 if (keep) list[len + __popc(m & ((1u << lane) - 1u))] = idx;
@@ -477,9 +537,14 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
                 }
             }
             __syncwarp();
+            // serial frontier admissions (order dependent): lane 0 runs the
+            // min-max heap; the visited-table insertions of the admitted rows
+            // follow, concurrently when the table cannot fill this step
             if (lane == 0) {
                 st.n_dist += static_cast<uint32_t>(len);
                 if (kBias && pred_on) st.n_probe += static_cast<uint32_t>(len);
+                uint32_t adm[2] = {0u, 0u};
+                int n_adm = 0;
                 for (int i = 0; i < len; ++i) {
                     if ((st.rej[i >> 5] >> (i & 31)) & 1u) continue;
                     FPair kp;
@@ -488,10 +553,30 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
                     kp.second = list[i] | (((st.pass[i >> 5] >> (i & 31)) & 1u) ? kPassBit : 0u);
                     if (st.heap_size >= QS + 1 && frontier[2].first < kp.first) continue;
                     smmh_insert(frontier, st.heap_size, kp);
-                    hash_add(hash, list[i]);
+                    adm[i >> 5] |= 1u << (i & 31);
+                    ++n_adm;
                     ++st.n_admit;
                     if (st.heap_size >= QS + 2) smmh_pop_max(frontier, st.heap_size);
                 }
+                st.adm[0] = adm[0];
+                st.adm[1] = adm[1];
+                // admitted rows are distinct and absent from the table (they
+                // passed the visited test this step); the reference inserts
+                // them right after each admission, nothing reads the table
+                // before the next step, so deferring the inserts is exact
+                st.serial_hash = st.hash_count + n_adm > kHashCap ? 1 : 0;
+                if (st.serial_hash) {
+                    for (int i = 0; i < len; ++i)
+                        if ((adm[i >> 5] >> (i & 31)) & 1u) st.hash_count += hash_add(hash, list[i]) ? 1 : 0;
+                } else {
+                    st.hash_count += n_adm;
+                }
+            }
+            __syncwarp();
+            if (!st.serial_hash) {
+#pragma unroll
+                for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half)
+                    if ((st.adm[half] >> lane) & 1u) hash_add_concurrent(hash, list[half * kWarp + lane]);
             }
             __syncwarp();
             if (step == 1) {
@@ -502,10 +587,16 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
                     nx.first = FLT_MAX; nx.second = kU32Max; nx.base = FLT_MAX;
                     st.next = nx;
                 }
+                if (found)
+                    prefetch_next(st, nadj, a.graph.adjacency, label_offset, a.graph.degree, deg,
+                                  st.next.second & kRowMask, lane);
             }
             if (lane == 0) st.now = st.next;
             __syncwarp();
         }
+
+        prefetch_wait_all();  // no copy of this route may land in the next route's slots
+        __syncwarp();
 
         // emit the shortlist ascending (in-place heap sort of the result heap)
         if (lane == 0) {

@@ -72,13 +72,29 @@ __device__ __forceinline__ bool hash_test(const uint32_t* t, uint32_t v)
     }
     return false;
 }
-__device__ __forceinline__ void hash_add(uint32_t* t, uint32_t v)
+// Returns true when v was inserted (false: already present, or table full).
+__device__ __forceinline__ bool hash_add(uint32_t* t, uint32_t v)
 {
     uint32_t s = hash_code(v);
     for (int p = 0; p < kHashCap; ++p) {
         const uint32_t x = t[s];
-        if (x == v) return;
-        if (x == kU32Max) { t[s] = v; return; }
+        if (x == v) return false;
+        if (x == kU32Max) { t[s] = v; return true; }
+        s = (s + 1) & (kHashCap - 1);
+    }
+    return false;
+}
+// Concurrent insertion of distinct absent values by several lanes.  The slot
+// a value lands in can differ from the one-at-a-time order, but membership --
+// the only thing hash_test reads -- is the same as long as the table cannot
+// fill (with linear probing over all slots an insertion fails only when every
+// slot is taken), which the caller guarantees.
+__device__ __forceinline__ void hash_add_concurrent(uint32_t* t, uint32_t v)
+{
+    uint32_t s = hash_code(v);
+    for (int p = 0; p < kHashCap; ++p) {
+        const uint32_t x = atomicCAS(t + s, kU32Max, v);
+        if (x == kU32Max || x == v) return;
         s = (s + 1) & (kHashCap - 1);
     }
 }

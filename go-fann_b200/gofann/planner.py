@@ -45,28 +45,42 @@ class Plan:
         return qoff, order
 
 
+def _residual_clauses(lab, primary):
+    """One DNF clause per route with the query labels other than the route's
+    own label, which every row of the route carries (its graph group or its
+    posting list): the compiled residual of the conjunction."""
+    res = [np.asarray([x for x in l if x != p], np.uint32) for l, p in zip(lab, primary)]
+    n = len(res)
+    rptr = np.zeros(n + 1, np.uint64)
+    rptr[1:] = np.cumsum([len(x) for x in res], dtype=np.uint64)
+    handles = np.concatenate(res).astype(np.uint32) if n else np.zeros(0, np.uint32)
+    if handles.size == 0:  # keep a valid (unreferenced) array: empty arrays map to NULL
+        handles = np.zeros(1, np.uint32)
+    clauses = np.zeros(n, A.CLAUSE_DTYPE)
+    clauses["label_begin"] = rptr[:-1].astype(np.uint32)
+    clauses["label_end"] = rptr[1:].astype(np.uint32)
+    enabled = np.array([len(x) > 0 for x in res], np.uint8)
+    return clauses, handles, enabled
+
+
 def _route_tables(qidx, labels_of, primary, group, start):
     n = len(qidx)
     indptr = np.zeros(n + 1, np.uint64)
     lab = [labels_of[q] for q in qidx]
     indptr[1:] = np.cumsum([len(x) for x in lab], dtype=np.uint64)
     indices = np.concatenate(lab).astype(np.uint32) if n else np.zeros(0, np.uint32)
-    # one clause per route holding all query labels; enabled for residuals
-    clauses = np.zeros(n, A.CLAUSE_DTYPE)
-    clauses["label_begin"] = indptr[:-1].astype(np.uint32)
-    clauses["label_end"] = indptr[1:].astype(np.uint32)
-    pred_offsets = np.arange(n + 1, dtype=np.uint32)
-    enabled = np.array([len(x) > 1 for x in lab], np.uint8)
+    primary = np.asarray(primary, np.uint32)
+    clauses, handles, enabled = _residual_clauses(lab, primary)
     return {
         "query_row": np.asarray(qidx, np.uint32),
         "group_id": np.asarray(group, np.uint32),
         "start_local": np.asarray(start, np.uint32),
         "qlabel_indptr": indptr,
         "qlabel_indices": indices,
-        "primary_label": np.asarray(primary, np.uint32),
-        "pred_offsets": pred_offsets,
+        "primary_label": primary,
+        "pred_offsets": np.arange(n + 1, dtype=np.uint32),
         "clauses": clauses,
-        "pred_handles": indices.copy(),
+        "pred_handles": handles,
         "pred_enabled": enabled,
     }
 
@@ -104,11 +118,9 @@ def subset_routes(routes: dict, sel: np.ndarray) -> dict:
     indptr = np.zeros(n + 1, np.uint64)
     indptr[1:] = np.cumsum([len(x) for x in lab], dtype=np.uint64)
     indices = np.concatenate(lab).astype(np.uint32) if n else np.zeros(0, np.uint32)
-    clauses = np.zeros(n, A.CLAUSE_DTYPE)
-    clauses["label_begin"] = indptr[:-1].astype(np.uint32)
-    clauses["label_end"] = indptr[1:].astype(np.uint32)
+    clauses, handles, enabled = _residual_clauses(lab, out["primary_label"])
     out.update(qlabel_indptr=indptr, qlabel_indices=indices, pred_offsets=np.arange(n + 1, dtype=np.uint32),
-               clauses=clauses, pred_handles=indices.copy())
+               clauses=clauses, pred_handles=handles, pred_enabled=enabled)
     return out
 
 
@@ -123,9 +135,8 @@ def concat_routes(a: dict, b: dict) -> dict:
     ip = np.concatenate([both["qlabel_indptr"], sb["qlabel_indptr"][1:] + both["qlabel_indptr"][-1]])
     ind = np.concatenate([both["qlabel_indices"], sb["qlabel_indices"]]).astype(np.uint32)
     n = na + nb
-    clauses = np.zeros(n, A.CLAUSE_DTYPE)
-    clauses["label_begin"] = ip[:-1].astype(np.uint32)
-    clauses["label_end"] = ip[1:].astype(np.uint32)
+    lab = [ind[ip[i]:ip[i + 1]] for i in range(n)]
+    clauses, handles, enabled = _residual_clauses(lab, out["primary_label"])
     out.update(qlabel_indptr=ip.astype(np.uint64), qlabel_indices=ind, pred_offsets=np.arange(n + 1, dtype=np.uint32),
-               clauses=clauses, pred_handles=ind.copy())
+               clauses=clauses, pred_handles=handles, pred_enabled=enabled)
     return out

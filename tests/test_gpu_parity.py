@@ -450,7 +450,7 @@ def test_pipeline_matches_oracle_and_recall(L, wl):
     from gofann.planner import _route_tables
     labs = [np.asarray(x, np.uint32) for x in w.query_labels]
     gt_routes = _route_tables(list(range(len(labs))), labs, [x[0] for x in labs], [0] * len(labs), [0] * len(labs))
-    gt_routes["pred_enabled"][:] = 1
+    gt_routes["pred_enabled"][:] = 0  # filter = every query label (residual check + primary)
     ti, _ = O.filtered_topk(w.base, dt, w.queries, idx.attrs(), gt_routes, 10)
     rec = np.mean([len((set(gi[i].tolist()) & set(ti[i].tolist())) - {A.U32MAX}) /
                    max(1, len(set(ti[i].tolist()) - {A.U32MAX})) for i in range(gi.shape[0])])
