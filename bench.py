@@ -124,10 +124,10 @@ def profiled_traffic() -> dict | None:
 # ------------------------------------------------------------ workload
 def build_workload(args, rank, world, device, t0):
     import torch
-    from gofann import workload_gpu as W
+    from gofann import sharding as S, workload_gpu as W
     data = W.generate(device=device, seed=args.seed, n=args.n, n_queries=args.queries, t0=t0)
     n = args.n
-    lo, hi = rank * n // world, (rank + 1) * n // world
+    lo, hi = S.shard_range(n, rank, world)
     gt = None
     eval_idx = np.arange(min(args.eval, args.queries))
     if rank == 0:
@@ -135,28 +135,9 @@ def build_workload(args, rank, world, device, t0):
         W._log(f"ground truth for {len(eval_idx)} queries", t0)
     shard = data
     if world > 1:
-        shard = shard_data(data, lo, hi, device)
+        shard = S.shard_data(data, lo, hi, device)
     idx = W.build_index(shard, seed=args.seed, t0=t0)
     return data, idx, gt, eval_idx, lo
-
-
-def shard_data(data, lo, hi, device):
-    """Rows [lo, hi) of the base set with their labels and postings (local ids)."""
-    import torch
-    ip = data["label_indptr"]
-    a, b = int(ip[lo]), int(ip[hi])
-    indptr = ip[lo:hi + 1] - a
-    indices = data["label_indices"][a:b]
-    base = data["base"][lo:hi]
-    vocab = data["vocab"]
-    rows = torch.repeat_interleave(torch.arange(hi - lo, device=device, dtype=torch.int64), indptr[1:] - indptr[:-1])
-    key = torch.sort((indices.to(torch.int64) << 24) | rows).values
-    pid = (key & ((1 << 24) - 1)).to(torch.int32)
-    card = torch.bincount(indices, minlength=vocab).cpu().numpy().astype(np.int64)
-    begin = np.zeros(vocab, np.int64)
-    begin[1:] = np.cumsum(card)[:-1]
-    return dict(base=base, label_indptr=indptr, label_indices=indices, posting_ids=pid, card=card, begin=begin,
-                queries=data["queries"], vocab=vocab, dim=data["dim"], n=hi - lo)
 
 
 def beam_bytes(counters: np.ndarray, n_routes: int, degree: int, pq_dim: int, avg_labels: float,
@@ -177,6 +158,7 @@ def run_gofann(args):
     import torch.distributed as dist
     from gofann import _abi as A, planner, workload_gpu as W
     from gofann.engine import DeviceIndex, DevicePlan, Pipeline, SearchConfig, stream_handle
+    from gofann.sharding import ShardExchange
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -200,22 +182,13 @@ def run_gofann(args):
         cfg = SearchConfig(queue_size=qs, result_width=100, pq_mode=args.pq_mode)
         return Pipeline(dindex, dplan, cfg)
 
-    gath_ids = torch.empty((world, nq, k), dtype=torch.int32, device=device) if world > 1 else None
-    gath_d = torch.empty((world, nq, k), dtype=torch.float32, device=device) if world > 1 else None
-    fin_ids = torch.empty((nq, k), dtype=torch.int32, device=device)
-    fin_d = torch.empty((nq, k), dtype=torch.float32, device=device)
+    xchg = ShardExchange(world, nq, k, device) if world > 1 else None
 
     def step(pipe, queries):
         ids, d = pipe.run(queries)
         if world == 1:
             return ids, d
-        s = stream_handle()
-        A.check(L.gofann_offset_ids(A.ptr(ids), ids.numel(), shard_base, s), "offset_ids")
-        dist.all_gather_into_tensor(gath_ids.view(-1), ids.reshape(-1))
-        dist.all_gather_into_tensor(gath_d.view(-1), d.reshape(-1))
-        A.check(L.gofann_shard_merge(A.ptr(gath_ids), A.ptr(gath_d), world, nq, k, A.ptr(fin_ids), A.ptr(fin_d), s),
-                "shard_merge")
-        return fin_ids, fin_d
+        return xchg.exchange(ids, d, shard_base, stream_handle())
 
     # queue-size sweep on the eval sample (every rank runs the same steps)
     sweep = [args.queue_size] if args.queue_size else QUEUE_SWEEP
@@ -266,12 +239,7 @@ def run_gofann(args):
         pipe.rerank(q.vectors)
         pipe.merge()
         if world > 1:
-            s = stream_handle()
-            A.check(L.gofann_offset_ids(A.ptr(pipe.out_ids), pipe.out_ids.numel(), shard_base, s), "offset_ids")
-            dist.all_gather_into_tensor(gath_ids.view(-1), pipe.out_ids.reshape(-1))
-            dist.all_gather_into_tensor(gath_d.view(-1), pipe.out_d.reshape(-1))
-            A.check(L.gofann_shard_merge(A.ptr(gath_ids), A.ptr(gath_d), world, nq, k, A.ptr(fin_ids),
-                                         A.ptr(fin_d), s), "shard_merge")
+            xchg.exchange(pipe.out_ids, pipe.out_d, shard_base, stream_handle())
     end.record(stream)
     torch.cuda.synchronize()
     if world > 1:

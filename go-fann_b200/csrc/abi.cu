@@ -43,6 +43,15 @@ int sm_count()
     return n;
 }
 
+size_t l2_bytes()
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrL2CacheSize, dev) != cudaSuccess) return 0;
+    return static_cast<size_t>(n);
+}
+
 }  // namespace gofann
 
 extern "C" {

@@ -152,16 +152,19 @@ __device__ void gofann_debug_pickup(const FPair* f, int size, int bi)
 // node expanded next is fixed one step ahead (the reference picks `next`
 // before processing `now`, backend_pq.cu:4257-4278), so its row is in flight
 // while the current step scores and admits candidates.
-__device__ __forceinline__ void prefetch_row(uint32_t* dst, const uint32_t* src, uint32_t deg, int lane)
+__device__ __forceinline__ void prefetch_row(uint32_t* dst, const uint32_t* src, uint32_t deg, int lane,
+                                             uint64_t pol)
 {
     const bool vec = (deg & 3u) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
     const uint32_t n = vec ? deg / 4 : deg;
     for (uint32_t i = lane; i < n; i += kWarp) {
         const uint32_t sa = static_cast<uint32_t>(__cvta_generic_to_shared(dst + (vec ? 4 * i : i)));
         if (vec)
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(src + 4 * i));
+            asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 16, %2;\n" ::"r"(sa),
+                         "l"(src + 4 * i), "l"(pol));
         else
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(sa), "l"(src + i));
+            asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 4, %2;\n" ::"r"(sa), "l"(src + i),
+                         "l"(pol));
     }
     asm volatile("cp.async.commit_group;\n" ::);
 }
@@ -172,11 +175,11 @@ __device__ __forceinline__ void prefetch_wait_older() { asm volatile("cp.async.w
 // now (double buffering across steps).
 __device__ __forceinline__ void prefetch_next(WarpState& st, uint32_t* nadj, const uint32_t* adjacency,
                                               uint32_t label_offset, uint32_t degree, uint32_t deg, uint32_t row,
-                                              int lane)
+                                              int lane, uint64_t pol)
 {
     const int slot = st.pf_last < 0 ? 0 : (st.pf_last ^ 1);
     prefetch_row(nadj + slot * GOFANN_MAX_DEGREE, adjacency + static_cast<size_t>(label_offset + row) * degree, deg,
-                 lane);
+                 lane, pol);
     __syncwarp();
     if (lane == 0) {
         st.pf_row[slot] = row;
@@ -228,14 +231,21 @@ struct Scorer {
     const float* cent;     // PQ_DIRECT codebook
     int dim;
     RqQueryView rq;        // RaBitQ
+    uint64_t keep, stream; // L2 policies: per-route tables / streaming rows
     __device__ __forceinline__ float operator()(const gofann_codes& c, uint32_t sample) const
     {
         if constexpr (kScorer == GOFANN_SCORER_PQ) {
             const uint8_t* code = c.pq_codes + static_cast<size_t>(sample) * c.pq_dim;
-            if constexpr (kMode == GOFANN_PQ_DIRECT)
-                return pq_adc_direct<kW, kMaxM>(lut_row, cent, dim, code, static_cast<int>(c.pq_dim));
-            else
-                return pq_adc_warp_order(lut_row, code, static_cast<int>(c.pq_dim));
+            if constexpr (kMode == GOFANN_PQ_DIRECT) {
+                return pq_adc_direct<kW, kMaxM>(lut_row, cent, dim, code, static_cast<int>(c.pq_dim), keep, stream);
+            } else {
+                uint32_t cw[kMaxPqDim / 4];
+                load_code_words(code, static_cast<int>(c.pq_dim), cw, stream);
+                if constexpr (kMode == GOFANN_PQ_LUT_GLOBAL)
+                    return pq_adc_words_global(lut_row, cw, static_cast<int>(c.pq_dim), keep);
+                else
+                    return pq_adc_words(lut_row, cw, static_cast<int>(c.pq_dim));
+            }
         } else {
             return rq_estimate(c, rq, sample);
         }
@@ -265,6 +275,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
     uint32_t* hash = a.hash + static_cast<size_t>(gwarp) * kHashCap;
     const int QS = p.queue_size, SW = p.stop_width, RW = p.result_width;
     const uint32_t deg = a.graph.degree < GOFANN_MAX_DEGREE ? a.graph.degree : GOFANN_MAX_DEGREE;
+    const uint64_t keep = l2_keep_policy(), stream = l2_stream_policy();
 
     for (;;) {
         uint32_t route = 0;
@@ -285,6 +296,8 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
             for (int i = lane; i < kHashCap / 4; i += kWarp) h4[i] = e;
         }
         Scorer<kScorer, kMode, kW, kMaxM> score;
+        score.keep = keep;
+        score.stream = stream;
         if constexpr (kScorer == GOFANN_SCORER_PQ) {
             if constexpr (kMode == GOFANN_PQ_DIRECT) {
                 const int dim = static_cast<int>(a.prep.dim);
@@ -384,7 +397,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
                 __syncwarp();
                 if (found)
                     prefetch_next(st, nadj, a.graph.adjacency, label_offset, a.graph.degree, deg,
-                                  st.next.second & kRowMask, lane);
+                                  st.next.second & kRowMask, lane, stream);
             }
             if (st.exhausted) break;
             const uint32_t now_row = st.now.second & kRowMask;
@@ -493,7 +506,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
             for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
                 const uint32_t i = half * kWarp + lane;
                 uint32_t idx = kU32Max;
-                if (i < deg) idx = prefetched ? adj[i] : __ldg(adj + i);
+                if (i < deg) idx = prefetched ? adj[i] : ldg_u32(adj + i, stream);
                 const bool keep = idx != kU32Max && !hash_test(hash, idx);
                 const unsigned m = __ballot_sync(kFull, keep);
                 if (keep) list[len + __popc(m & ((1u << lane) - 1u))] = idx;
@@ -509,7 +522,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
 
             // score every listed candidate, one candidate per lane
             for (int i = lane; i < len; i += kWarp) {
-                const uint32_t s = __ldg(a.graph.row_to_sample + label_offset + list[i]);
+                const uint32_t s = ldg_u32(a.graph.row_to_sample + label_offset + list[i], stream);
                 slist[i] = s;
                 dist[i] = score(a.codes, s);
             }
@@ -589,7 +602,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
                 }
                 if (found)
                     prefetch_next(st, nadj, a.graph.adjacency, label_offset, a.graph.degree, deg,
-                                  st.next.second & kRowMask, lane);
+                                  st.next.second & kRowMask, lane, stream);
             }
             if (lane == 0) st.now = st.next;
             __syncwarp();
@@ -694,6 +707,31 @@ uint32_t grid_blocks(uint32_t n_routes, int warps_per_block, int per_sm)
     return need < cap ? need : cap;
 }
 
+// Share of L2 that the automatic grid size lets the running routes' tables
+// (lookup row + visited table per warp) occupy when the lookup tables are
+// read from global memory; 0 disables the automatic cap.
+constexpr double kAutoL2Share = 0.0;
+
+// Routes in flight: an explicit resident_warps caps the grid; with 0, in
+// GOFANN_PQ_LUT_GLOBAL mode the grid is cut to the warps whose tables fit in
+// kAutoL2Share of L2 (never below one block per SM).
+uint32_t cap_blocks(uint32_t blocks, const gofann_search_params& p, int wpb, int pq_mode, uint32_t pq_dim)
+{
+    uint64_t cap_warps = 0;
+    if (p.resident_warps > 0) {
+        cap_warps = static_cast<uint64_t>(p.resident_warps);
+    } else if (p.scorer == GOFANN_SCORER_PQ && pq_mode == GOFANN_PQ_LUT_GLOBAL && kAutoL2Share > 0.0) {
+        const uint64_t per_warp = static_cast<uint64_t>(pq_dim) * GOFANN_PQ_CENTROIDS * 4 + kHashCap * 4;
+        cap_warps = static_cast<uint64_t>(kAutoL2Share * static_cast<double>(l2_bytes())) / per_warp;
+        const uint64_t floor_warps = static_cast<uint64_t>(sm_count() > 0 ? sm_count() : 1) * wpb;
+        if (cap_warps < floor_warps) cap_warps = floor_warps;
+    }
+    if (cap_warps == 0) return blocks;
+    uint64_t cap = cap_warps / static_cast<uint64_t>(wpb);
+    if (cap == 0) cap = 1;
+    return blocks < cap ? blocks : static_cast<uint32_t>(cap);
+}
+
 constexpr size_t kCounterBytes = 256;  // route counter, kept 256-byte aligned
 
 }  // namespace
@@ -732,6 +770,8 @@ int gofann_beam_search(const gofann_graph* graph, const gofann_attrs* attrs, con
                     GOFANN_MAX_RESULT_WIDTH);
     if (p.early_stop_mode < 0 || p.early_stop_mode > 2)
         return fail(GOFANN_ERR_INVALID, "beam_search: unknown early_stop_mode %d", p.early_stop_mode);
+    if (p.resident_warps < 0)
+        return fail(GOFANN_ERR_INVALID, "beam_search: resident_warps %d is negative", p.resident_warps);
     if (!graph->adjacency || !graph->row_to_sample || !graph->label_offset || graph->degree == 0)
         return fail(GOFANN_ERR_INVALID, "beam_search: graph arrays missing");
     if (!routes->query_row || !routes->group_id || !routes->start_local || !out->ids || !out->dists)
@@ -793,7 +833,7 @@ int gofann_beam_search(const gofann_graph* graph, const gofann_attrs* attrs, con
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, wpb * 32, smem);
     if (e != cudaSuccess) return cuda_status(e, "beam_search: occupancy query");
     if (per_sm <= 0) return fail(GOFANN_ERR_UNSUPPORTED, "beam_search: kernel does not fit on an SM");
-    const uint32_t blocks = grid_blocks(routes->n_routes, wpb, per_sm);
+    const uint32_t blocks = cap_blocks(grid_blocks(routes->n_routes, wpb, per_sm), p, wpb, pq_mode, codes->pq_dim);
     const size_t need = kCounterBytes + static_cast<size_t>(blocks) * wpb * kHashCap * sizeof(uint32_t);
     if (scratch_bytes < need)
         return fail(GOFANN_ERR_CAPACITY, "beam_search: scratch of %zu bytes, %zu needed", scratch_bytes, need);
@@ -893,6 +933,8 @@ int gofann_beam_search_noalloc(const gofann_graph* graph, const gofann_attrs* at
                     GOFANN_MAX_RESULT_WIDTH);
     if (p.early_stop_mode < 0 || p.early_stop_mode > 2)
         return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: unknown early_stop_mode %d", p.early_stop_mode);
+    if (p.resident_warps < 0)
+        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: resident_warps %d is negative", p.resident_warps);
     if (!graph->adjacency || !graph->row_to_sample || !graph->label_offset || graph->degree == 0)
         return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: graph arrays missing");
     if (!routes->query_row || !routes->group_id || !routes->start_local || !out->ids || !out->dists)
@@ -958,7 +1000,7 @@ int gofann_beam_search_noalloc(const gofann_graph* graph, const gofann_attrs* at
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, wpb * 32, smem);
     if (e != cudaSuccess) return cuda_status(e, "beam_search_noalloc: occupancy query");
     if (per_sm <= 0) return fail(GOFANN_ERR_UNSUPPORTED, "beam_search_noalloc: kernel does not fit on an SM");
-    uint32_t blocks = grid_blocks(routes->n_routes, wpb, per_sm);
+    uint32_t blocks = cap_blocks(grid_blocks(routes->n_routes, wpb, per_sm), p, wpb, pq_mode, codes->pq_dim);
     const uint32_t max_blocks = static_cast<uint32_t>(kNoAllocTables / wpb);
     if (blocks > max_blocks) blocks = max_blocks;
     const size_t need = kCounterBytes + static_cast<size_t>(blocks) * wpb * kHashCap * sizeof(uint32_t);

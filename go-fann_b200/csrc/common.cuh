@@ -23,6 +23,7 @@ int fail(int status, const char* fmt, ...);
 int cuda_status(cudaError_t err, const char* what);
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 int sm_count();
+size_t l2_bytes();  // L2 size of the current device (0 on error)
 
 #define GOFANN_CHECK_LAUNCH(what)                                      \
     do {                                                               \
@@ -35,6 +36,58 @@ constexpr uint32_t kPoolUsed = 0x80000000u;
 constexpr int kWarp = 32;
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kHashCap = GOFANN_HASH_CAPACITY;
+
+// ---------------------------------------------------- L2 residency classes
+// A traversal re-reads its route's tables (the 48 KB PQ lookup row at
+// config-2 shape) for every candidate of every step, but reads graph rows,
+// code rows and the row->sample map about once per route.  With thousands of
+// routes in flight the tables alone approach the L2 size, so plain LRU lets
+// the streaming reads evict them and the table gathers fall through to HBM as
+// 32-byte sectors.  Table loads therefore carry an L2 evict_last policy and
+// streaming loads an evict_first policy (PTX createpolicy + .L2::cache_hint).
+// Policies change only caching, never values.
+__device__ __forceinline__ uint64_t l2_keep_policy()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_stream_policy()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+// Read-only (non-coherent) global loads with a cache policy; the data must
+// not be written while the kernel runs.
+__device__ __forceinline__ float ldg_f32(const float* p, uint64_t pol)
+{
+    float v;
+    asm volatile("ld.global.nc.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(v) : "l"(p), "l"(pol));
+    return v;
+}
+__device__ __forceinline__ float4 ldg_f32x4(const float4* p, uint64_t pol)
+{
+    float4 v;
+    asm volatile("ld.global.nc.L2::cache_hint.v4.f32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p), "l"(pol));
+    return v;
+}
+__device__ __forceinline__ uint32_t ldg_u32(const uint32_t* p, uint64_t pol)
+{
+    uint32_t v;
+    asm volatile("ld.global.nc.L2::cache_hint.u32 %0, [%1], %2;" : "=r"(v) : "l"(p), "l"(pol));
+    return v;
+}
+__device__ __forceinline__ uint4 ldg_u32x4(const uint4* p, uint64_t pol)
+{
+    uint4 v;
+    asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p), "l"(pol));
+    return v;
+}
 
 // --------------------------------------------------- float order helpers
 // Lane-0 value of `v += __shfl_xor_sync(v, off)` for off = 16..1, replayed

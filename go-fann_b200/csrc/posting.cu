@@ -79,8 +79,9 @@ __global__ void __launch_bounds__(kScanThreads) posting_scan_kernel(
             __syncthreads();
             const int w = dim / static_cast<int>(codes.pq_dim);
             const float* crow = prep.pq_centroids + static_cast<size_t>(tid) * dim;  // kScanThreads == 256
+            const uint64_t keep = l2_keep_policy();  // the codebook is shared by every route
             for (int m = 0; m < static_cast<int>(codes.pq_dim); ++m)
-                table[m * GOFANN_PQ_CENTROIDS + tid] = pq_entry<0>(q + m * w, crow + m * w, w);
+                table[m * GOFANN_PQ_CENTROIDS + tid] = pq_entry<0>(q + m * w, crow + m * w, w, keep);
         }
     } else {
         rq_build_planes(prep.rq_q8 + static_cast<size_t>(row) * codes.padded_dim, static_cast<int>(codes.padded_dim),

@@ -37,6 +37,26 @@ __device__ __forceinline__ void load_code_words(const uint8_t* __restrict__ code
     }
 }
 
+// The same with an L2 policy on the row (code rows are streaming data).
+__device__ __forceinline__ void load_code_words(const uint8_t* __restrict__ code, int m_bytes,
+                                                uint32_t (&cw)[kMaxPqDim / 4], uint64_t pol)
+{
+    if ((m_bytes & 15) == 0 && (reinterpret_cast<uintptr_t>(code) & 15) == 0) {
+        const uint4* p = reinterpret_cast<const uint4*>(code);
+#pragma unroll
+        for (int i = 0; i < kMaxPqDim / 16; ++i) {
+            if (i < (m_bytes >> 4)) {
+                const uint4 x = ldg_u32x4(p + i, pol);
+                cw[4 * i + 0] = x.x; cw[4 * i + 1] = x.y; cw[4 * i + 2] = x.z; cw[4 * i + 3] = x.w;
+            } else {
+                cw[4 * i + 0] = cw[4 * i + 1] = cw[4 * i + 2] = cw[4 * i + 3] = 0;
+            }
+        }
+    } else {
+        load_code_words(code, m_bytes, cw);
+    }
+}
+
 __device__ __forceinline__ uint32_t code_byte(const uint32_t (&cw)[kMaxPqDim / 4], int m)
 {
     return (cw[m >> 2] >> ((m & 3) * 8)) & 0xffu;
@@ -57,6 +77,21 @@ __device__ __forceinline__ float pq_adc_words(const float* lut_row, const uint32
     return butterfly_sum32(v);
 }
 
+// pq_adc_words over a table row in global memory, table gathers under the
+// `keep` L2 policy.
+__device__ __forceinline__ float pq_adc_words_global(const float* __restrict__ lut_row,
+                                                     const uint32_t (&cw)[kMaxPqDim / 4], int pq_dim, uint64_t keep)
+{
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+#pragma unroll
+    for (int m = 0; m < kMaxPqDim; ++m)
+        if (m < pq_dim)
+            v[m & 31] = __fadd_rn(v[m & 31], ldg_f32(lut_row + m * GOFANN_PQ_CENTROIDS + code_byte(cw, m), keep));
+    return butterfly_sum32(v);
+}
+
 __device__ __forceinline__ float pq_adc_warp_order(const float* lut_row, const uint8_t* code, int pq_dim)
 {
     uint32_t cw[kMaxPqDim / 4];
@@ -68,11 +103,11 @@ __device__ __forceinline__ float pq_adc_warp_order(const float* lut_row, const u
 // q - c, sequential (computePQTable, backend_pq.cu:1999-2022).  `q` is the
 // query subvector (shared memory), `cr` the centroid subvector (global).
 template <int kW>
-__device__ __forceinline__ float pq_entry(const float* q, const float* __restrict__ cr, int w)
+__device__ __forceinline__ float pq_entry(const float* q, const float* __restrict__ cr, int w, uint64_t keep)
 {
     float acc = 0.0f;
     if constexpr (kW == 4) {
-        const float4 c = __ldg(reinterpret_cast<const float4*>(cr));
+        const float4 c = ldg_f32x4(reinterpret_cast<const float4*>(cr), keep);
         float d = __fsub_rn(q[0], c.x);
         acc = __fmaf_rn(d, d, acc);
         d = __fsub_rn(q[1], c.y);
@@ -83,7 +118,7 @@ __device__ __forceinline__ float pq_entry(const float* q, const float* __restric
         acc = __fmaf_rn(d, d, acc);
     } else {
         for (int d = 0; d < w; ++d) {
-            const float diff = __fsub_rn(q[d], __ldg(cr + d));
+            const float diff = __fsub_rn(q[d], ldg_f32(cr + d, keep));
             acc = __fmaf_rn(diff, diff, acc);
         }
     }
@@ -97,10 +132,10 @@ __device__ __forceinline__ float pq_entry(const float* q, const float* __restric
 // no 48 KB table per in-flight query.
 template <int kW, int kMaxM>
 __device__ __forceinline__ float pq_adc_direct(const float* q, const float* __restrict__ cent, int dim,
-                                               const uint8_t* code, int pq_dim)
+                                               const uint8_t* code, int pq_dim, uint64_t keep, uint64_t stream)
 {
     uint32_t cw[kMaxPqDim / 4];
-    load_code_words(code, pq_dim, cw);
+    load_code_words(code, pq_dim, cw, stream);
     const int w = dim / pq_dim;
     float v[32];
 #pragma unroll
@@ -109,7 +144,7 @@ __device__ __forceinline__ float pq_adc_direct(const float* q, const float* __re
     for (int m = 0; m < kMaxM; ++m) {
         if (m < pq_dim) {
             const uint32_t c = code_byte(cw, m);
-            const float e = pq_entry<kW>(q + m * w, cent + static_cast<size_t>(c) * dim + m * w, w);
+            const float e = pq_entry<kW>(q + m * w, cent + static_cast<size_t>(c) * dim + m * w, w, keep);
             v[m & 31] = __fadd_rn(v[m & 31], e);
         }
     }

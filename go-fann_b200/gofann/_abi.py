@@ -77,7 +77,7 @@ class SearchParams(C.Structure):
     _fields_ = [("queue_size", I32), ("stop_width", I32), ("result_width", I32), ("finish_limit", I32),
                 ("early_stop_mode", I32), ("max_steps", I32), ("scorer", I32), ("predicate_bias", I32),
                 ("alpha", C.c_float), ("pending_base_stop", I32), ("full_label_check", I32),
-                ("pq_mode", I32)]
+                ("pq_mode", I32), ("resident_warps", I32)]
 
 
 class SearchOut(C.Structure):
@@ -181,7 +181,8 @@ def fill_params(**kw) -> SearchParams:
     s = SearchParams()
     defaults = dict(queue_size=64, stop_width=10, result_width=100, finish_limit=100,
                     early_stop_mode=EARLY_STOP_ADAPTIVE, max_steps=0, scorer=SCORER_PQ, predicate_bias=0,
-                    alpha=0.15, pending_base_stop=0, full_label_check=0, pq_mode=PQ_LUT_GLOBAL)
+                    alpha=0.15, pending_base_stop=0, full_label_check=0, pq_mode=PQ_LUT_GLOBAL,
+                    resident_warps=0)
     defaults.update(kw)
     for k, v in defaults.items():
         setattr(s, k, v)

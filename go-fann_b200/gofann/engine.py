@@ -58,6 +58,7 @@ class SearchConfig:
     predicate_bias: int = 1
     alpha: float = 0.15
     pq_mode: int = A.PQ_LUT_GLOBAL
+    resident_warps: int = 0
     lowfreq_shortlist: int = 100
     topk: int = 10
 
@@ -65,7 +66,7 @@ class SearchConfig:
         return A.fill_params(queue_size=self.queue_size, stop_width=self.stop_width, result_width=self.result_width,
                              finish_limit=self.finish_limit, early_stop_mode=self.early_stop_mode,
                              max_steps=self.max_steps, scorer=scorer, predicate_bias=self.predicate_bias,
-                             alpha=self.alpha, pq_mode=self.pq_mode)
+                             alpha=self.alpha, pq_mode=self.pq_mode, resident_warps=self.resident_warps)
 
 
 class DeviceIndex:

@@ -180,6 +180,10 @@ typedef struct gofann_search_params {
     int32_t pending_base_stop;
     int32_t full_label_check;     /* 1 = resident residual label check on expansion */
     int32_t pq_mode;              /* PQ scoring: GOFANN_PQ_LUT_GLOBAL, _LUT_SHARED or _DIRECT */
+    int32_t resident_warps;       /* cap on concurrently running routes (warps) of the persistent
+                                     grid; 0 = automatic: as many as fit on the SMs, reduced in
+                                     GOFANN_PQ_LUT_GLOBAL mode so that the per-route tables in
+                                     flight stay L2-resident */
 } gofann_search_params;
 
 /* Per-route device counters written by gofann_beam_search (may be NULL):

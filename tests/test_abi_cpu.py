@@ -41,7 +41,7 @@ int main(void) {
   S(gofann_clause) S(gofann_range_atom) S(gofann_graph) S(gofann_attrs) S(gofann_codes)
   S(gofann_prepared) S(gofann_routes) S(gofann_search_params) S(gofann_search_out)
   O(gofann_codes, rq_codes) O(gofann_codes, padded_dim) O(gofann_routes, query_row)
-  O(gofann_routes, route_compiled) O(gofann_search_params, alpha) O(gofann_search_params, pq_mode) O(gofann_prepared, dim) O(gofann_prepared, pq_query)
+  O(gofann_routes, route_compiled) O(gofann_search_params, alpha) O(gofann_search_params, pq_mode) O(gofann_search_params, resident_warps) O(gofann_prepared, dim) O(gofann_prepared, pq_query)
   O(gofann_graph, total_rows) O(gofann_attrs, n_samples) O(gofann_prepared, n_rows)
   return 0; }
 '''
