@@ -52,6 +52,7 @@ struct WarpState {
     int serial_hash;     // 1: this step's insertions could fill the table
     uint32_t pf_row[2];  // local rows whose adjacency sits in the two prefetch slots
     int pf_last;         // slot of the most recently issued prefetch (-1: none)
+    float edge[2];       // sorted frontier: priorities merged into slots QS-1 and QS
 };
 
 struct BeamArgs {
@@ -69,7 +70,7 @@ struct BeamArgs {
 };
 
 struct SmemLayout {
-    uint32_t frontier, topk, stop, list, sample, dist, prio, state, nadj, table, total;
+    uint32_t frontier, topk, stop, list, sample, dist, prio, akey, state, nadj, table, total;
 };
 
 __host__ __device__ inline uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
@@ -79,6 +80,8 @@ __host__ __device__ inline SmemLayout smem_layout(const gofann_search_params& p,
 {
     SmemLayout s;
     uint32_t o = 0;
+    // frontier: the reference heap (queue_size + 3 FPair) or, in the same
+    // bytes, the sorted frontier's three arrays of queue_size + 2 words
     s.frontier = o; o = align16(o + (p.queue_size + 3) * sizeof(FPair));
     s.topk = o; o = align16(o + (p.result_width + 1) * sizeof(RPair));
     s.stop = o; o = align16(o + (GOFANN_MAX_TOPK + 2) * sizeof(SPair));
@@ -86,6 +89,7 @@ __host__ __device__ inline SmemLayout smem_layout(const gofann_search_params& p,
     s.sample = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
     s.dist = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
     s.prio = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
+    s.akey = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
     s.state = o; o = align16(o + sizeof(WarpState));
     s.nadj = o; o = align16(o + 2 * GOFANN_MAX_DEGREE * 4);
     s.table = o;
@@ -239,12 +243,12 @@ struct Scorer {
             if constexpr (kMode == GOFANN_PQ_DIRECT) {
                 return pq_adc_direct<kW, kMaxM>(lut_row, cent, dim, code, static_cast<int>(c.pq_dim), keep, stream);
             } else {
-                uint32_t cw[kMaxPqDim / 4];
-                load_code_words(code, static_cast<int>(c.pq_dim), cw, stream);
+                uint32_t cw[kMaxM / 4];
+                load_code_words<kMaxM>(code, static_cast<int>(c.pq_dim), cw, stream);
                 if constexpr (kMode == GOFANN_PQ_LUT_GLOBAL)
-                    return pq_adc_words_global(lut_row, cw, static_cast<int>(c.pq_dim), keep);
+                    return pq_adc_words_global<kMaxM>(lut_row, cw, static_cast<int>(c.pq_dim), keep);
                 else
-                    return pq_adc_words(lut_row, cw, static_cast<int>(c.pq_dim));
+                    return pq_adc_words<kMaxM>(lut_row, cw, static_cast<int>(c.pq_dim));
             }
         } else {
             return rq_estimate(c, rq, sample);
@@ -252,281 +256,509 @@ struct Scorer {
     }
 };
 
-template <int kScorer, bool kBias, int kMode, int kW, int kMaxM>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamArgs a)
+// ---------------------------------------------------------------------------
+// Sorted frontier (the fast path).
+//
+// With pairwise distinct priorities the reference's symmetric min-max heap
+// behaves as a set: after every admission it holds the queue_size smallest
+// entries admitted so far (insert, then pop_max once it holds queue_size+1);
+// pickup takes the smallest unused entry; a candidate is rejected exactly when
+// the heap is full and its priority is above the heap maximum.  Kept as an
+// ascending array, one step's admissions become a warp-parallel merge:
+// candidate i (list order) is admitted iff fewer than queue_size entries of
+// the frontier plus candidates before i have a smaller priority (a candidate
+// rejected earlier in the step is above the maximum at its turn, which only
+// decreases, so it is never smaller than a later admitted one), and the array
+// becomes the queue_size smallest of the frontier and the admitted
+// candidates.  Admission decisions compare priorities only, so they are the
+// same with ties; the heap's array layout decides only which of two equal
+// entries pickup returns or pop_max evicts.  The sorted array orders equal
+// priorities deterministically (frontier entries first, then candidates in
+// list order) and the fast path gives up on a route when such a choice is
+// actually made -- two unused entries tie for the smallest priority at a
+// pickup, or equal priorities straddle the queue_size boundary of a merge --
+// or when a priority is NaN; the route then runs again from the start with
+// the reference's heap (run_route<false>).
+struct SortedFrontier {
+    float* key;     // priority (`first`), ascending
+    uint32_t* val;  // local row | used bit | pass bit
+    float* base;    // unbiased score
+};
+
+// Smallest unused entry: 1 found, 0 none left, -1 another unused entry has
+// the same priority (the reference heap's layout would decide).
+__device__ __forceinline__ int sorted_pickup(const SortedFrontier& f, int n, FPair* out, int lane)
 {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
+    for (int c = 0; c < n; c += kWarp) {
+        const int k = c + lane;
+        const bool unused = k < n && !(f.val[k] & kPoolUsed);
+        const unsigned m = __ballot_sync(kFull, unused);
+        if (m) {
+            const int bi = c + __ffs(m) - 1;
+            const float key = f.key[bi];
+            // equal priorities sit right after bi in the sorted array
+            const int k2 = bi + 1 + lane;
+            const bool twin = k2 < n && f.key[k2] == key && !(f.val[k2] & kPoolUsed);
+            const bool run_on = lane == kWarp - 1 && k2 < n && f.key[k2] == key;  // run may go on: be safe
+            if (__any_sync(kFull, twin || run_on)) return -1;
+            if (lane == 0) {
+                out->first = key;
+                out->second = f.val[bi];
+                out->base = f.base[bi];
+                f.val[bi] |= kPoolUsed;
+            }
+            __syncwarp();
+            return 1;
+        }
+    }
+    return 0;
+}
+
+// Smallest priority (or unbiased score) over the unused entries.
+__device__ __forceinline__ float sorted_unused_min(const SortedFrontier& f, int n, bool use_base, int lane)
+{
+    float m = FLT_MAX;
+    for (int k = lane; k < n; k += kWarp)
+        if (!(f.val[k] & kPoolUsed)) m = fminf(m, use_base ? f.base[k] : f.key[k]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fminf(m, __shfl_xor_sync(kFull, m, off));
+    return m;
+}
+
+// Number of entries of the ascending array a[0..n) below x.
+__device__ __forceinline__ int count_below(const float* a, int n, float x)
+{
+    int lo = 0, hi = n;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (a[mid] < x) lo = mid + 1;
+        else hi = mid;
+    }
+    return lo;
+}
+
+// One step's admissions into the sorted frontier (see above).  Candidates
+// are list[0..len) with priorities prio[], unbiased scores dist[] and pass
+// bits pass[]; akey is 64 floats of scratch.  Writes the admitted mask to
+// adm[2] and the admitted count to n_adm.  Returns false when a NaN priority
+// or a tie across the queue_size boundary makes the result depend on the
+// reference heap's layout (the frontier is then left inconsistent: the
+// caller abandons the route).
+__device__ __forceinline__ bool sorted_admit(const SortedFrontier& f, WarpState& st, int QS, const uint32_t* list,
+                                             const float* prio, const float* dist, const uint32_t pass[2], int len,
+                                             float* akey, uint32_t adm[2], int& n_adm, int lane)
+{
+    const int n = st.heap_size - 1;
+    bool nan = false;
+    unsigned am[2];
+    int pos[2] = {0, 0};
+#pragma unroll
+    for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
+        const int i = half * kWarp + lane;
+        bool admitted = false;
+        if (i < len) {
+            const float key = prio[i];
+            if (!(key == key)) nan = true;
+            const int below = count_below(f.key, n, key);
+            int before = 0;
+            for (int j = 0; j < i; ++j) before += prio[j] < key ? 1 : 0;
+            admitted = below + before < QS;
+            // slot order among equal priorities: frontier entries first
+            int not_above = below;
+            while (not_above < n && f.key[not_above] == key) ++not_above;
+            pos[half] = not_above;
+        }
+        am[half] = __ballot_sync(kFull, admitted);
+    }
+    if (__any_sync(kFull, nan)) return false;
+    n_adm = __popc(am[0]) + __popc(am[1]);
+    adm[0] = am[0];
+    adm[1] = am[1];
+    if (n_adm == 0) return true;
+    if (lane == 0) {
+        st.edge[0] = -FLT_MAX;  // priority landing in slot QS - 1
+        st.edge[1] = FLT_MAX;   // priority landing in slot QS (evicted first)
+    }
+    __syncwarp();
+    // final slot of each admitted candidate: frontier entries not above it
+    // plus admitted candidates before it in (priority, list index) order;
+    // admitted priorities in that order into akey
+#pragma unroll
+    for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
+        const int i = half * kWarp + lane;
+        if ((am[half] >> lane) & 1u) {
+            const float key = prio[i];
+            int rank = 0;
+#pragma unroll
+            for (int h2 = 0; h2 < GOFANN_MAX_DEGREE / kWarp; ++h2) {
+                unsigned bits = am[h2];
+                while (bits) {
+                    const int j = h2 * kWarp + __ffs(bits) - 1;
+                    bits &= bits - 1;
+                    const float kj = prio[j];
+                    rank += (kj < key || (kj == key && j < i)) ? 1 : 0;
+                }
+            }
+            akey[rank] = key;
+            pos[half] += rank;
+            if (pos[half] == QS - 1) st.edge[0] = key;
+            if (pos[half] == QS) st.edge[1] = key;
+        }
+    }
+    __syncwarp();
+    // move the frontier entries up by the number of admitted candidates
+    // strictly below them, highest chunk first (every slot written was read
+    // already)
+    for (int c = (n - 1) & ~(kWarp - 1); c >= 0; c -= kWarp) {
+        const int k = c + lane;
+        float key = 0.0f, b = 0.0f;
+        uint32_t v = 0;
+        int np = QS + 1;
+        if (k < n) {
+            key = f.key[k];
+            v = f.val[k];
+            b = f.base[k];
+            np = k + count_below(akey, n_adm, key);
+            if (np == QS - 1) st.edge[0] = key;
+            if (np == QS) st.edge[1] = key;
+        }
+        __syncwarp();
+        if (np < QS) {
+            f.key[np] = key;
+            f.val[np] = v;
+            f.base[np] = b;
+        }
+        __syncwarp();
+    }
+#pragma unroll
+    for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
+        const int i = half * kWarp + lane;
+        if (((am[half] >> lane) & 1u) && pos[half] < QS) {
+            f.key[pos[half]] = prio[i];
+            f.val[pos[half]] = list[i] | (((pass[half] >> lane) & 1u) ? kPassBit : 0u);
+            f.base[pos[half]] = dist[i];
+        }
+    }
+    __syncwarp();
+    const bool tie_at_edge = n + n_adm > QS && st.edge[0] == st.edge[1];
+    if (lane == 0) st.heap_size = (n + n_adm < QS ? n + n_adm : QS) + 1;
+    __syncwarp();
+    return !tie_at_edge;
+}
+
+// Per-warp shared-memory views.
+struct WarpBufs {
+    FPair* frontier;    // reference heap (exact path)
+    SortedFrontier sf;  // sorted frontier (fast path), same bytes
+    RPair* topk;
+    SPair* stopk;
+    uint32_t* list;
+    uint32_t* slist;
+    float* dist;
+    float* prio;
+    float* akey;
+    WarpState* st;
+    uint32_t* nadj;
+    uint32_t* hash;
+};
+
+// One route from its seed to its shortlist.  kFast selects the sorted
+// frontier; it returns false when it gives up on a tie (nothing of the route
+// is final then: the caller runs the route again with kFast = false, which
+// rewrites every output).
+template <bool kFast, int kScorer, bool kBias, int kMode, int kW, int kMaxM>
+__device__ __forceinline__ bool run_route(const BeamArgs& a, const WarpBufs& w,
+                                          const Scorer<kScorer, kMode, kW, kMaxM>& score, uint32_t route,
+                                          uint32_t label_offset, uint32_t begin_id, uint64_t qbit, bool pred_on,
+                                          uint32_t deg, uint64_t stream, int lane)
+{
     const gofann_search_params& p = a.p;
-    const SmemLayout L = smem_layout(p, a.codes, kMode, a.prep.dim);
-    unsigned char* base = smem_raw + static_cast<size_t>(warp) * a.warp_smem;
-    FPair* frontier = reinterpret_cast<FPair*>(base + L.frontier);
-    RPair* topk = reinterpret_cast<RPair*>(base + L.topk);
-    SPair* stopk = reinterpret_cast<SPair*>(base + L.stop);
-    uint32_t* list = reinterpret_cast<uint32_t*>(base + L.list);
-    uint32_t* slist = reinterpret_cast<uint32_t*>(base + L.sample);
-    float* dist = reinterpret_cast<float*>(base + L.dist);
-    float* prio = reinterpret_cast<float*>(base + L.prio);
-    WarpState& st = *reinterpret_cast<WarpState*>(base + L.state);
-    float* table = reinterpret_cast<float*>(base + L.table);
-    uint32_t* nadj = reinterpret_cast<uint32_t*>(base + L.nadj);
-    const uint32_t gwarp = blockIdx.x * (blockDim.x >> 5) + warp;
-    uint32_t* hash = a.hash + static_cast<size_t>(gwarp) * kHashCap;
     const int QS = p.queue_size, SW = p.stop_width, RW = p.result_width;
-    const uint32_t deg = a.graph.degree < GOFANN_MAX_DEGREE ? a.graph.degree : GOFANN_MAX_DEGREE;
-    const uint64_t keep = l2_keep_policy(), stream = l2_stream_policy();
+    WarpState& st = *w.st;
+    FPair* frontier = w.frontier;
+    const SortedFrontier& sf = w.sf;
+    RPair* topk = w.topk;
+    SPair* stopk = w.stopk;
+    uint32_t* list = w.list;
+    uint32_t* slist = w.slist;
+    float* dist = w.dist;
+    float* prio = w.prio;
+    uint32_t* nadj = w.nadj;
+    uint32_t* hash = w.hash;
 
-    for (;;) {
-        uint32_t route = 0;
-        if (lane == 0) route = atomicAdd(a.route_counter, 1u);
-        route = __shfl_sync(kFull, route, 0);
-        if (route >= a.routes.n_routes) break;
+    // visited table clear (native_visited_hash::clear)
+    {
+        uint4* h4 = reinterpret_cast<uint4*>(hash);
+        const uint4 e = make_uint4(kU32Max, kU32Max, kU32Max, kU32Max);
+        for (int i = lane; i < kHashCap / 4; i += kWarp) h4[i] = e;
+    }
+    __syncwarp();
 
-        const uint32_t row = a.routes.query_row[route];
-        const uint32_t label_offset = a.graph.label_offset[a.routes.group_id[route]];
-        const uint32_t begin_id = a.routes.start_local[route];
-        const uint64_t qbit = a.routes.filter_bits ? a.routes.filter_bits[route] : ~0ull;
-        const bool pred_on = pred_enabled(a.routes, route);
-
-        // visited table clear (native_visited_hash::clear)
-        {
-            uint4* h4 = reinterpret_cast<uint4*>(hash);
-            const uint4 e = make_uint4(kU32Max, kU32Max, kU32Max, kU32Max);
-            for (int i = lane; i < kHashCap / 4; i += kWarp) h4[i] = e;
+    // start node (backend_pq.cu:4172-4209)
+    if (lane == 0) {
+        const uint32_t begin_sample = a.graph.row_to_sample[label_offset + begin_id];
+        const float start = score(a.codes, begin_sample);
+        float penalty = 0.0f;
+        if (kBias) {
+            const double wide = static_cast<double>(p.alpha) * fmax(static_cast<double>(fabsf(start)), 1e-6);
+            penalty = isfinite(wide) ? static_cast<float>(fmin(wide, static_cast<double>(FLT_MAX))) : 0.0f;
         }
-        Scorer<kScorer, kMode, kW, kMaxM> score;
-        score.keep = keep;
-        score.stream = stream;
-        if constexpr (kScorer == GOFANN_SCORER_PQ) {
-            if constexpr (kMode == GOFANN_PQ_DIRECT) {
-                const int dim = static_cast<int>(a.prep.dim);
-                if (a.prep.pq_query_dtype == GOFANN_DTYPE_U8) {
-                    const uint8_t* qr = static_cast<const uint8_t*>(a.prep.pq_query) + static_cast<size_t>(row) * dim;
-                    for (int i = lane; i < dim; i += kWarp) table[i] = static_cast<float>(qr[i]);
-                } else {
-                    const float* qr = static_cast<const float*>(a.prep.pq_query) + static_cast<size_t>(row) * dim;
-                    for (int i = lane; i < dim; i += kWarp) table[i] = qr[i];
-                }
-                score.lut_row = table;
-                score.cent = a.prep.pq_centroids;
-                score.dim = dim;
-            } else {
-                const float* g = a.prep.pq_lut + static_cast<size_t>(row) * a.codes.pq_dim * GOFANN_PQ_CENTROIDS;
-                if constexpr (kMode == GOFANN_PQ_LUT_SHARED) {
-                    const float4* s4 = reinterpret_cast<const float4*>(g);
-                    float4* d4 = reinterpret_cast<float4*>(table);
-                    const int n4 = static_cast<int>(a.codes.pq_dim) * GOFANN_PQ_CENTROIDS / 4;
-                    for (int i = lane; i < n4; i += kWarp) d4[i] = __ldg(s4 + i);
-                    score.lut_row = table;
-                } else {
-                    score.lut_row = g;
-                }
-            }
+        st.penalty = penalty;
+        st.heap_size = 1;
+        st.stop_size = 0;
+        st.topk_size = 0;
+        st.stop_worst = -FLT_MAX;
+        st.finished = 0;
+        st.exhausted = 0;
+        st.expanded = 0;
+        st.passed = 0;
+        st.n_dist = 1;
+        st.n_probe = 0;
+        st.n_admit = 0;
+        FPair kp;
+        kp.first = start;
+        kp.second = begin_id;
+        kp.base = start;
+        if (kBias && pred_on && pred_matches(a.routes, a.attrs, route, begin_sample)) kp.second |= kPassBit;
+        if constexpr (kFast) {
+            sf.key[0] = kp.first;
+            sf.val[0] = kp.second;
+            sf.base[0] = kp.base;
+            st.heap_size = 2;
+            st.brk = start == start ? 0 : 1;  // a NaN seed takes the exact path
         } else {
-            rq_build_planes(a.prep.rq_q8 + static_cast<size_t>(row) * a.codes.padded_dim,
-                            static_cast<int>(a.codes.padded_dim), reinterpret_cast<uint32_t*>(table), lane,
-                            kWarp);
-            score.rq.planes = reinterpret_cast<const uint32_t*>(table);
-            score.rq.scale = a.prep.rq_scale[row];
-            score.rq.k1 = a.prep.rq_k1xsumq[row];
-            score.rq.gdist = a.prep.rq_centroid_dist + static_cast<size_t>(row) * a.codes.num_anchors;
-        }
-        __syncwarp();
-
-        // start node (backend_pq.cu:4172-4209)
-        if (lane == 0) {
-            const uint32_t begin_sample = a.graph.row_to_sample[label_offset + begin_id];
-            const float start = score(a.codes, begin_sample);
-            float penalty = 0.0f;
-            if (kBias) {
-                const double wide = static_cast<double>(p.alpha) * fmax(static_cast<double>(fabsf(start)), 1e-6);
-                penalty = isfinite(wide) ? static_cast<float>(fmin(wide, static_cast<double>(FLT_MAX))) : 0.0f;
-            }
-            st.penalty = penalty;
-            st.heap_size = 1;
-            st.stop_size = 0;
-            st.topk_size = 0;
-            st.stop_worst = -FLT_MAX;
-            st.finished = 0;
-            st.exhausted = 0;
-            st.expanded = 0;
-            st.passed = 0;
-            st.n_dist = 1;
-            st.n_probe = 0;
-            st.n_admit = 0;
-            FPair kp;
-            kp.first = start;
-            kp.second = begin_id;
-            kp.base = start;
-            if (kBias && pred_on && pred_matches(a.routes, a.attrs, route, begin_sample)) kp.second |= kPassBit;
             smmh_insert(frontier, st.heap_size, kp);
-            hash_add(hash, begin_id);
-            st.hash_count = 1;
-            st.pf_row[0] = st.pf_row[1] = kU32Max;
-            st.pf_last = -1;
         }
-        __syncwarp();
+        hash_add(hash, begin_id);
+        st.hash_count = 1;
+        st.pf_row[0] = st.pf_row[1] = kU32Max;
+        st.pf_last = -1;
+    }
+    __syncwarp();
+    if constexpr (kFast) {
+        if (st.brk) return false;
+        sorted_pickup(sf, st.heap_size - 1, &st.now, lane);  // a single entry: no tie
+    } else {
         coop_pickup(frontier, st.heap_size, &st.now, lane);
+    }
 
-        int step = 0;
-        for (;;) {
-            if (step != 0 && st.heap_size <= 1) break;
-            ++step;
-            if (step != 1) {
-                FPair nx;
-                const bool found = coop_pickup(frontier, st.heap_size, &st.next, lane);
-                if (lane == 0) {
-                    if (!found) {
-                        st.exhausted = 1;
-                        nx.first = FLT_MAX; nx.second = kU32Max; nx.base = FLT_MAX;
-                        st.next = nx;
-                    } else if (st.stop_size == SW) {
-                        float pending = st.next.first;
-                        if (p.pending_base_stop && pred_on) {
-                            float m = fminf(FLT_MAX, kBias ? st.now.base : st.now.first);
-                            m = fminf(m, kBias ? st.next.base : st.next.first);
+    int step = 0;
+    for (;;) {
+        if (step != 0 && st.heap_size <= 1) break;
+        ++step;
+        if (step != 1) {
+            FPair nx;
+            bool found;
+            float unused_min = FLT_MAX;
+            if constexpr (kFast) {
+                const int got = sorted_pickup(sf, st.heap_size - 1, &st.next, lane);
+                if (got < 0) {
+                    prefetch_wait_all();
+                    __syncwarp();
+                    return false;
+                }
+                found = got > 0;
+                if (found && st.stop_size == SW && p.pending_base_stop && pred_on)
+                    unused_min = sorted_unused_min(sf, st.heap_size - 1, kBias, lane);
+            } else {
+                found = coop_pickup(frontier, st.heap_size, &st.next, lane);
+            }
+            if (lane == 0) {
+                if (!found) {
+                    st.exhausted = 1;
+                    nx.first = FLT_MAX; nx.second = kU32Max; nx.base = FLT_MAX;
+                    st.next = nx;
+                } else if (st.stop_size == SW) {
+                    float pending = st.next.first;
+                    if (p.pending_base_stop && pred_on) {
+                        float m = fminf(FLT_MAX, kBias ? st.now.base : st.now.first);
+                        m = fminf(m, kBias ? st.next.base : st.next.first);
+                        if constexpr (kFast) {
+                            m = fminf(m, unused_min);
+                        } else {
                             for (int i = 1; i < st.heap_size; ++i)
                                 if (!(frontier[i].second & kPoolUsed))
                                     m = fminf(m, kBias ? frontier[i].base : frontier[i].first);
-                            pending = m;
                         }
-                        if (p.early_stop_mode != GOFANN_EARLY_STOP_OFF && st.stop_worst <= pending) ++st.finished;
+                        pending = m;
                     }
+                    if (p.early_stop_mode != GOFANN_EARLY_STOP_OFF && st.stop_worst <= pending) ++st.finished;
                 }
-                __syncwarp();
-                if (found)
-                    prefetch_next(st, nadj, a.graph.adjacency, label_offset, a.graph.degree, deg,
-                                  st.next.second & kRowMask, lane, stream);
             }
-            if (st.exhausted) break;
-            const uint32_t now_row = st.now.second & kRowMask;
-            const uint32_t grow = label_offset + now_row;
+            __syncwarp();
+            if (found)
+                prefetch_next(st, nadj, a.graph.adjacency, label_offset, a.graph.degree, deg,
+                              st.next.second & kRowMask, lane, stream);
+        }
+        if (st.exhausted) break;
+        const uint32_t now_row = st.now.second & kRowMask;
+        const uint32_t grow = label_offset + now_row;
 
-            if (lane == 0) {
-                // filter verdict of the expanded node (backend_pq.cu:4394-4440)
-                const bool bit_match = a.graph.row_filter_mask ? (a.graph.row_filter_mask[grow] & qbit) != 0ull
-                                                               : qbit != 0ull;
-                const bool need_sample = a.routes.range_modes != nullptr || p.full_label_check != 0 ||
-                                         (pred_on && !kBias);
-                const uint32_t sample = need_sample ? a.graph.row_to_sample[grow] : 0u;
-                uint32_t active = 0, matched = 0;
-                if (a.routes.range_modes) {
-                    for (uint32_t i = 0; i < a.routes.range_count; ++i) {
-                        const size_t qf = static_cast<size_t>(route) * a.routes.range_count + i;
-                        const uint8_t mode = a.routes.range_modes[qf];
-                        if (mode == 0) continue;
-                        ++active;
-                        if (a.routes.range_lower && a.routes.range_upper && a.attrs.ranges &&
-                            range_match(mode, a.routes.range_lower[qf], a.routes.range_upper[qf],
-                                        a.attrs.ranges[static_cast<size_t>(sample) * a.routes.range_count + i]))
-                            ++matched;
-                    }
-                    if (!a.routes.range_lower || !a.routes.range_upper || !a.attrs.ranges) matched = 0;
+        if (lane == 0) {
+            // filter verdict of the expanded node (backend_pq.cu:4394-4440)
+            const bool bit_match = a.graph.row_filter_mask ? (a.graph.row_filter_mask[grow] & qbit) != 0ull
+                                                           : qbit != 0ull;
+            const bool need_sample = a.routes.range_modes != nullptr || p.full_label_check != 0 ||
+                                     (pred_on && !kBias);
+            const uint32_t sample = need_sample ? a.graph.row_to_sample[grow] : 0u;
+            uint32_t active = 0, matched = 0;
+            if (a.routes.range_modes) {
+                for (uint32_t i = 0; i < a.routes.range_count; ++i) {
+                    const size_t qf = static_cast<size_t>(route) * a.routes.range_count + i;
+                    const uint8_t mode = a.routes.range_modes[qf];
+                    if (mode == 0) continue;
+                    ++active;
+                    if (a.routes.range_lower && a.routes.range_upper && a.attrs.ranges &&
+                        range_match(mode, a.routes.range_lower[qf], a.routes.range_upper[qf],
+                                    a.attrs.ranges[static_cast<size_t>(sample) * a.routes.range_count + i]))
+                        ++matched;
                 }
-                const bool exact_range = active == 0 || matched == active;
-                int nfr = (p.full_label_check == 0 || labels_match(a.routes, a.attrs, route, sample)) ? 1 : 2;
-                if (pred_on) {
-                    if (kBias)
-                        nfr = (st.now.second & kPassBit) ? 1 : 2;
-                    else
-                        nfr = pred_matches(a.routes, a.attrs, route, sample) ? 1 : 2;
-                    ++st.n_probe;
-                } else if (!a.routes.route_compiled || !a.routes.route_compiled[route]) {
-                    nfr = (nfr == 1 && bit_match && exact_range) ? 1 : 2;
-                }
-                st.nfr = nfr;
-                st.brk = stop_now(p, st, step) ? 1 : 0;
-                if (!st.brk) {
-                    if (a.out.trace && static_cast<uint32_t>(st.expanded) < a.out.trace_width)
-                        a.out.trace[static_cast<size_t>(route) * a.out.trace_width + st.expanded] = now_row;
-                    ++st.expanded;
-                    if (nfr == 1) {
-                        // stop top-k and result heap (backend_pq.cu:4583-4630)
-                        ++st.passed;
-                        const float current = kBias ? st.now.base : st.now.first;
-                        RPair te;
-                        te.first = current;
-                        te.second = now_row;
-                        SPair se;
-                        se.first = current;
-                        se.pad = 0;
-                        se.second = (static_cast<uint64_t>(__float_as_uint(current)) << 32) | now_row;
-                        bool improved = false;
-                        if (st.stop_size < SW) {
-                            stopk[st.stop_size++] = se;
-                            bheap_push(stopk, st.stop_size);
-                            improved = true;
-                            if (st.stop_size == 1 || current > st.stop_worst) st.stop_worst = current;
-                        } else if (se.first < stopk[0].first) {
-                            stopk[st.stop_size++] = se;
-                            bheap_push(stopk, st.stop_size);
-                            const SPair removed = bheap_pop(stopk, st.stop_size);
-                            --st.stop_size;
-                            improved = true;
-                            const uint32_t removed_bits = static_cast<uint32_t>(removed.second >> 32);
-                            if (current > st.stop_worst) {
-                                st.stop_worst = current;
-                            } else if (removed_bits == __float_as_uint(st.stop_worst)) {
-                                st.stop_worst = -FLT_MAX;
-                                for (int i = 0; i < st.stop_size; ++i) {
-                                    const float pd = __uint_as_float(static_cast<uint32_t>(stopk[i].second >> 32));
-                                    if (pd > st.stop_worst) st.stop_worst = pd;
-                                }
+                if (!a.routes.range_lower || !a.routes.range_upper || !a.attrs.ranges) matched = 0;
+            }
+            const bool exact_range = active == 0 || matched == active;
+            int nfr = (p.full_label_check == 0 || labels_match(a.routes, a.attrs, route, sample)) ? 1 : 2;
+            if (pred_on) {
+                if (kBias)
+                    nfr = (st.now.second & kPassBit) ? 1 : 2;
+                else
+                    nfr = pred_matches(a.routes, a.attrs, route, sample) ? 1 : 2;
+                ++st.n_probe;
+            } else if (!a.routes.route_compiled || !a.routes.route_compiled[route]) {
+                nfr = (nfr == 1 && bit_match && exact_range) ? 1 : 2;
+            }
+            st.nfr = nfr;
+            st.brk = stop_now(p, st, step) ? 1 : 0;
+            if (!st.brk) {
+                if (a.out.trace && static_cast<uint32_t>(st.expanded) < a.out.trace_width)
+                    a.out.trace[static_cast<size_t>(route) * a.out.trace_width + st.expanded] = now_row;
+                ++st.expanded;
+                if (nfr == 1) {
+                    // stop top-k and result heap (backend_pq.cu:4583-4630)
+                    ++st.passed;
+                    const float current = kBias ? st.now.base : st.now.first;
+                    RPair te;
+                    te.first = current;
+                    te.second = now_row;
+                    SPair se;
+                    se.first = current;
+                    se.pad = 0;
+                    se.second = (static_cast<uint64_t>(__float_as_uint(current)) << 32) | now_row;
+                    bool improved = false;
+                    if (st.stop_size < SW) {
+                        stopk[st.stop_size++] = se;
+                        bheap_push(stopk, st.stop_size);
+                        improved = true;
+                        if (st.stop_size == 1 || current > st.stop_worst) st.stop_worst = current;
+                    } else if (se.first < stopk[0].first) {
+                        stopk[st.stop_size++] = se;
+                        bheap_push(stopk, st.stop_size);
+                        const SPair removed = bheap_pop(stopk, st.stop_size);
+                        --st.stop_size;
+                        improved = true;
+                        const uint32_t removed_bits = static_cast<uint32_t>(removed.second >> 32);
+                        if (current > st.stop_worst) {
+                            st.stop_worst = current;
+                        } else if (removed_bits == __float_as_uint(st.stop_worst)) {
+                            st.stop_worst = -FLT_MAX;
+                            for (int i = 0; i < st.stop_size; ++i) {
+                                const float pd = __uint_as_float(static_cast<uint32_t>(stopk[i].second >> 32));
+                                if (pd > st.stop_worst) st.stop_worst = pd;
                             }
                         }
-                        if (p.early_stop_mode == GOFANN_EARLY_STOP_ADAPTIVE && improved) st.finished = 0;
-                        if (st.topk_size < RW) {
-                            topk[st.topk_size++] = te;
-                            bheap_push(topk, st.topk_size);
-                        } else if (te.first < topk[0].first) {
-                            topk[st.topk_size++] = te;
-                            bheap_push(topk, st.topk_size);
-                            bheap_pop(topk, st.topk_size);
-                            --st.topk_size;
-                        }
+                    }
+                    if (p.early_stop_mode == GOFANN_EARLY_STOP_ADAPTIVE && improved) st.finished = 0;
+                    if (st.topk_size < RW) {
+                        topk[st.topk_size++] = te;
+                        bheap_push(topk, st.topk_size);
+                    } else if (te.first < topk[0].first) {
+                        topk[st.topk_size++] = te;
+                        bheap_push(topk, st.topk_size);
+                        bheap_pop(topk, st.topk_size);
+                        --st.topk_size;
                     }
                 }
             }
-            __syncwarp();
-            if (st.brk) break;
+        }
+        __syncwarp();
+        if (st.brk) break;
 
-            // neighbour list: parallel read + visited test, in-order compaction
-            const int pslot = st.pf_row[0] == now_row ? 0 : (st.pf_row[1] == now_row ? 1 : -1);
-            if (pslot >= 0) {
-                if (pslot == st.pf_last) prefetch_wait_all();
-                else prefetch_wait_older();  // the newer group (the next row) may stay in flight
-            }
-            __syncwarp();
-            const bool prefetched = pslot >= 0;
-            const uint32_t* adj = prefetched ? nadj + pslot * GOFANN_MAX_DEGREE
-                                             : a.graph.adjacency + static_cast<size_t>(grow) * a.graph.degree;
-            int len = 0;
+        // neighbour list: parallel read + visited test, in-order compaction
+        const int pslot = st.pf_row[0] == now_row ? 0 : (st.pf_row[1] == now_row ? 1 : -1);
+        if (pslot >= 0) {
+            if (pslot == st.pf_last) prefetch_wait_all();
+            else prefetch_wait_older();  // the newer group (the next row) may stay in flight
+        }
+        __syncwarp();
+        const bool prefetched = pslot >= 0;
+        const uint32_t* adj = prefetched ? nadj + pslot * GOFANN_MAX_DEGREE
+                                         : a.graph.adjacency + static_cast<size_t>(grow) * a.graph.degree;
+        int len = 0;
+#pragma unroll
+        for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
+            const uint32_t i = half * kWarp + lane;
+            uint32_t idx = kU32Max;
+            if (i < deg) idx = prefetched ? adj[i] : ldg_u32(adj + i, stream);
+            const bool keep = idx != kU32Max && !hash_test(hash, idx);
+            const unsigned m = __ballot_sync(kFull, keep);
+            if (keep) list[len + __popc(m & ((1u << lane) - 1u))] = idx;
+            len += __popc(m);
+        }
+        __syncwarp();
+        if (lane == 0) {
+            st.len = len;
+            st.brk = stop_now(p, st, step) ? 1 : 0;
+        }
+        __syncwarp();
+        if (st.brk) break;
+
+        // score every listed candidate, one candidate per lane
+        for (int i = lane; i < len; i += kWarp) {
+            const uint32_t s = ldg_u32(a.graph.row_to_sample + label_offset + list[i], stream);
+            slist[i] = s;
+            dist[i] = score(a.codes, s);
+        }
+        __syncwarp();
+        if constexpr (kFast) {
+            // priorities and pass bits; admissions as one sorted merge
+            uint32_t pbits[2];
 #pragma unroll
             for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
-                const uint32_t i = half * kWarp + lane;
-                uint32_t idx = kU32Max;
-                if (i < deg) idx = prefetched ? adj[i] : ldg_u32(adj + i, stream);
-                const bool keep = idx != kU32Max && !hash_test(hash, idx);
-                const unsigned m = __ballot_sync(kFull, keep);
-                if (keep) list[len + __popc(m & ((1u << lane) - 1u))] = idx;
-                len += __popc(m);
+                const int i = half * kWarp + lane;
+                bool pass = false;
+                if (i < len) {
+                    float pr = dist[i];
+                    if (kBias && pred_on) {
+                        pass = pred_matches(a.routes, a.attrs, route, slist[i]);
+                        pr = pred_priority(dist[i], st.penalty, pass);
+                    }
+                    prio[i] = pr;
+                }
+                pbits[half] = __ballot_sync(kFull, pass);
             }
             __syncwarp();
+            uint32_t adm[2] = {0u, 0u};
+            int n_adm = 0;
+            if (!sorted_admit(sf, st, QS, list, prio, dist, pbits, len, w.akey, adm, n_adm, lane)) {
+                prefetch_wait_all();
+                __syncwarp();
+                return false;
+            }
             if (lane == 0) {
-                st.len = len;
-                st.brk = stop_now(p, st, step) ? 1 : 0;
+                st.n_dist += static_cast<uint32_t>(len);
+                if (kBias && pred_on) st.n_probe += static_cast<uint32_t>(len);
+                st.n_admit += static_cast<uint32_t>(n_adm);
+                st.adm[0] = adm[0];
+                st.adm[1] = adm[1];
+                st.serial_hash = st.hash_count + n_adm > kHashCap ? 1 : 0;
+                if (st.serial_hash) {
+                    for (int i = 0; i < len; ++i)
+                        if ((adm[i >> 5] >> (i & 31)) & 1u) st.hash_count += hash_add(hash, list[i]) ? 1 : 0;
+                } else {
+                    st.hash_count += n_adm;
+                }
             }
             __syncwarp();
-            if (st.brk) break;
-
-            // score every listed candidate, one candidate per lane
-            for (int i = lane; i < len; i += kWarp) {
-                const uint32_t s = ldg_u32(a.graph.row_to_sample + label_offset + list[i], stream);
-                slist[i] = s;
-                dist[i] = score(a.codes, s);
-            }
-            __syncwarp();
+        } else {
             const bool full = st.heap_size >= QS + 1;
             const float maxv = full ? frontier[2].first : 0.0f;
 #pragma unroll
@@ -586,70 +818,168 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) beam_search_kernel(BeamAr
                 }
             }
             __syncwarp();
-            if (!st.serial_hash) {
+        }
+        if (!st.serial_hash) {
 #pragma unroll
-                for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half)
-                    if ((st.adm[half] >> lane) & 1u) hash_add_concurrent(hash, list[half * kWarp + lane]);
-            }
-            __syncwarp();
-            if (step == 1) {
-                const bool found = coop_pickup(frontier, st.heap_size, &st.next, lane);
-                if (lane == 0 && !found) {
-                    st.exhausted = 1;
-                    FPair nx;
-                    nx.first = FLT_MAX; nx.second = kU32Max; nx.base = FLT_MAX;
-                    st.next = nx;
+            for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half)
+                if ((st.adm[half] >> lane) & 1u) hash_add_concurrent(hash, list[half * kWarp + lane]);
+        }
+        __syncwarp();
+        if (step == 1) {
+            bool found;
+            if constexpr (kFast) {
+                const int got = sorted_pickup(sf, st.heap_size - 1, &st.next, lane);
+                if (got < 0) {
+                    prefetch_wait_all();
+                    __syncwarp();
+                    return false;
                 }
-                if (found)
-                    prefetch_next(st, nadj, a.graph.adjacency, label_offset, a.graph.degree, deg,
-                                  st.next.second & kRowMask, lane, stream);
+                found = got > 0;
+            } else {
+                found = coop_pickup(frontier, st.heap_size, &st.next, lane);
             }
-            if (lane == 0) st.now = st.next;
-            __syncwarp();
-        }
-
-        prefetch_wait_all();  // no copy of this route may land in the next route's slots
-        __syncwarp();
-
-        // emit the shortlist ascending (in-place heap sort of the result heap)
-        if (lane == 0) {
-            const int valid = st.topk_size;
-            for (int i = 0; i < valid; ++i) {
-                const int n = valid - i;
-                const RPair r = bheap_pop(topk, n);
-                topk[n - 1] = r;
+            if (lane == 0 && !found) {
+                st.exhausted = 1;
+                FPair nx;
+                nx.first = FLT_MAX; nx.second = kU32Max; nx.base = FLT_MAX;
+                st.next = nx;
             }
-            if (step >= (p.max_steps > 0 ? p.max_steps : kMaxSteps) && p.max_steps == 0 && a.status)
-                atomicExch(a.status, GOFANN_ERR_CAPACITY);
+            if (found)
+                prefetch_next(st, nadj, a.graph.adjacency, label_offset, a.graph.degree, deg,
+                              st.next.second & kRowMask, lane, stream);
         }
+        if (lane == 0) st.now = st.next;
         __syncwarp();
+    }
+
+    prefetch_wait_all();  // no copy of this route may land in the next route's slots
+    __syncwarp();
+
+    // emit the shortlist ascending (in-place heap sort of the result heap)
+    if (lane == 0) {
         const int valid = st.topk_size;
-        uint32_t* oid = a.out.ids + static_cast<size_t>(route) * RW;
-        float* od = a.out.dists + static_cast<size_t>(route) * RW;
-        for (int i = lane; i < RW; i += kWarp) {
-            uint32_t id = kU32Max;
-            float d = FLT_MAX;
-            if (i < valid && topk[i].second != kU32Max) {
-                id = a.graph.row_to_sample[label_offset + topk[i].second];
-                d = topk[i].first;
-            }
-            oid[i] = id;
-            od[i] = d;
+        for (int i = 0; i < valid; ++i) {
+            const int n = valid - i;
+            const RPair r = bheap_pop(topk, n);
+            topk[n - 1] = r;
         }
-        if (a.out.trace)
-            for (uint32_t i = static_cast<uint32_t>(st.expanded) + lane; i < a.out.trace_width; i += kWarp)
-                a.out.trace[static_cast<size_t>(route) * a.out.trace_width + i] = kU32Max;
-        if (lane == 0) {
-            if (a.out.steps) a.out.steps[route] = step;
-            if (a.out.counters) {
-                uint32_t* c = a.out.counters + static_cast<size_t>(route) * 4;
-                c[0] = static_cast<uint32_t>(st.expanded);
-                c[1] = st.n_dist;
-                c[2] = st.n_probe;
-                c[3] = st.n_admit;
+        if (step >= (p.max_steps > 0 ? p.max_steps : kMaxSteps) && p.max_steps == 0 && a.status)
+            atomicExch(a.status, GOFANN_ERR_CAPACITY);
+    }
+    __syncwarp();
+    const int valid = st.topk_size;
+    uint32_t* oid = a.out.ids + static_cast<size_t>(route) * RW;
+    float* od = a.out.dists + static_cast<size_t>(route) * RW;
+    for (int i = lane; i < RW; i += kWarp) {
+        uint32_t id = kU32Max;
+        float d = FLT_MAX;
+        if (i < valid && topk[i].second != kU32Max) {
+            id = a.graph.row_to_sample[label_offset + topk[i].second];
+            d = topk[i].first;
+        }
+        oid[i] = id;
+        od[i] = d;
+    }
+    if (a.out.trace)
+        for (uint32_t i = static_cast<uint32_t>(st.expanded) + lane; i < a.out.trace_width; i += kWarp)
+            a.out.trace[static_cast<size_t>(route) * a.out.trace_width + i] = kU32Max;
+    if (lane == 0) {
+        if (a.out.steps) a.out.steps[route] = step;
+        if (a.out.counters) {
+            uint32_t* c = a.out.counters + static_cast<size_t>(route) * 4;
+            c[0] = static_cast<uint32_t>(st.expanded);
+            c[1] = st.n_dist;
+            c[2] = st.n_probe;
+            c[3] = st.n_admit;
+        }
+    }
+    __syncwarp();
+    return true;
+}
+
+template <int kScorer, bool kBias, int kMode, int kW, int kMaxM>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, 6) beam_search_kernel(BeamArgs a)
+{
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const gofann_search_params& p = a.p;
+    const SmemLayout L = smem_layout(p, a.codes, kMode, a.prep.dim);
+    unsigned char* base = smem_raw + static_cast<size_t>(warp) * a.warp_smem;
+    const uint32_t fcap = static_cast<uint32_t>(p.queue_size) + 2;
+    WarpBufs w;
+    w.frontier = reinterpret_cast<FPair*>(base + L.frontier);
+    w.sf.key = reinterpret_cast<float*>(base + L.frontier);
+    w.sf.val = reinterpret_cast<uint32_t*>(base + L.frontier + 4 * fcap);
+    w.sf.base = reinterpret_cast<float*>(base + L.frontier + 8 * fcap);
+    w.topk = reinterpret_cast<RPair*>(base + L.topk);
+    w.stopk = reinterpret_cast<SPair*>(base + L.stop);
+    w.list = reinterpret_cast<uint32_t*>(base + L.list);
+    w.slist = reinterpret_cast<uint32_t*>(base + L.sample);
+    w.dist = reinterpret_cast<float*>(base + L.dist);
+    w.prio = reinterpret_cast<float*>(base + L.prio);
+    w.akey = reinterpret_cast<float*>(base + L.akey);
+    w.st = reinterpret_cast<WarpState*>(base + L.state);
+    w.nadj = reinterpret_cast<uint32_t*>(base + L.nadj);
+    float* table = reinterpret_cast<float*>(base + L.table);
+    const uint32_t gwarp = blockIdx.x * (blockDim.x >> 5) + warp;
+    w.hash = a.hash + static_cast<size_t>(gwarp) * kHashCap;
+    const uint32_t deg = a.graph.degree < GOFANN_MAX_DEGREE ? a.graph.degree : GOFANN_MAX_DEGREE;
+    const uint64_t keep = l2_keep_policy(), stream = l2_stream_policy();
+
+    for (;;) {
+        uint32_t route = 0;
+        if (lane == 0) route = atomicAdd(a.route_counter, 1u);
+        route = __shfl_sync(kFull, route, 0);
+        if (route >= a.routes.n_routes) break;
+
+        const uint32_t row = a.routes.query_row[route];
+        const uint32_t label_offset = a.graph.label_offset[a.routes.group_id[route]];
+        const uint32_t begin_id = a.routes.start_local[route];
+        const uint64_t qbit = a.routes.filter_bits ? a.routes.filter_bits[route] : ~0ull;
+        const bool pred_on = pred_enabled(a.routes, route);
+
+        Scorer<kScorer, kMode, kW, kMaxM> score;
+        score.keep = keep;
+        score.stream = stream;
+        if constexpr (kScorer == GOFANN_SCORER_PQ) {
+            if constexpr (kMode == GOFANN_PQ_DIRECT) {
+                const int dim = static_cast<int>(a.prep.dim);
+                if (a.prep.pq_query_dtype == GOFANN_DTYPE_U8) {
+                    const uint8_t* qr = static_cast<const uint8_t*>(a.prep.pq_query) + static_cast<size_t>(row) * dim;
+                    for (int i = lane; i < dim; i += kWarp) table[i] = static_cast<float>(qr[i]);
+                } else {
+                    const float* qr = static_cast<const float*>(a.prep.pq_query) + static_cast<size_t>(row) * dim;
+                    for (int i = lane; i < dim; i += kWarp) table[i] = qr[i];
+                }
+                score.lut_row = table;
+                score.cent = a.prep.pq_centroids;
+                score.dim = dim;
+            } else {
+                const float* g = a.prep.pq_lut + static_cast<size_t>(row) * a.codes.pq_dim * GOFANN_PQ_CENTROIDS;
+                if constexpr (kMode == GOFANN_PQ_LUT_SHARED) {
+                    const float4* s4 = reinterpret_cast<const float4*>(g);
+                    float4* d4 = reinterpret_cast<float4*>(table);
+                    const int n4 = static_cast<int>(a.codes.pq_dim) * GOFANN_PQ_CENTROIDS / 4;
+                    for (int i = lane; i < n4; i += kWarp) d4[i] = __ldg(s4 + i);
+                    score.lut_row = table;
+                } else {
+                    score.lut_row = g;
+                }
             }
+        } else {
+            rq_build_planes(a.prep.rq_q8 + static_cast<size_t>(row) * a.codes.padded_dim,
+                            static_cast<int>(a.codes.padded_dim), reinterpret_cast<uint32_t*>(table), lane,
+                            kWarp);
+            score.rq.planes = reinterpret_cast<const uint32_t*>(table);
+            score.rq.scale = a.prep.rq_scale[row];
+            score.rq.k1 = a.prep.rq_k1xsumq[row];
+            score.rq.gdist = a.prep.rq_centroid_dist + static_cast<size_t>(row) * a.codes.num_anchors;
         }
         __syncwarp();
+
+        if (!run_route<true, kScorer, kBias, kMode, kW, kMaxM>(a, w, score, route, label_offset, begin_id, qbit, pred_on, deg, stream, lane))
+            run_route<false, kScorer, kBias, kMode, kW, kMaxM>(a, w, score, route, label_offset, begin_id, qbit, pred_on, deg, stream, lane);
     }
 }
 
@@ -664,8 +994,11 @@ KernelFn pick_pq(int mode, bool w4, bool small_m)
         return small_m ? beam_search_kernel<0, kBias, GOFANN_PQ_DIRECT, 0, 64>
                        : beam_search_kernel<0, kBias, GOFANN_PQ_DIRECT, 0, 128>;
     }
-    if (mode == GOFANN_PQ_LUT_SHARED) return beam_search_kernel<0, kBias, GOFANN_PQ_LUT_SHARED, 0, 128>;
-    return beam_search_kernel<0, kBias, GOFANN_PQ_LUT_GLOBAL, 0, 128>;
+    if (mode == GOFANN_PQ_LUT_SHARED)
+        return small_m ? beam_search_kernel<0, kBias, GOFANN_PQ_LUT_SHARED, 0, 64>
+                       : beam_search_kernel<0, kBias, GOFANN_PQ_LUT_SHARED, 0, 128>;
+    return small_m ? beam_search_kernel<0, kBias, GOFANN_PQ_LUT_GLOBAL, 0, 64>
+                   : beam_search_kernel<0, kBias, GOFANN_PQ_LUT_GLOBAL, 0, 128>;
 }
 
 // w4: 4-wide subvectors with 16-byte aligned codebook rows (vector loads);

@@ -37,14 +37,16 @@ __device__ __forceinline__ void load_code_words(const uint8_t* __restrict__ code
     }
 }
 
-// The same with an L2 policy on the row (code rows are streaming data).
+// Code row of at most kMaxM bytes with an L2 policy (code rows are streaming
+// data), into kMaxM / 4 words.
+template <int kMaxM>
 __device__ __forceinline__ void load_code_words(const uint8_t* __restrict__ code, int m_bytes,
-                                                uint32_t (&cw)[kMaxPqDim / 4], uint64_t pol)
+                                                uint32_t (&cw)[kMaxM / 4], uint64_t pol)
 {
     if ((m_bytes & 15) == 0 && (reinterpret_cast<uintptr_t>(code) & 15) == 0) {
         const uint4* p = reinterpret_cast<const uint4*>(code);
 #pragma unroll
-        for (int i = 0; i < kMaxPqDim / 16; ++i) {
+        for (int i = 0; i < kMaxM / 16; ++i) {
             if (i < (m_bytes >> 4)) {
                 const uint4 x = ldg_u32x4(p + i, pol);
                 cw[4 * i + 0] = x.x; cw[4 * i + 1] = x.y; cw[4 * i + 2] = x.z; cw[4 * i + 3] = x.w;
@@ -53,40 +55,50 @@ __device__ __forceinline__ void load_code_words(const uint8_t* __restrict__ code
             }
         }
     } else {
-        load_code_words(code, m_bytes, cw);
+#pragma unroll
+        for (int i = 0; i < kMaxM / 4; ++i) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int b = 0; b < 4; ++b)
+                if (4 * i + b < m_bytes) word |= static_cast<uint32_t>(__ldg(code + 4 * i + b)) << (8 * b);
+            cw[i] = word;
+        }
     }
 }
 
-__device__ __forceinline__ uint32_t code_byte(const uint32_t (&cw)[kMaxPqDim / 4], int m)
+template <int kWords>
+__device__ __forceinline__ uint32_t code_byte(const uint32_t (&cw)[kWords], int m)
 {
     return (cw[m >> 2] >> ((m & 3) * 8)) & 0xffu;
 }
 
+
 // ADC in the reference's warp order (backend_pq.cu:4711-4725), computed by
 // one thread: lane j's partial sums subspaces j, j+32, ... from 0, then the
 // xor butterfly.  `lut_row` is [pq_dim][256] in global or shared memory.
-__device__ __forceinline__ float pq_adc_words(const float* lut_row, const uint32_t (&cw)[kMaxPqDim / 4],
-                                              int pq_dim)
+template <int kMaxM>
+__device__ __forceinline__ float pq_adc_words(const float* lut_row, const uint32_t (&cw)[kMaxM / 4], int pq_dim)
 {
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = 0.0f;
 #pragma unroll
-    for (int m = 0; m < kMaxPqDim; ++m)
+    for (int m = 0; m < kMaxM; ++m)
         if (m < pq_dim) v[m & 31] = __fadd_rn(v[m & 31], lut_row[m * GOFANN_PQ_CENTROIDS + code_byte(cw, m)]);
     return butterfly_sum32(v);
 }
 
 // pq_adc_words over a table row in global memory, table gathers under the
 // `keep` L2 policy.
+template <int kMaxM>
 __device__ __forceinline__ float pq_adc_words_global(const float* __restrict__ lut_row,
-                                                     const uint32_t (&cw)[kMaxPqDim / 4], int pq_dim, uint64_t keep)
+                                                     const uint32_t (&cw)[kMaxM / 4], int pq_dim, uint64_t keep)
 {
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = 0.0f;
 #pragma unroll
-    for (int m = 0; m < kMaxPqDim; ++m)
+    for (int m = 0; m < kMaxM; ++m)
         if (m < pq_dim)
             v[m & 31] = __fadd_rn(v[m & 31], ldg_f32(lut_row + m * GOFANN_PQ_CENTROIDS + code_byte(cw, m), keep));
     return butterfly_sum32(v);
@@ -96,7 +108,7 @@ __device__ __forceinline__ float pq_adc_warp_order(const float* lut_row, const u
 {
     uint32_t cw[kMaxPqDim / 4];
     load_code_words(code, pq_dim, cw);
-    return pq_adc_words(lut_row, cw, pq_dim);
+    return pq_adc_words<kMaxPqDim>(lut_row, cw, pq_dim);
 }
 
 // Table entry (m, c) = sum over the subvector of fma(diff, diff, acc), diff =
@@ -134,8 +146,8 @@ template <int kW, int kMaxM>
 __device__ __forceinline__ float pq_adc_direct(const float* q, const float* __restrict__ cent, int dim,
                                                const uint8_t* code, int pq_dim, uint64_t keep, uint64_t stream)
 {
-    uint32_t cw[kMaxPqDim / 4];
-    load_code_words(code, pq_dim, cw, stream);
+    uint32_t cw[kMaxM / 4];
+    load_code_words<kMaxM>(code, pq_dim, cw, stream);
     const int w = dim / pq_dim;
     float v[32];
 #pragma unroll

@@ -313,8 +313,12 @@ def build_index(data: dict, threshold=2000, degree=64, n_random=40, pq_dim=48, s
                 nn = merge_candidates(torch.cat(cand_i, 1), torch.cat(cand_d, 1), n_near)
             adj = adjacency[row:row + nl]
             adj[:, :n_near] = nn.to(torch.int32)
-            rnd = torch.randint(0, nl, (nl, n_random), generator=grand, device=dev)
-            dup = (rnd.unsqueeze(2) == nn.unsqueeze(1)).any(2) | (rnd == torch.arange(nl, device=dev).unsqueeze(1))
+            # long-range edges: distinct per row (sorted, repeats dropped), never
+            # the row itself or one of its near edges
+            rnd = torch.randint(0, nl, (nl, n_random), generator=grand, device=dev).sort(dim=1).values
+            dup = torch.zeros_like(rnd, dtype=torch.bool)
+            dup[:, 1:] = rnd[:, 1:] == rnd[:, :-1]
+            dup |= (rnd.unsqueeze(2) == nn.unsqueeze(1)).any(2) | (rnd == torch.arange(nl, device=dev).unsqueeze(1))
             adj[:, n_near:] = torch.where(dup, torch.full_like(rnd, -1), rnd).to(torch.int32)
             mean = x.mean(0)
             seeds[gi] = int((x - mean).square().sum(1).argmin())

@@ -229,6 +229,31 @@ def test_beam_search_pq_bitexact(L, wl, vi):
         assert np.array_equal(g, o), f"{name} differ in {np.count_nonzero(np.any(np.atleast_2d(g != o), axis=-1))} routes"
 
 
+@pytest.mark.parametrize("share", [2, 20])
+@pytest.mark.parametrize("vi", [0, 2, 5, 6])
+def test_beam_search_pq_ties_bitexact(L, share, vi):
+    """Equal priorities: samples share PQ codes (every 2nd, or every 20th,
+    sample copies its neighbour's code row), so candidates tie exactly and the
+    order among equal entries is decided by the reference heap's layout."""
+    w, idx, plan = cfg2_small()
+    codes = idx.codes()
+    pq = codes["pq_codes"].copy()
+    rows = np.arange(pq.shape[0])
+    dup = rows[(rows % share) == 1]
+    pq[dup] = pq[dup - 1]
+    codes = dict(codes, pq_codes=pq)
+    params = dict(BEAM_VARIANTS[vi], scorer=A.SCORER_PQ)
+    lut = O.pq_build_lut(w.queries.astype(np.float32), idx.pq_centroids, pq.shape[1])
+    want = O.beam_search(idx.graph(), idx.attrs(), codes, {"pq_lut": lut}, plan.graph_routes, threads=8,
+                         trace_width=64, **params)
+    got = run_gpu_beam(L, idx.graph(), idx.attrs(), codes, pq_prep(w, idx, params["pq_mode"]), plan.graph_routes,
+                       trace_width=64, **params)
+    for name, g, o in zip(("ids", "dists", "steps", "counters", "trace"), got, want):
+        if name == "dists":
+            g, o = fbits(g), fbits(o)
+        assert np.array_equal(g, o), f"{name} differ in {np.count_nonzero(np.any(np.atleast_2d(g != o), axis=-1))} routes"
+
+
 @pytest.mark.parametrize("vi", [0, 1, 3])
 def test_beam_search_rabitq_bitexact(L, vi):
     w, idx, plan, rq, anchors, qr = rabitq_artifacts()
