@@ -35,6 +35,7 @@ for p in (str(ROOT), str(ROOT / "go-fann_b200")):
 import numpy as np  # noqa: E402
 
 QUEUE_SWEEP = [16, 32, 48, 64, 96, 128, 192, 256, 384, 512]  # configs/yfcc10m/categorical.json
+PQ_MODE_NAMES = {0: "table_global", 1: "table_shared", 2: "direct", 3: "u8_codebook"}
 METRIC = "filtered QPS @ recall@10=0.95"
 
 
@@ -49,7 +50,10 @@ def parse():
     ap.add_argument("--eval", type=int, default=2000, help="queries with exact ground truth")
     ap.add_argument("--queue-size", type=int, default=0, help="fixed queue size (0 = sweep)")
     ap.add_argument("--recall", type=float, default=0.95)
-    ap.add_argument("--pq-mode", type=int, default=0, help="0 LUT in global, 1 LUT in shared, 2 direct")
+    ap.add_argument("--pq-mode", type=int, default=3,
+                    help="PQ scoring: 0 table in global memory, 1 table in shared memory, 2 direct from the "
+                         "codebook, 3 integer codebook (u8; the index builder rounds the codebook)")
+    ap.add_argument("--resident-warps", type=int, default=0, help="cap on concurrent routes (0 = automatic)")
     ap.add_argument("--cpu-sample", type=int, default=0, help="queries in the CPU baseline sample (0 = auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
@@ -141,15 +145,17 @@ def build_workload(args, rank, world, device, t0):
 
 
 def beam_bytes(counters: np.ndarray, n_routes: int, degree: int, pq_dim: int, avg_labels: float,
-               result_width: int) -> float:
+               result_width: int, route_table_bytes: int) -> float:
     """Algorithmic HBM bytes of one beam-search launch: per expansion the
     adjacency row and its row->sample entry; per distance evaluation the
     row->sample entry and the code row; per predicate probe the CSR offsets
-    and the sample's label row; per route its LUT row once and its shortlist
-    output.  Cache hits are not discounted, nothing is counted twice."""
+    and the sample's label row; per route its query state once (the 48 KB
+    lookup row in the table modes, the query row in the integer-codebook
+    mode) and its shortlist output.  Cache hits are not discounted, nothing
+    is counted twice."""
     e, v, p = counters[:, 0].sum(), counters[:, 1].sum(), counters[:, 2].sum()
     return float(e * (degree * 4 + 4) + v * (4 + pq_dim) + p * (16 + 4 * avg_labels) +
-                 n_routes * (pq_dim * 256 * 4 + result_width * 8))
+                 n_routes * (route_table_bytes + result_width * 8))
 
 
 # ------------------------------------------------------------ GPU arm
@@ -179,7 +185,7 @@ def run_gofann(args):
     k = 10
 
     def make_pipe(qs):
-        cfg = SearchConfig(queue_size=qs, result_width=100, pq_mode=args.pq_mode)
+        cfg = SearchConfig(queue_size=qs, result_width=100, pq_mode=args.pq_mode, resident_warps=args.resident_warps)
         return Pipeline(dindex, dplan, cfg)
 
     xchg = ShardExchange(world, nq, k, device) if world > 1 else None
@@ -294,7 +300,8 @@ def run_gofann(args):
     # ---- roofline of the beam-search kernel (counters of the last launch)
     cnt = pipe.g_counters[:dplan.n_graph].cpu().numpy().view(np.uint32).astype(np.int64)
     avg_labels = float(idx.label_indices.numel()) / max(1, idx.n)
-    bytes_launch = beam_bytes(cnt, dplan.n_graph, idx.degree, dindex.pq_dim, avg_labels, 100)
+    table_bytes = dindex.pq_dim * 256 * 4 if args.pq_mode in A.TABLE_MODES else idx.dim
+    bytes_launch = beam_bytes(cnt, dplan.n_graph, idx.degree, dindex.pq_dim, avg_labels, 100, table_bytes)
     peaks = measured_peaks()
     achieved = bytes_launch / (beam_ms / 1e3) / 1e9
     prof = profiled_traffic()
@@ -313,7 +320,8 @@ def run_gofann(args):
                        "queue_size": chosen, "recall_at_10": round(final_recall, 4), "recall_sweep": recalls,
                        "graph_routes": dplan.n_graph, "posting_routes": dplan.n_post,
                        "graph_rows": idx.stats.get("graph_rows"), "label_graphs": idx.stats.get("groups"),
-                       "l2_flush": "inputs larger than L2 (index ~25 GB, LUTs 4.9 GB per batch)",
+                       "pq_mode": PQ_MODE_NAMES.get(args.pq_mode, str(args.pq_mode)),
+                       "l2_flush": "inputs larger than L2 (index ~25 GB resident, rows read at random)",
                        "parallelism": f"shard{world}" if world > 1 else "single"},
             "e2e": {"value": round(nq / (e_ms / 1e3), 1), "unit": "queries/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(nq * k * 8)},

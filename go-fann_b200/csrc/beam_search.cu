@@ -29,6 +29,17 @@ namespace gofann {
 namespace {
 
 constexpr int kWarpsPerBlock = 4;
+// GOFANN_PQ_U8 blocks share one packed codebook in shared memory: one large
+// block per SM (48 KB codebook + 24 warps' areas) amortises it.
+constexpr int kU8BlockWarps = 24;
+constexpr int kMaxBlockWarps = 32;  // scratch sizing bound over all variants
+
+template <int kMode>
+constexpr int block_warps() { return kMode == GOFANN_PQ_U8 ? kU8BlockWarps : kWarpsPerBlock; }
+// Blocks per SM the register budget is sized for: 24 warps where registers
+// bound the occupancy; with the table in shared memory one block fits anyway.
+template <int kMode>
+constexpr int min_blocks() { return kMode == GOFANN_PQ_U8 ? 1 : (kMode == GOFANN_PQ_LUT_SHARED ? 1 : 6); }
 // Frontier payload: local row in bits 0..29, bit 31 = expanded ("used",
 // backend_pq.cu:738-758), bit 30 = the row passed the route's DNF predicate
 // when it was admitted (recorded only with predicate bias, where the
@@ -52,7 +63,6 @@ struct WarpState {
     int serial_hash;     // 1: this step's insertions could fill the table
     uint32_t pf_row[2];  // local rows whose adjacency sits in the two prefetch slots
     int pf_last;         // slot of the most recently issued prefetch (-1: none)
-    float edge[2];       // sorted frontier: priorities merged into slots QS-1 and QS
 };
 
 struct BeamArgs {
@@ -67,10 +77,11 @@ struct BeamArgs {
     uint32_t* route_counter; // one uint32, zeroed before launch
     int32_t* status;
     uint32_t warp_smem;      // bytes of dynamic shared memory per warp
+    uint32_t block_smem;     // bytes shared by the block ahead of the warps' areas
 };
 
 struct SmemLayout {
-    uint32_t frontier, topk, stop, list, sample, dist, prio, akey, state, nadj, table, total;
+    uint32_t frontier, topk, stop, list, sample, dist, prio, state, nadj, table, total;
 };
 
 __host__ __device__ inline uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
@@ -80,22 +91,21 @@ __host__ __device__ inline SmemLayout smem_layout(const gofann_search_params& p,
 {
     SmemLayout s;
     uint32_t o = 0;
-    // frontier: the reference heap (queue_size + 3 FPair) or, in the same
-    // bytes, the sorted frontier's three arrays of queue_size + 2 words
-    s.frontier = o; o = align16(o + (p.queue_size + 3) * sizeof(FPair));
+    // frontier: the reference heap as three arrays of queue_size + 3 words
+    s.frontier = o; o = align16(o + (p.queue_size + 3) * 12);
     s.topk = o; o = align16(o + (p.result_width + 1) * sizeof(RPair));
     s.stop = o; o = align16(o + (GOFANN_MAX_TOPK + 2) * sizeof(SPair));
     s.list = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
     s.sample = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
     s.dist = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
     s.prio = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
-    s.akey = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
     s.state = o; o = align16(o + sizeof(WarpState));
     s.nadj = o; o = align16(o + 2 * GOFANN_MAX_DEGREE * 4);
     s.table = o;
     if (p.scorer == GOFANN_SCORER_PQ) {
         if (pq_mode == GOFANN_PQ_LUT_SHARED) o = align16(o + c.pq_dim * GOFANN_PQ_CENTROIDS * 4);
         if (pq_mode == GOFANN_PQ_DIRECT) o = align16(o + dim * 4);
+        if (pq_mode == GOFANN_PQ_U8) o = align16(o + dim);  // query bytes
     } else {
         o = align16(o + 8 * (c.padded_dim / 32) * 4);
     }
@@ -132,26 +142,6 @@ __device__ __forceinline__ bool stop_now(const gofann_search_params& p, const Wa
     return st.exhausted || es || step >= cap;
 }
 
-#ifdef GOFANN_DEBUG_PICKUP
-// Debug builds only: prints every pickup (run with a single route).
-__device__ void gofann_debug_pickup(const FPair* f, int size, int bi)
-{
-    printf("PICK size=%d idx=%d row=%u first=%.9g\n", size, bi,
-           bi >= 0 ? (f[bi].second & ~kPoolUsed) : 0xffffffffu, bi >= 0 ? f[bi].first : 0.f);
-    if (bi >= 0)
-        for (int i = 1; i < size; ++i)
-            if (i != bi && !(f[i].second & kPoolUsed) && !(f[i].first < f[bi].first) && !(f[bi].first < f[i].first))
-                printf("  TIE idx=%d row=%u bits=%08x vs %08x\n", i, f[i].second, __float_as_uint(f[i].first),
-                       __float_as_uint(f[bi].first));
-}
-#endif
-// Cooperative pickup (backend_pq.cu:844-893): the unused entry with the
-// smallest `first`, lowest array index on ties; lane 0 copies and marks it.
-// The order is taken as one 64-bit key (order-preserving float bits, with
-// -0 folded onto +0, above the index) reduced by an xor-shuffle min: exact
-// for every finite or infinite distance and NaN-safe.  (The reference's
-// tie clause `!(b < a) && !(a < b) && ia < ib` inside a shfl_down tree was
-// observed to keep the larger index on sm_100a with nvcc 12.9 -O3.)
 // Asynchronous copy of the adjacency row at `src` into a prefetch slot.  The
 // node expanded next is fixed one step ahead (the reference picks `next`
 // before processing `now`, backend_pq.cu:4257-4278), so its row is in flight
@@ -199,33 +189,6 @@ __device__ __forceinline__ uint32_t ordered_bits(float f)
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
-__device__ __forceinline__ bool coop_pickup(FPair* f, int size, FPair* out, int lane)
-{
-    unsigned long long best = ~0ull;
-    for (int i = lane + 1; i < size; i += kWarp) {
-        const FPair e = f[i];
-        if (e.second & kPoolUsed) continue;
-        const unsigned long long k = (static_cast<unsigned long long>(ordered_bits(e.first)) << 32) |
-                                     static_cast<uint32_t>(i);
-        best = k < best ? k : best;
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-        const unsigned long long o = __shfl_xor_sync(kFull, best, off);
-        best = o < best ? o : best;
-    }
-    const int bi = best == ~0ull ? -1 : static_cast<int>(best & 0xffffffffu);
-    if (lane == 0 && bi >= 0) {
-        *out = f[bi];
-        f[bi].second |= kPoolUsed;
-    }
-#ifdef GOFANN_DEBUG_PICKUP
-    if (lane == 0) gofann_debug_pickup(f, size, bi);
-#endif
-    __syncwarp();
-    return bi >= 0;
-}
-
 // kMode: PQ_LUT_GLOBAL / PQ_LUT_SHARED read a table row; PQ_DIRECT evaluates
 // entries from the query row (shared memory) and the codebook; kW is the
 // subvector width when it is 4 (vector loads), else 0; kMaxM bounds pq_dim.
@@ -236,12 +199,19 @@ struct Scorer {
     int dim;
     RqQueryView rq;        // RaBitQ
     uint64_t keep, stream; // L2 policies: per-route tables / streaming rows
+    const uint32_t* qw;    // PQ_U8: query words (shared memory)
+    const uint32_t* cbw;   // PQ_U8: packed codebook (shared memory)
+    int wq;                // PQ_U8: words per subvector
     __device__ __forceinline__ float operator()(const gofann_codes& c, uint32_t sample) const
     {
         if constexpr (kScorer == GOFANN_SCORER_PQ) {
             const uint8_t* code = c.pq_codes + static_cast<size_t>(sample) * c.pq_dim;
             if constexpr (kMode == GOFANN_PQ_DIRECT) {
                 return pq_adc_direct<kW, kMaxM>(lut_row, cent, dim, code, static_cast<int>(c.pq_dim), keep, stream);
+            } else if constexpr (kMode == GOFANN_PQ_U8) {
+                uint32_t cw[kMaxM / 4];
+                load_code_words<kMaxM>(code, static_cast<int>(c.pq_dim), cw, stream);
+                return pq_adc_u8<kW, kMaxM>(qw, cbw, cw, static_cast<int>(c.pq_dim), wq);
             } else {
                 uint32_t cw[kMaxM / 4];
                 load_code_words<kMaxM>(code, static_cast<int>(c.pq_dim), cw, stream);
@@ -256,218 +226,67 @@ struct Scorer {
     }
 };
 
-// ---------------------------------------------------------------------------
-// Sorted frontier (the fast path).
-//
-// With pairwise distinct priorities the reference's symmetric min-max heap
-// behaves as a set: after every admission it holds the queue_size smallest
-// entries admitted so far (insert, then pop_max once it holds queue_size+1);
-// pickup takes the smallest unused entry; a candidate is rejected exactly when
-// the heap is full and its priority is above the heap maximum.  Kept as an
-// ascending array, one step's admissions become a warp-parallel merge:
-// candidate i (list order) is admitted iff fewer than queue_size entries of
-// the frontier plus candidates before i have a smaller priority (a candidate
-// rejected earlier in the step is above the maximum at its turn, which only
-// decreases, so it is never smaller than a later admitted one), and the array
-// becomes the queue_size smallest of the frontier and the admitted
-// candidates.  Admission decisions compare priorities only, so they are the
-// same with ties; the heap's array layout decides only which of two equal
-// entries pickup returns or pop_max evicts.  The sorted array orders equal
-// priorities deterministically (frontier entries first, then candidates in
-// list order) and the fast path gives up on a route when such a choice is
-// actually made -- two unused entries tie for the smallest priority at a
-// pickup, or equal priorities straddle the queue_size boundary of a merge --
-// or when a priority is NaN; the route then runs again from the start with
-// the reference's heap (run_route<false>).
-struct SortedFrontier {
-    float* key;     // priority (`first`), ascending
-    uint32_t* val;  // local row | used bit | pass bit
-    float* base;    // unbiased score
-};
-
-// Smallest unused entry: 1 found, 0 none left, -1 another unused entry has
-// the same priority (the reference heap's layout would decide).
-__device__ __forceinline__ int sorted_pickup(const SortedFrontier& f, int n, FPair* out, int lane)
+// Cooperative pickup (backend_pq.cu:844-893): the unused entry with the
+// smallest key, lowest heap index on ties; lane 0 copies and marks it.  The
+// order is taken as one 64-bit key (order-preserving float bits, with -0
+// folded onto +0, above the index) reduced by an xor-shuffle min: exact for
+// every finite or infinite key and NaN-safe.  (The reference's tie clause
+// `!(b < a) && !(a < b) && ia < ib` inside a shfl_down tree was observed to
+// keep the larger index on sm_100a with nvcc 12.9 -O3.)
+__device__ __forceinline__ bool smmh_pickup(const Smmh& h, int size, FPair* out, int lane)
 {
-    for (int c = 0; c < n; c += kWarp) {
-        const int k = c + lane;
-        const bool unused = k < n && !(f.val[k] & kPoolUsed);
-        const unsigned m = __ballot_sync(kFull, unused);
-        if (m) {
-            const int bi = c + __ffs(m) - 1;
-            const float key = f.key[bi];
-            // equal priorities sit right after bi in the sorted array
-            const int k2 = bi + 1 + lane;
-            const bool twin = k2 < n && f.key[k2] == key && !(f.val[k2] & kPoolUsed);
-            const bool run_on = lane == kWarp - 1 && k2 < n && f.key[k2] == key;  // run may go on: be safe
-            if (__any_sync(kFull, twin || run_on)) return -1;
-            if (lane == 0) {
-                out->first = key;
-                out->second = f.val[bi];
-                out->base = f.base[bi];
-                f.val[bi] |= kPoolUsed;
-            }
-            __syncwarp();
-            return 1;
-        }
+    unsigned long long best = ~0ull;
+    for (int i = lane + 1; i < size; i += kWarp) {
+        if (h.val[i] & kPoolUsed) continue;
+        const unsigned long long k = (static_cast<unsigned long long>(ordered_bits(h.key[i])) << 32) |
+                                     static_cast<uint32_t>(i);
+        best = k < best ? k : best;
     }
-    return 0;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const unsigned long long o = __shfl_xor_sync(kFull, best, off);
+        best = o < best ? o : best;
+    }
+    const int bi = best == ~0ull ? -1 : static_cast<int>(best & 0xffffffffu);
+    if (lane == 0 && bi >= 0) {
+        out->first = h.key[bi];
+        out->second = h.val[bi];
+        out->base = h.base[bi];
+        h.val[bi] |= kPoolUsed;
+    }
+    __syncwarp();
+    return bi >= 0;
 }
 
-// Smallest priority (or unbiased score) over the unused entries.
-__device__ __forceinline__ float sorted_unused_min(const SortedFrontier& f, int n, bool use_base, int lane)
+// Smallest key (or unbiased score) over the unused entries: fminf is exact
+// and order-independent for the non-NaN values a frontier holds.
+__device__ __forceinline__ float smmh_unused_min(const Smmh& h, int size, bool use_base, int lane)
 {
     float m = FLT_MAX;
-    for (int k = lane; k < n; k += kWarp)
-        if (!(f.val[k] & kPoolUsed)) m = fminf(m, use_base ? f.base[k] : f.key[k]);
+    for (int i = lane + 1; i < size; i += kWarp)
+        if (!(h.val[i] & kPoolUsed)) m = fminf(m, use_base ? h.base[i] : h.key[i]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) m = fminf(m, __shfl_xor_sync(kFull, m, off));
     return m;
 }
 
-// Number of entries of the ascending array a[0..n) below x.
-__device__ __forceinline__ int count_below(const float* a, int n, float x)
-{
-    int lo = 0, hi = n;
-    while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        if (a[mid] < x) lo = mid + 1;
-        else hi = mid;
-    }
-    return lo;
-}
-
-// One step's admissions into the sorted frontier (see above).  Candidates
-// are list[0..len) with priorities prio[], unbiased scores dist[] and pass
-// bits pass[]; akey is 64 floats of scratch.  Writes the admitted mask to
-// adm[2] and the admitted count to n_adm.  Returns false when a NaN priority
-// or a tie across the queue_size boundary makes the result depend on the
-// reference heap's layout (the frontier is then left inconsistent: the
-// caller abandons the route).
-__device__ __forceinline__ bool sorted_admit(const SortedFrontier& f, WarpState& st, int QS, const uint32_t* list,
-                                             const float* prio, const float* dist, const uint32_t pass[2], int len,
-                                             float* akey, uint32_t adm[2], int& n_adm, int lane)
-{
-    const int n = st.heap_size - 1;
-    bool nan = false;
-    unsigned am[2];
-    int pos[2] = {0, 0};
-#pragma unroll
-    for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
-        const int i = half * kWarp + lane;
-        bool admitted = false;
-        if (i < len) {
-            const float key = prio[i];
-            if (!(key == key)) nan = true;
-            const int below = count_below(f.key, n, key);
-            int before = 0;
-            for (int j = 0; j < i; ++j) before += prio[j] < key ? 1 : 0;
-            admitted = below + before < QS;
-            // slot order among equal priorities: frontier entries first
-            int not_above = below;
-            while (not_above < n && f.key[not_above] == key) ++not_above;
-            pos[half] = not_above;
-        }
-        am[half] = __ballot_sync(kFull, admitted);
-    }
-    if (__any_sync(kFull, nan)) return false;
-    n_adm = __popc(am[0]) + __popc(am[1]);
-    adm[0] = am[0];
-    adm[1] = am[1];
-    if (n_adm == 0) return true;
-    if (lane == 0) {
-        st.edge[0] = -FLT_MAX;  // priority landing in slot QS - 1
-        st.edge[1] = FLT_MAX;   // priority landing in slot QS (evicted first)
-    }
-    __syncwarp();
-    // final slot of each admitted candidate: frontier entries not above it
-    // plus admitted candidates before it in (priority, list index) order;
-    // admitted priorities in that order into akey
-#pragma unroll
-    for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
-        const int i = half * kWarp + lane;
-        if ((am[half] >> lane) & 1u) {
-            const float key = prio[i];
-            int rank = 0;
-#pragma unroll
-            for (int h2 = 0; h2 < GOFANN_MAX_DEGREE / kWarp; ++h2) {
-                unsigned bits = am[h2];
-                while (bits) {
-                    const int j = h2 * kWarp + __ffs(bits) - 1;
-                    bits &= bits - 1;
-                    const float kj = prio[j];
-                    rank += (kj < key || (kj == key && j < i)) ? 1 : 0;
-                }
-            }
-            akey[rank] = key;
-            pos[half] += rank;
-            if (pos[half] == QS - 1) st.edge[0] = key;
-            if (pos[half] == QS) st.edge[1] = key;
-        }
-    }
-    __syncwarp();
-    // move the frontier entries up by the number of admitted candidates
-    // strictly below them, highest chunk first (every slot written was read
-    // already)
-    for (int c = (n - 1) & ~(kWarp - 1); c >= 0; c -= kWarp) {
-        const int k = c + lane;
-        float key = 0.0f, b = 0.0f;
-        uint32_t v = 0;
-        int np = QS + 1;
-        if (k < n) {
-            key = f.key[k];
-            v = f.val[k];
-            b = f.base[k];
-            np = k + count_below(akey, n_adm, key);
-            if (np == QS - 1) st.edge[0] = key;
-            if (np == QS) st.edge[1] = key;
-        }
-        __syncwarp();
-        if (np < QS) {
-            f.key[np] = key;
-            f.val[np] = v;
-            f.base[np] = b;
-        }
-        __syncwarp();
-    }
-#pragma unroll
-    for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
-        const int i = half * kWarp + lane;
-        if (((am[half] >> lane) & 1u) && pos[half] < QS) {
-            f.key[pos[half]] = prio[i];
-            f.val[pos[half]] = list[i] | (((pass[half] >> lane) & 1u) ? kPassBit : 0u);
-            f.base[pos[half]] = dist[i];
-        }
-    }
-    __syncwarp();
-    const bool tie_at_edge = n + n_adm > QS && st.edge[0] == st.edge[1];
-    if (lane == 0) st.heap_size = (n + n_adm < QS ? n + n_adm : QS) + 1;
-    __syncwarp();
-    return !tie_at_edge;
-}
-
 // Per-warp shared-memory views.
 struct WarpBufs {
-    FPair* frontier;    // reference heap (exact path)
-    SortedFrontier sf;  // sorted frontier (fast path), same bytes
+    Smmh heap;          // frontier: the reference's min-max heap, array layout
     RPair* topk;
     SPair* stopk;
     uint32_t* list;
     uint32_t* slist;
     float* dist;
     float* prio;
-    float* akey;
     WarpState* st;
     uint32_t* nadj;
     uint32_t* hash;
 };
 
-// One route from its seed to its shortlist.  kFast selects the sorted
-// frontier; it returns false when it gives up on a tie (nothing of the route
-// is final then: the caller runs the route again with kFast = false, which
-// rewrites every output).
-template <bool kFast, int kScorer, bool kBias, int kMode, int kW, int kMaxM>
-__device__ __forceinline__ bool run_route(const BeamArgs& a, const WarpBufs& w,
+// One route from its seed to its shortlist.
+template <int kScorer, bool kBias, int kMode, int kW, int kMaxM>
+__device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
                                           const Scorer<kScorer, kMode, kW, kMaxM>& score, uint32_t route,
                                           uint32_t label_offset, uint32_t begin_id, uint64_t qbit, bool pred_on,
                                           uint32_t deg, uint64_t stream, int lane)
@@ -475,8 +294,7 @@ __device__ __forceinline__ bool run_route(const BeamArgs& a, const WarpBufs& w,
     const gofann_search_params& p = a.p;
     const int QS = p.queue_size, SW = p.stop_width, RW = p.result_width;
     WarpState& st = *w.st;
-    FPair* frontier = w.frontier;
-    const SortedFrontier& sf = w.sf;
+    const Smmh& h = w.heap;
     RPair* topk = w.topk;
     SPair* stopk = w.stopk;
     uint32_t* list = w.list;
@@ -520,27 +338,17 @@ __device__ __forceinline__ bool run_route(const BeamArgs& a, const WarpBufs& w,
         kp.second = begin_id;
         kp.base = start;
         if (kBias && pred_on && pred_matches(a.routes, a.attrs, route, begin_sample)) kp.second |= kPassBit;
-        if constexpr (kFast) {
-            sf.key[0] = kp.first;
-            sf.val[0] = kp.second;
-            sf.base[0] = kp.base;
-            st.heap_size = 2;
-            st.brk = start == start ? 0 : 1;  // a NaN seed takes the exact path
-        } else {
-            smmh_insert(frontier, st.heap_size, kp);
-        }
+        h.key[1] = kp.first;  // insert into the empty heap
+        h.val[1] = kp.second;
+        h.base[1] = kp.base;
+        st.heap_size = 2;
         hash_add(hash, begin_id);
         st.hash_count = 1;
         st.pf_row[0] = st.pf_row[1] = kU32Max;
         st.pf_last = -1;
     }
     __syncwarp();
-    if constexpr (kFast) {
-        if (st.brk) return false;
-        sorted_pickup(sf, st.heap_size - 1, &st.now, lane);  // a single entry: no tie
-    } else {
-        coop_pickup(frontier, st.heap_size, &st.now, lane);
-    }
+    smmh_pickup(h, st.heap_size, &st.now, lane);
 
     int step = 0;
     for (;;) {
@@ -548,21 +356,10 @@ __device__ __forceinline__ bool run_route(const BeamArgs& a, const WarpBufs& w,
         ++step;
         if (step != 1) {
             FPair nx;
-            bool found;
+            const bool found = smmh_pickup(h, st.heap_size, &st.next, lane);
             float unused_min = FLT_MAX;
-            if constexpr (kFast) {
-                const int got = sorted_pickup(sf, st.heap_size - 1, &st.next, lane);
-                if (got < 0) {
-                    prefetch_wait_all();
-                    __syncwarp();
-                    return false;
-                }
-                found = got > 0;
-                if (found && st.stop_size == SW && p.pending_base_stop && pred_on)
-                    unused_min = sorted_unused_min(sf, st.heap_size - 1, kBias, lane);
-            } else {
-                found = coop_pickup(frontier, st.heap_size, &st.next, lane);
-            }
+            if (found && st.stop_size == SW && p.pending_base_stop && pred_on)
+                unused_min = smmh_unused_min(h, st.heap_size, kBias, lane);
             if (lane == 0) {
                 if (!found) {
                     st.exhausted = 1;
@@ -573,14 +370,7 @@ __device__ __forceinline__ bool run_route(const BeamArgs& a, const WarpBufs& w,
                     if (p.pending_base_stop && pred_on) {
                         float m = fminf(FLT_MAX, kBias ? st.now.base : st.now.first);
                         m = fminf(m, kBias ? st.next.base : st.next.first);
-                        if constexpr (kFast) {
-                            m = fminf(m, unused_min);
-                        } else {
-                            for (int i = 1; i < st.heap_size; ++i)
-                                if (!(frontier[i].second & kPoolUsed))
-                                    m = fminf(m, kBias ? frontier[i].base : frontier[i].first);
-                        }
-                        pending = m;
+                        pending = fminf(m, unused_min);
                     }
                     if (p.early_stop_mode != GOFANN_EARLY_STOP_OFF && st.stop_worst <= pending) ++st.finished;
                 }
@@ -693,11 +483,17 @@ __device__ __forceinline__ bool run_route(const BeamArgs& a, const WarpBufs& w,
         const uint32_t* adj = prefetched ? nadj + pslot * GOFANN_MAX_DEGREE
                                          : a.graph.adjacency + static_cast<size_t>(grow) * a.graph.degree;
         int len = 0;
+        uint32_t nid[GOFANN_MAX_DEGREE / kWarp];
 #pragma unroll
         for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
             const uint32_t i = half * kWarp + lane;
-            uint32_t idx = kU32Max;
-            if (i < deg) idx = prefetched ? adj[i] : ldg_u32(adj + i, stream);
+            nid[half] = kU32Max;
+            if (i < deg) nid[half] = prefetched ? adj[i] : ldg_u32(adj + i, stream);
+            if (nid[half] != kU32Max) prefetch_l1(hash + hash_code(nid[half]));
+        }
+#pragma unroll
+        for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
+            const uint32_t idx = nid[half];
             const bool keep = idx != kU32Max && !hash_test(hash, idx);
             const unsigned m = __ballot_sync(kFull, keep);
             if (keep) list[len + __popc(m & ((1u << lane) - 1u))] = idx;
@@ -718,91 +514,62 @@ __device__ __forceinline__ bool run_route(const BeamArgs& a, const WarpBufs& w,
             dist[i] = score(a.codes, s);
         }
         __syncwarp();
-        if constexpr (kFast) {
-            // priorities and pass bits; admissions as one sorted merge
-            uint32_t pbits[2];
+        // priorities, pass bits and the candidates certainly rejected (above
+        // the heap maximum while the heap is full: the maximum only
+        // decreases within a step)
+        const bool full = st.heap_size >= QS + 1;
+        const float maxv = full ? h.key[2] : 0.0f;
+        uint32_t rej[GOFANN_MAX_DEGREE / kWarp], pbits[GOFANN_MAX_DEGREE / kWarp];
 #pragma unroll
-            for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
-                const int i = half * kWarp + lane;
-                bool pass = false;
-                if (i < len) {
-                    float pr = dist[i];
-                    if (kBias && pred_on) {
-                        pass = pred_matches(a.routes, a.attrs, route, slist[i]);
-                        pr = pred_priority(dist[i], st.penalty, pass);
-                    }
-                    prio[i] = pr;
+        for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
+            const int i = half * kWarp + lane;
+            bool reject = false, pass = false;
+            if (i < len) {
+                float pr = dist[i];
+                if (kBias && pred_on) {
+                    pass = pred_matches(a.routes, a.attrs, route, slist[i]);
+                    pr = pred_priority(dist[i], st.penalty, pass);
                 }
-                pbits[half] = __ballot_sync(kFull, pass);
+                prio[i] = pr;
+                reject = full && maxv < pr;
             }
-            __syncwarp();
+            rej[half] = __ballot_sync(kFull, reject);
+            pbits[half] = __ballot_sync(kFull, pass);
+        }
+        __syncwarp();
+        // frontier admissions in list order (order dependent), the whole warp
+        // on each insert / pop_max; the visited-table insertions of the
+        // admitted rows follow, concurrently when the table cannot fill
+        {
+            int hs = st.heap_size;
             uint32_t adm[2] = {0u, 0u};
             int n_adm = 0;
-            if (!sorted_admit(sf, st, QS, list, prio, dist, pbits, len, w.akey, adm, n_adm, lane)) {
-                prefetch_wait_all();
-                __syncwarp();
-                return false;
+#pragma unroll
+            for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
+                // the candidates not rejected up front, in list order
+                const int n_here = len - half * kWarp;
+                unsigned todo = n_here <= 0 ? 0u : ~rej[half] & (n_here >= kWarp ? kFull : (1u << n_here) - 1u);
+                while (todo) {
+                    const int i = half * kWarp + __ffs(todo) - 1;
+                    todo &= todo - 1;
+                    const float key = prio[i];
+                    if (hs >= QS + 1 && h.key[2] < key) continue;
+                    const uint32_t val = list[i] | (((pbits[half] >> (i & 31)) & 1u) ? kPassBit : 0u);
+                    smmh_insert_warp(h, hs, key, val, dist[i], lane);
+                    ++hs;
+                    adm[half] |= 1u << (i & 31);
+                    ++n_adm;
+                    if (hs >= QS + 2) {
+                        smmh_pop_max_warp(h, hs, lane);
+                        --hs;
+                    }
+                }
             }
             if (lane == 0) {
+                st.heap_size = hs;
                 st.n_dist += static_cast<uint32_t>(len);
                 if (kBias && pred_on) st.n_probe += static_cast<uint32_t>(len);
                 st.n_admit += static_cast<uint32_t>(n_adm);
-                st.adm[0] = adm[0];
-                st.adm[1] = adm[1];
-                st.serial_hash = st.hash_count + n_adm > kHashCap ? 1 : 0;
-                if (st.serial_hash) {
-                    for (int i = 0; i < len; ++i)
-                        if ((adm[i >> 5] >> (i & 31)) & 1u) st.hash_count += hash_add(hash, list[i]) ? 1 : 0;
-                } else {
-                    st.hash_count += n_adm;
-                }
-            }
-            __syncwarp();
-        } else {
-            const bool full = st.heap_size >= QS + 1;
-            const float maxv = full ? frontier[2].first : 0.0f;
-#pragma unroll
-            for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
-                const int i = half * kWarp + lane;
-                bool reject = false, pass = false;
-                if (i < len) {
-                    float pr = dist[i];
-                    if (kBias && pred_on) {
-                        pass = pred_matches(a.routes, a.attrs, route, slist[i]);
-                        pr = pred_priority(dist[i], st.penalty, pass);
-                    }
-                    prio[i] = pr;
-                    reject = full && maxv < pr;  // definitely rejected (max only decreases)
-                }
-                const unsigned m = __ballot_sync(kFull, reject);
-                const unsigned pm = __ballot_sync(kFull, pass);
-                if (lane == 0) {
-                    st.rej[half] = m;
-                    st.pass[half] = pm;
-                }
-            }
-            __syncwarp();
-            // serial frontier admissions (order dependent): lane 0 runs the
-            // min-max heap; the visited-table insertions of the admitted rows
-            // follow, concurrently when the table cannot fill this step
-            if (lane == 0) {
-                st.n_dist += static_cast<uint32_t>(len);
-                if (kBias && pred_on) st.n_probe += static_cast<uint32_t>(len);
-                uint32_t adm[2] = {0u, 0u};
-                int n_adm = 0;
-                for (int i = 0; i < len; ++i) {
-                    if ((st.rej[i >> 5] >> (i & 31)) & 1u) continue;
-                    FPair kp;
-                    kp.first = prio[i];
-                    kp.base = dist[i];
-                    kp.second = list[i] | (((st.pass[i >> 5] >> (i & 31)) & 1u) ? kPassBit : 0u);
-                    if (st.heap_size >= QS + 1 && frontier[2].first < kp.first) continue;
-                    smmh_insert(frontier, st.heap_size, kp);
-                    adm[i >> 5] |= 1u << (i & 31);
-                    ++n_adm;
-                    ++st.n_admit;
-                    if (st.heap_size >= QS + 2) smmh_pop_max(frontier, st.heap_size);
-                }
                 st.adm[0] = adm[0];
                 st.adm[1] = adm[1];
                 // admitted rows are distinct and absent from the table (they
@@ -826,18 +593,7 @@ __device__ __forceinline__ bool run_route(const BeamArgs& a, const WarpBufs& w,
         }
         __syncwarp();
         if (step == 1) {
-            bool found;
-            if constexpr (kFast) {
-                const int got = sorted_pickup(sf, st.heap_size - 1, &st.next, lane);
-                if (got < 0) {
-                    prefetch_wait_all();
-                    __syncwarp();
-                    return false;
-                }
-                found = got > 0;
-            } else {
-                found = coop_pickup(frontier, st.heap_size, &st.next, lane);
-            }
+            const bool found = smmh_pickup(h, st.heap_size, &st.next, lane);
             if (lane == 0 && !found) {
                 st.exhausted = 1;
                 FPair nx;
@@ -894,31 +650,38 @@ __device__ __forceinline__ bool run_route(const BeamArgs& a, const WarpBufs& w,
         }
     }
     __syncwarp();
-    return true;
 }
 
 template <int kScorer, bool kBias, int kMode, int kW, int kMaxM>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32, 6) beam_search_kernel(BeamArgs a)
+__global__ void __launch_bounds__(block_warps<kMode>() * 32, min_blocks<kMode>()) beam_search_kernel(BeamArgs a)
 {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const gofann_search_params& p = a.p;
     const SmemLayout L = smem_layout(p, a.codes, kMode, a.prep.dim);
-    unsigned char* base = smem_raw + static_cast<size_t>(warp) * a.warp_smem;
-    const uint32_t fcap = static_cast<uint32_t>(p.queue_size) + 2;
+    if constexpr (kMode == GOFANN_PQ_U8) {
+        // the block's packed codebook, checked while it is packed
+        const bool ok = pack_u8_codebook(a.prep.pq_centroids, static_cast<int>(a.prep.dim),
+                                         static_cast<int>(a.codes.pq_dim), reinterpret_cast<uint32_t*>(smem_raw),
+                                         threadIdx.x, blockDim.x);
+        if (__syncthreads_or(!ok)) {
+            if (threadIdx.x == 0 && a.status) atomicExch(a.status, GOFANN_ERR_INVALID);
+            return;
+        }
+    }
+    unsigned char* base = smem_raw + a.block_smem + static_cast<size_t>(warp) * a.warp_smem;
+    const uint32_t fcap = static_cast<uint32_t>(p.queue_size) + 3;
     WarpBufs w;
-    w.frontier = reinterpret_cast<FPair*>(base + L.frontier);
-    w.sf.key = reinterpret_cast<float*>(base + L.frontier);
-    w.sf.val = reinterpret_cast<uint32_t*>(base + L.frontier + 4 * fcap);
-    w.sf.base = reinterpret_cast<float*>(base + L.frontier + 8 * fcap);
+    w.heap.key = reinterpret_cast<float*>(base + L.frontier);
+    w.heap.val = reinterpret_cast<uint32_t*>(base + L.frontier + 4 * fcap);
+    w.heap.base = reinterpret_cast<float*>(base + L.frontier + 8 * fcap);
     w.topk = reinterpret_cast<RPair*>(base + L.topk);
     w.stopk = reinterpret_cast<SPair*>(base + L.stop);
     w.list = reinterpret_cast<uint32_t*>(base + L.list);
     w.slist = reinterpret_cast<uint32_t*>(base + L.sample);
     w.dist = reinterpret_cast<float*>(base + L.dist);
     w.prio = reinterpret_cast<float*>(base + L.prio);
-    w.akey = reinterpret_cast<float*>(base + L.akey);
     w.st = reinterpret_cast<WarpState*>(base + L.state);
     w.nadj = reinterpret_cast<uint32_t*>(base + L.nadj);
     float* table = reinterpret_cast<float*>(base + L.table);
@@ -943,7 +706,16 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 6) beam_search_kernel(Bea
         score.keep = keep;
         score.stream = stream;
         if constexpr (kScorer == GOFANN_SCORER_PQ) {
-            if constexpr (kMode == GOFANN_PQ_DIRECT) {
+            if constexpr (kMode == GOFANN_PQ_U8) {
+                const int nw = static_cast<int>(a.prep.dim) / 4;
+                const uint32_t* qr = reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(a.prep.pq_query) +
+                                                                       static_cast<size_t>(row) * a.prep.dim);
+                uint32_t* qw = reinterpret_cast<uint32_t*>(table);
+                for (int i = lane; i < nw; i += kWarp) qw[i] = qr[i];
+                score.qw = qw;
+                score.cbw = reinterpret_cast<const uint32_t*>(smem_raw);
+                score.wq = static_cast<int>(a.prep.dim / a.codes.pq_dim) / 4;
+            } else if constexpr (kMode == GOFANN_PQ_DIRECT) {
                 const int dim = static_cast<int>(a.prep.dim);
                 if (a.prep.pq_query_dtype == GOFANN_DTYPE_U8) {
                     const uint8_t* qr = static_cast<const uint8_t*>(a.prep.pq_query) + static_cast<size_t>(row) * dim;
@@ -978,8 +750,8 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 6) beam_search_kernel(Bea
         }
         __syncwarp();
 
-        if (!run_route<true, kScorer, kBias, kMode, kW, kMaxM>(a, w, score, route, label_offset, begin_id, qbit, pred_on, deg, stream, lane))
-            run_route<false, kScorer, kBias, kMode, kW, kMaxM>(a, w, score, route, label_offset, begin_id, qbit, pred_on, deg, stream, lane);
+        run_route<kScorer, kBias, kMode, kW, kMaxM>(a, w, score, route, label_offset, begin_id, qbit, pred_on, deg,
+                                                    stream, lane);
     }
 }
 
@@ -993,6 +765,12 @@ KernelFn pick_pq(int mode, bool w4, bool small_m)
                                : beam_search_kernel<0, kBias, GOFANN_PQ_DIRECT, 4, 128>;
         return small_m ? beam_search_kernel<0, kBias, GOFANN_PQ_DIRECT, 0, 64>
                        : beam_search_kernel<0, kBias, GOFANN_PQ_DIRECT, 0, 128>;
+    }
+    if (mode == GOFANN_PQ_U8) {
+        if (w4) return small_m ? beam_search_kernel<0, kBias, GOFANN_PQ_U8, 4, 64>
+                               : beam_search_kernel<0, kBias, GOFANN_PQ_U8, 4, 128>;
+        return small_m ? beam_search_kernel<0, kBias, GOFANN_PQ_U8, 0, 64>
+                       : beam_search_kernel<0, kBias, GOFANN_PQ_U8, 0, 128>;
     }
     if (mode == GOFANN_PQ_LUT_SHARED)
         return small_m ? beam_search_kernel<0, kBias, GOFANN_PQ_LUT_SHARED, 0, 64>
@@ -1024,6 +802,17 @@ int check_pq_mode(const gofann_search_params& p, const gofann_codes& c, const go
             return fail(GOFANN_ERR_INVALID, "%s: pq_query_dtype must be u8 or f32", who);
         if (prep.dim > 4096) return fail(GOFANN_ERR_UNSUPPORTED, "%s: dim %u above 4096", who, prep.dim);
         w4 = prep.dim / c.pq_dim == 4 && (reinterpret_cast<uintptr_t>(prep.pq_centroids) & 15) == 0;
+        return GOFANN_OK;
+    }
+    if (p.pq_mode == GOFANN_PQ_U8) {
+        if (!prep.pq_query || !prep.pq_centroids || prep.pq_query_dtype != GOFANN_DTYPE_U8 || prep.dim == 0 ||
+            prep.dim % c.pq_dim != 0 || (prep.dim / c.pq_dim) % 4 != 0)
+            return fail(GOFANN_ERR_INVALID,
+                        "%s: u8 PQ scoring needs u8 pq_query, pq_centroids and dim / pq_dim a multiple of 4", who);
+        if ((reinterpret_cast<uintptr_t>(prep.pq_query) & 3) != 0)
+            return fail(GOFANN_ERR_INVALID, "%s: pq_query must be 4-byte aligned", who);
+        if (prep.dim > 256) return fail(GOFANN_ERR_UNSUPPORTED, "%s: u8 PQ scoring needs dim <= 256", who);
+        w4 = prep.dim / c.pq_dim == 4;
         return GOFANN_OK;
     }
     if (p.pq_mode != GOFANN_PQ_LUT_GLOBAL && p.pq_mode != GOFANN_PQ_LUT_SHARED)
@@ -1079,10 +868,11 @@ size_t gofann_beam_search_scratch_bytes(uint32_t n_routes)
     // Upper bound over variants: one table per warp of the persistent grid,
     // which never exceeds one warp per route nor 64 warps per SM.
     const uint32_t sms = static_cast<uint32_t>(sm_count() > 0 ? sm_count() : 148);
-    uint64_t warps = (static_cast<uint64_t>(n_routes) + kWarpsPerBlock - 1) / kWarpsPerBlock * kWarpsPerBlock;
+    // (the last block of a grid of ceil(n_routes / wpb) blocks adds < wpb warps)
+    uint64_t warps = static_cast<uint64_t>(n_routes) + kMaxBlockWarps - 1;
     const uint64_t cap = static_cast<uint64_t>(sms) * 64;
     if (warps > cap) warps = cap;
-    if (warps == 0) warps = kWarpsPerBlock;
+    if (warps == 0) warps = kMaxBlockWarps;
     return kCounterBytes + warps * kHashCap * sizeof(uint32_t);
 }
 
@@ -1152,10 +942,14 @@ int gofann_beam_search(const gofann_graph* graph, const gofann_attrs* attrs, con
     args.status = out->status;
     const SmemLayout L = smem_layout(p, *codes, pq_mode, prep->dim);
     args.warp_smem = L.total;
+    // GOFANN_PQ_U8: the packed codebook ahead of the warps' areas
+    args.block_smem = pq_mode == GOFANN_PQ_U8 && p.scorer == GOFANN_SCORER_PQ
+                          ? static_cast<uint32_t>(codes->pq_dim * GOFANN_PQ_CENTROIDS * (prep->dim / codes->pq_dim))
+                          : 0u;
     constexpr size_t kMaxSmem = 227 * 1024;
-    int wpb = kWarpsPerBlock;
-    while (wpb > 1 && static_cast<size_t>(L.total) * wpb > kMaxSmem) --wpb;
-    const size_t smem = static_cast<size_t>(L.total) * wpb;
+    int wpb = pq_mode == GOFANN_PQ_U8 && p.scorer == GOFANN_SCORER_PQ ? kU8BlockWarps : kWarpsPerBlock;
+    while (wpb > 1 && args.block_smem + static_cast<size_t>(L.total) * wpb > kMaxSmem) --wpb;
+    const size_t smem = args.block_smem + static_cast<size_t>(L.total) * wpb;
     if (smem > kMaxSmem)
         return fail(GOFANN_ERR_UNSUPPORTED, "beam_search: %zu bytes of shared memory per warp exceed 227 KB", smem);
     const bool bias = p.predicate_bias != 0;
@@ -1319,10 +1113,14 @@ int gofann_beam_search_noalloc(const gofann_graph* graph, const gofann_attrs* at
     args.status = out->status;
     const SmemLayout L = smem_layout(p, *codes, pq_mode, prep->dim);
     args.warp_smem = L.total;
+    // GOFANN_PQ_U8: the packed codebook ahead of the warps' areas
+    args.block_smem = pq_mode == GOFANN_PQ_U8 && p.scorer == GOFANN_SCORER_PQ
+                          ? static_cast<uint32_t>(codes->pq_dim * GOFANN_PQ_CENTROIDS * (prep->dim / codes->pq_dim))
+                          : 0u;
     constexpr size_t kMaxSmem = 227 * 1024;
-    int wpb = kWarpsPerBlock;
-    while (wpb > 1 && static_cast<size_t>(L.total) * wpb > kMaxSmem) --wpb;
-    const size_t smem = static_cast<size_t>(L.total) * wpb;
+    int wpb = pq_mode == GOFANN_PQ_U8 && p.scorer == GOFANN_SCORER_PQ ? kU8BlockWarps : kWarpsPerBlock;
+    while (wpb > 1 && args.block_smem + static_cast<size_t>(L.total) * wpb > kMaxSmem) --wpb;
+    const size_t smem = args.block_smem + static_cast<size_t>(L.total) * wpb;
     if (smem > kMaxSmem)
         return fail(GOFANN_ERR_UNSUPPORTED, "beam_search_noalloc: %zu bytes of shared memory per warp exceed 227 KB",
                     smem);

@@ -89,6 +89,14 @@ __device__ __forceinline__ uint4 ldg_u32x4(const uint4* p, uint64_t pol)
     return v;
 }
 
+// Non-blocking fetch of the line holding p into L1 (PTX prefetch): issued for
+// every candidate of a step before any of them is evaluated, so that their
+// dependent loads overlap instead of running one candidate after another.
+__device__ __forceinline__ void prefetch_l1(const void* p)
+{
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
 // --------------------------------------------------- float order helpers
 // Lane-0 value of `v += __shfl_xor_sync(v, off)` for off = 16..1, replayed
 // inside one thread from the 32 lane partials (backend_pq.cu:4716-4721).
@@ -224,6 +232,138 @@ __device__ __forceinline__ void smmh_pop_max(FPair* h, int& size)
         if (x == y) break;
         y = x;
     }
+}
+
+// The same heap stored as three arrays (key = `first`, val = payload, base =
+// unbiased score) and operated on by a whole warp.  Every lane runs the
+// same, warp-uniform sequence of the reference's decisions on broadcast
+// shared-memory reads; lane 0 writes.  Only the fetching is parallel:
+//   * insert: the new element climbs the chain of ancestor pairs fixed by
+//     its leaf position; at each pair the reference compares it strictly with
+//     the left (min) element, then the right (max) one, and once it moves up
+//     one side it can never satisfy the other side's test again (the heap
+//     order), so lane j reads the pair j levels up, a ballot over "strictly
+//     below the left" (or "strictly above the right") gives the number of
+//     levels climbed -- the leading passed levels, exactly where the
+//     reference stops -- and the displaced elements move down one level
+//     together;
+//   * pop_max: the sift-down stays sequential (each level depends on the
+//     previous one); the moving element lives in registers and a level's
+//     sibling and child entries are read together.
+struct Smmh {
+    float* key;
+    uint32_t* val;
+    float* base;
+};
+
+// Inserts (ek, ev, eb) into a heap whose next free index is `size` (entries
+// + 1); the caller increments its size.
+__device__ __forceinline__ void smmh_insert_warp(const Smmh& h, int size, float ek, uint32_t ev, float eb, int lane)
+{
+    int y = size;
+    if ((y & 1) == 0) {  // adjust_sibling at the leaf: a right child below its left sibling swaps
+        const float sk = h.key[y - 1];
+        if (ek < sk) {
+            if (lane == 0) {
+                h.key[y] = sk;
+                h.val[y] = h.val[y - 1];
+                h.base[y] = h.base[y - 1];
+            }
+            y -= 1;
+        }
+    }
+    if (y > 2) {
+        const int p0 = (y - 1) >> 1;              // pair of y; pair P's elements are 2P+1, 2P+2
+        const int levels = 31 - __clz(p0 + 1);    // ancestor pairs above it
+        bool up_min = false, up_max = false;
+        if (lane >= 1 && lane <= levels) {
+            const int P = ((p0 + 1) >> lane) - 1;
+            up_min = h.key[2 * P + 1] > ek;
+            up_max = h.key[2 * P + 2] < ek;
+        }
+        const unsigned bmin = __ballot_sync(kFull, up_min) >> 1;  // bit j-1: pair j levels up
+        const unsigned bmax = __ballot_sync(kFull, up_max) >> 1;
+        int side = 0;
+        unsigned passed = 0;
+        if (bmin & 1u) { side = 1; passed = bmin; }
+        else if (bmax & 1u) { side = 2; passed = bmax; }
+        if (side != 0) {
+            const int climb = __ffs(~passed) - 1;
+            const bool mover = lane >= 1 && lane <= climb;
+            float mk = 0.0f, mb = 0.0f;
+            uint32_t mv = 0;
+            int dst = 0;
+            if (mover) {
+                const int src = 2 * (((p0 + 1) >> lane) - 1) + side;
+                mk = h.key[src];
+                mv = h.val[src];
+                mb = h.base[src];
+                dst = lane == 1 ? y : 2 * (((p0 + 1) >> (lane - 1)) - 1) + side;
+            }
+            __syncwarp();
+            if (mover) {
+                h.key[dst] = mk;
+                h.val[dst] = mv;
+                h.base[dst] = mb;
+            }
+            y = 2 * (((p0 + 1) >> climb) - 1) + side;
+        }
+    }
+    __syncwarp();
+    if (lane == 0) {
+        h.key[y] = ek;
+        h.val[y] = ev;
+        h.base[y] = eb;
+    }
+    __syncwarp();
+}
+
+// Removes the maximum (index 2) of a heap of `size` - 1 entries; the caller
+// decrements its size.  Needs at least 3 entries (`size` >= 4), which the
+// traversal guarantees (it pops only above queue_size + 1 >= 3 entries).
+__device__ __forceinline__ void smmh_pop_max_warp(const Smmh& h, int size, int lane)
+{
+    --size;
+    float ck = h.key[size];  // h[2] = h[--size]
+    uint32_t cv = h.val[size];
+    float cb = h.base[size];
+    int y = 2;  // stays a right (even) index
+    for (;;) {
+        const int s = y - 1, cl = 2 * y, cr = 2 * y + 2;
+        const float sk = h.key[s];
+        const uint32_t sv = h.val[s];
+        const float sb = h.base[s];
+        float lk = 0.0f, lb = 0.0f, rk = 0.0f, rb = 0.0f;
+        uint32_t lv = 0, rv = 0;
+        if (cl < size) { lk = h.key[cl]; lv = h.val[cl]; lb = h.base[cl]; }
+        if (cr < size) { rk = h.key[cr]; rv = h.val[cr]; rb = h.base[cr]; }
+        // adjust_sibling (the reference's pop_max ignores the index it returns)
+        if (ck < sk) {
+            if (lane == 0) {
+                h.key[s] = ck;
+                h.val[s] = cv;
+                h.base[s] = cb;
+            }
+            ck = sk; cv = sv; cb = sb;
+        }
+        // adjust_grandchild: the larger right child of the two child pairs
+        if (cl >= size) break;
+        bool right = cr < size && rk > lk;
+        const float chk = right ? rk : lk;
+        if (!(chk > ck)) break;
+        if (lane == 0) {
+            h.key[y] = chk;
+            h.val[y] = right ? rv : lv;
+            h.base[y] = right ? rb : lb;
+        }
+        y = right ? cr : cl;
+    }
+    if (lane == 0) {
+        h.key[y] = ck;
+        h.val[y] = cv;
+        h.base[y] = cb;
+    }
+    __syncwarp();
 }
 
 // -------------------------------------------------------- binary max heaps

@@ -163,6 +163,59 @@ __device__ __forceinline__ float pq_adc_direct(const float* q, const float* __re
     return butterfly_sum32(v);
 }
 
+// Packed codebook for GOFANN_PQ_U8: word (m * 256 + c) * wq + t holds the
+// bytes of centroid c's subvector m, dimensions 4t..4t+3 (wq = w / 4).
+// Returns false when a centroid value is not an integer in 0..255.
+__device__ __forceinline__ bool pack_u8_codebook(const float* __restrict__ cent, int dim, int pq_dim,
+                                                 uint32_t* cbw, int tid, int nthreads)
+{
+    const int w = dim / pq_dim, wq = w / 4;
+    const int words = pq_dim * GOFANN_PQ_CENTROIDS * wq;
+    bool ok = true;
+    for (int i = tid; i < words; i += nthreads) {
+        const int t = i % wq, mc = i / wq;
+        const int c = mc % GOFANN_PQ_CENTROIDS, m = mc / GOFANN_PQ_CENTROIDS;
+        const float* src = cent + static_cast<size_t>(c) * dim + m * w + 4 * t;
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const float v = src[b];
+            ok = ok && v >= 0.0f && v <= 255.0f && v == rintf(v);
+            word |= (static_cast<uint32_t>(v >= 0.0f && v <= 255.0f ? v : 0.0f) & 0xffu) << (8 * b);
+        }
+        cbw[i] = word;
+    }
+    return ok;
+}
+
+// GOFANN_PQ_U8 distance: sum over subspaces of |q - c|^2 per byte, as an
+// integer (at most 4096 * 255^2 < 2^32; below 2^24 for dim <= 258, where it
+// equals the reference's float ADC bit for bit).  qw: query words
+// [pq_dim * wq] (shared memory), cbw: packed codebook (shared memory).
+template <int kW, int kMaxM>
+__device__ __forceinline__ float pq_adc_u8(const uint32_t* qw, const uint32_t* cbw, const uint32_t (&cw)[kMaxM / 4],
+                                           int pq_dim, int wq)
+{
+    uint32_t acc = 0;
+#pragma unroll
+    for (int m = 0; m < kMaxM; ++m) {
+        if (m < pq_dim) {
+            const uint32_t c = code_byte(cw, m);
+            if constexpr (kW == 4) {
+                const uint32_t d = __vabsdiffu4(qw[m], cbw[m * GOFANN_PQ_CENTROIDS + c]);
+                acc = __dp4a(d, d, acc);
+            } else {
+                const uint32_t* e = cbw + (m * GOFANN_PQ_CENTROIDS + c) * wq;
+                for (int t = 0; t < wq; ++t) {
+                    const uint32_t d = __vabsdiffu4(qw[m * wq + t], e[t]);
+                    acc = __dp4a(d, d, acc);
+                }
+            }
+        }
+    }
+    return __uint2float_rn(acc);
+}
+
 // Posting-scan order: sequential over subspaces (backend_pq.cu:2101-2104).
 __device__ __forceinline__ float pq_adc_sequential(const float* lut_row, const uint8_t* code, int pq_dim)
 {

@@ -21,7 +21,8 @@ ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_CAPACITY, ERR_TIMEOUT = -1, -2, -3, 
 EARLY_STOP_FIXED, EARLY_STOP_OFF, EARLY_STOP_ADAPTIVE = 0, 1, 2
 SCORER_PQ, SCORER_RABITQ = 0, 1
 DTYPE_U8, DTYPE_F32, DTYPE_F16 = 0, 1, 2
-PQ_LUT_GLOBAL, PQ_LUT_SHARED, PQ_DIRECT = 0, 1, 2
+PQ_LUT_GLOBAL, PQ_LUT_SHARED, PQ_DIRECT, PQ_U8 = 0, 1, 2, 3
+TABLE_MODES = (PQ_LUT_GLOBAL, PQ_LUT_SHARED)  # modes that read a per-query table batch
 MAX_DEGREE, MAX_QUEUE, MAX_TOPK, MAX_RESULT_WIDTH, MAX_SHORTLIST = 64, 512, 10, 512, 400
 PQ_CENTROIDS, HASH_CAPACITY = 256, 4096
 U32MAX = 0xFFFFFFFF

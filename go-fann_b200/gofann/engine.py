@@ -126,7 +126,7 @@ class Pipeline:
         rw, sl, k = cfg.result_width, cfg.lowfreq_shortlist, cfg.topk
         # a per-query table batch is only materialised for the table modes
         self.lut = (torch.empty((nq, dindex.pq_dim, A.PQ_CENTROIDS), dtype=torch.float32, device=d)
-                    if cfg.pq_mode != A.PQ_DIRECT else None)
+                    if cfg.pq_mode in A.TABLE_MODES else None)
         self.g_ids = torch.empty((max(ng, 1), rw), dtype=torch.int32, device=d)
         self.g_d = torch.empty((max(ng, 1), rw), dtype=torch.float32, device=d)
         self.g_steps = torch.empty(max(ng, 1), dtype=torch.int32, device=d)
@@ -146,7 +146,7 @@ class Pipeline:
         self.params = cfg.params(A.SCORER_PQ)
         self.out_s = A.SearchOut(ids=A.ptr(self.g_ids), dists=A.ptr(self.g_d), steps=A.ptr(self.g_steps),
                                  counters=A.ptr(self.g_counters), status=A.ptr(self.status))
-        self.launches_per_run = ((1 if cfg.pq_mode != A.PQ_DIRECT else 0) + 2 * (1 if ng else 0) +
+        self.launches_per_run = ((1 if cfg.pq_mode in A.TABLE_MODES else 0) + 2 * (1 if ng else 0) +
                                  2 * (1 if npo else 0) + 1)
 
     # -- individual stages (device pointers, current stream) --------------
@@ -155,14 +155,14 @@ class Pipeline:
         if queries is self.queries:
             return
         self.queries = queries
-        if self.cfg.pq_mode == A.PQ_DIRECT:
+        if self.cfg.pq_mode not in A.TABLE_MODES:
             self.prep = {"pq_query": queries, "pq_centroids": self.di.pq_centroids}
         else:
             self.prep = {"pq_lut": self.lut}
         self.prep_s = A.fill_prepared(self.prep)
 
     def build_lut(self, queries: torch.Tensor, stream=None):
-        """Table build for the table modes (a no-op in PQ_DIRECT)."""
+        """Table build for the table modes (a no-op in PQ_DIRECT and PQ_U8)."""
         self.set_queries(queries)
         if self.lut is None:
             return

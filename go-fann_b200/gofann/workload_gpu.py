@@ -251,7 +251,9 @@ def build_index(data: dict, threshold=2000, degree=64, n_random=40, pq_dim=48, s
     prev_tf32 = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = True  # exact for uint8 inputs
     try:
-        cent = train_pq_gpu(base, pq_dim, seed)
+        # codebook values rounded to integers in 0..255: with u8 queries every
+        # table entry and ADC sum is then an exact integer (GOFANN_PQ_U8)
+        cent = train_pq_gpu(base, pq_dim, seed).round_().clamp_(0, 255)
         codes = torch.empty((n, pq_dim), dtype=torch.uint8, device=dev)
         if torch_encode:
             w = dim // pq_dim

@@ -70,8 +70,16 @@ enum { GOFANN_SCORER_PQ = 0, GOFANN_SCORER_RABITQ = 1 };
 enum { GOFANN_DTYPE_U8 = 0, GOFANN_DTYPE_F32 = 1, GOFANN_DTYPE_F16 = 2 };
 /* PQ scoring inside the traversal: read a prebuilt LUT from global memory,
  * stage it in shared memory per route, or evaluate each table entry from the
- * query and the codebook where it is used (no per-query table at all). */
-enum { GOFANN_PQ_LUT_GLOBAL = 0, GOFANN_PQ_LUT_SHARED = 1, GOFANN_PQ_DIRECT = 2 };
+ * query and the codebook where it is used (no per-query table at all).
+ * GOFANN_PQ_U8: u8 queries and a codebook whose values are integers in
+ * 0..255 (checked on the device: any other value sets the status word to
+ * GOFANN_ERR_INVALID and nothing is searched).  Every table entry and every
+ * partial sum of the reference's float ADC is then an integer below 2^24,
+ * exact in float whatever the order, so the distance is scored as an integer
+ * sum of byte differences (absolute difference + dot product of packed
+ * bytes) against a packed copy of the codebook in shared memory: the same
+ * bits as the table modes, no per-query table. */
+enum { GOFANN_PQ_LUT_GLOBAL = 0, GOFANN_PQ_LUT_SHARED = 1, GOFANN_PQ_DIRECT = 2, GOFANN_PQ_U8 = 3 };
 
 /* DNF clause over label handles and range atoms (gpu_predicate_index.cuh:24-25). */
 typedef struct gofann_clause {
@@ -179,7 +187,7 @@ typedef struct gofann_search_params {
     float alpha;             /* predicate_bias_alpha */
     int32_t pending_base_stop;
     int32_t full_label_check;     /* 1 = resident residual label check on expansion */
-    int32_t pq_mode;              /* PQ scoring: GOFANN_PQ_LUT_GLOBAL, _LUT_SHARED or _DIRECT */
+    int32_t pq_mode;              /* PQ scoring: GOFANN_PQ_LUT_GLOBAL, _LUT_SHARED, _DIRECT or _U8 */
     int32_t resident_warps;       /* cap on concurrently running routes (warps) of the persistent
                                      grid; 0 = automatic: as many as fit on the SMs, reduced in
                                      GOFANN_PQ_LUT_GLOBAL mode so that the per-route tables in

@@ -1,6 +1,7 @@
 """Shared seeded test workloads (small enough for the CPU oracle)."""
 from __future__ import annotations
 
+import copy
 import functools
 
 import numpy as np
@@ -23,6 +24,19 @@ def cfg2_small(n=5000, vocab=120, n_queries=160, threshold=300, degree=64, pq_di
     idx = index_build.build_index(w, threshold=threshold, degree=degree, pq_dim=pq_dim, seed=seed)
     plan = planner.plan_queries(idx, w.query_labels)
     return w, idx, plan
+
+
+@functools.lru_cache(maxsize=None)
+def cfg2_small_u8cb():
+    """cfg2_small with its codebook rounded to integers in 0..255 and the
+    codes re-encoded against it: the preconditions of GOFANN_PQ_U8."""
+    from oracle import oracle as O
+    w, idx, plan = cfg2_small()
+    cent = np.clip(np.rint(idx.pq_centroids), 0, 255).astype(np.float32)
+    idx2 = copy.copy(idx)
+    idx2.pq_centroids = cent
+    idx2.pq_codes = O.pq_encode(w.base.astype(np.float32), cent, idx.pq_codes.shape[1])
+    return w, idx2, plan
 
 
 def random_orthogonal(p: int, seed: int) -> np.ndarray:

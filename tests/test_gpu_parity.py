@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 import torch
 
-from fixtures import cfg1_small, cfg2_small, dev, dev_dict, fbits, host, rabitq_artifacts
+from fixtures import cfg1_small, cfg2_small, cfg2_small_u8cb, dev, dev_dict, fbits, host, rabitq_artifacts
 from gofann import _abi as A
 from oracle import oracle as O
 
@@ -163,7 +163,7 @@ def test_rabitq_score_bitexact(L):
 
 
 # ----------------------------------------------------------- traversal
-def run_gpu_beam(L, graph, attrs, codes, prep, routes, trace_width=0, **params):
+def run_gpu_beam(L, graph, attrs, codes, prep, routes, trace_width=0, expect_status=0, **params):
     dg, da, dc, dp, dr = dev_dict(graph), dev_dict(attrs), dev_dict(codes), prep, dev_dict(routes)
     gs, at, cs, ps, rs = A.fill_graph(dg), A.fill_attrs(da), A.fill_codes(dc), A.fill_prepared(dp), A.fill_routes(dr)
     sp = A.fill_params(**params)
@@ -181,7 +181,7 @@ def run_gpu_beam(L, graph, attrs, codes, prep, routes, trace_width=0, **params):
     A.check(L.gofann_beam_search(C.byref(gs), C.byref(at), C.byref(cs), C.byref(ps), C.byref(rs), C.byref(sp),
                                  C.byref(out), A.ptr(scratch), nbytes, stream()), "beam_search")
     torch.cuda.synchronize()
-    assert int(status.item()) == 0
+    assert int(status.item()) == expect_status
     res = (host(ids, np.uint32), d.cpu().numpy(), steps.cpu().numpy(), host(cnt, np.uint32))
     if trace_width:
         return res + (host(trace, np.uint32),)
@@ -208,7 +208,7 @@ BEAM_VARIANTS = [
 
 def pq_prep(w, idx, mode):
     """Device prepared state for a PQ mode: the LUT batch, or query rows + codebook."""
-    if mode == A.PQ_DIRECT:
+    if mode in (A.PQ_DIRECT, A.PQ_U8):
         return {"pq_query": dev(w.queries), "pq_centroids": dev(idx.pq_centroids)}
     return {"pq_lut": dev(O.pq_build_lut(w.queries.astype(np.float32), idx.pq_centroids, idx.pq_codes.shape[1]))}
 
@@ -227,6 +227,35 @@ def test_beam_search_pq_bitexact(L, wl, vi):
         if name == "dists":
             g, o = fbits(g), fbits(o)
         assert np.array_equal(g, o), f"{name} differ in {np.count_nonzero(np.any(np.atleast_2d(g != o), axis=-1))} routes"
+
+
+@pytest.mark.parametrize("vi", range(len(BEAM_VARIANTS)))
+def test_beam_search_pq_u8_bitexact(L, vi):
+    """GOFANN_PQ_U8 (integer codebook, u8 queries) against the oracle's float
+    table + float ADC on the same codebook: the same bits.  Integer
+    distances tie often, so the exact-heap fallback runs here too."""
+    w, idx, plan = cfg2_small_u8cb()
+    params = dict(BEAM_VARIANTS[vi], scorer=A.SCORER_PQ, pq_mode=A.PQ_U8)
+    lut = O.pq_build_lut(w.queries.astype(np.float32), idx.pq_centroids, idx.pq_codes.shape[1])
+    want = O.beam_search(idx.graph(), idx.attrs(), idx.codes(), {"pq_lut": lut}, plan.graph_routes, threads=8,
+                         trace_width=64, **params)
+    got = run_gpu_beam(L, idx.graph(), idx.attrs(), idx.codes(), pq_prep(w, idx, A.PQ_U8), plan.graph_routes,
+                       trace_width=64, **params)
+    for name, g, o in zip(("ids", "dists", "steps", "counters", "trace"), got, want):
+        if name == "dists":
+            g, o = fbits(g), fbits(o)
+        assert np.array_equal(g, o), f"{name} differ in {np.count_nonzero(np.any(np.atleast_2d(g != o), axis=-1))} routes"
+
+
+def test_beam_search_pq_u8_rejects_fractional_codebook(L):
+    """A codebook value that is not an integer in 0..255 sets the status word
+    to GOFANN_ERR_INVALID (checked on the device) instead of searching."""
+    w, idx, plan = cfg2_small_u8cb()
+    cent = idx.pq_centroids.copy()
+    cent[17, 5] += 0.5
+    params = dict(BEAM_VARIANTS[1], scorer=A.SCORER_PQ, pq_mode=A.PQ_U8)
+    run_gpu_beam(L, idx.graph(), idx.attrs(), idx.codes(), {"pq_query": dev(w.queries), "pq_centroids": dev(cent)},
+                 plan.graph_routes, expect_status=A.ERR_INVALID, **params)
 
 
 @pytest.mark.parametrize("share", [2, 20])
