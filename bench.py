@@ -304,10 +304,12 @@ def run_gofann(args):
     bytes_launch = beam_bytes(cnt, dplan.n_graph, idx.degree, dindex.pq_dim, avg_labels, 100, table_bytes)
     peaks = measured_peaks()
     achieved = bytes_launch / (beam_ms / 1e3) / 1e9
+    # DRAM bytes per launch: the ncu capture of a small case of the same
+    # kernel, scaled by algorithmic bytes (profiles/beam_search_config2_traffic.json)
     prof = profiled_traffic()
     traffic = None
-    if prof and prof.get("workload") == f"config2_n{args.n}_q{args.queries}" and prof.get("queue_size") == chosen:
-        traffic = prof.get("bytes_per_launch")
+    if prof and prof.get("pq_mode") == PQ_MODE_NAMES.get(args.pq_mode):
+        traffic = int(prof["traffic_per_algorithmic_byte"] * bytes_launch)
 
     if rank == 0:
         final_recall = W.recall_at_k(final_pred, gt, k)
