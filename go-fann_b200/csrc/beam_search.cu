@@ -209,9 +209,13 @@ struct Scorer {
             if constexpr (kMode == GOFANN_PQ_DIRECT) {
                 return pq_adc_direct<kW, kMaxM>(lut_row, cent, dim, code, static_cast<int>(c.pq_dim), keep, stream);
             } else if constexpr (kMode == GOFANN_PQ_U8) {
-                uint32_t cw[kMaxM / 4];
-                load_code_words<kMaxM>(code, static_cast<int>(c.pq_dim), cw, stream);
-                return pq_adc_u8<kW, kMaxM>(qw, cbw, cw, static_cast<int>(c.pq_dim), wq);
+                if constexpr (kW == 4) {  // 4-wide subvectors, pq_dim a multiple of 16 (host-checked)
+                    return pq_adc_u8_chunked(qw, cbw, code, static_cast<int>(c.pq_dim), stream);
+                } else {
+                    uint32_t cw[kMaxM / 4];
+                    load_code_words<kMaxM>(code, static_cast<int>(c.pq_dim), cw, stream);
+                    return pq_adc_u8<kMaxM>(qw, cbw, cw, static_cast<int>(c.pq_dim), wq);
+                }
             } else {
                 uint32_t cw[kMaxM / 4];
                 load_code_words<kMaxM>(code, static_cast<int>(c.pq_dim), cw, stream);
@@ -519,9 +523,8 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
         // decreases within a step)
         const bool full = st.heap_size >= QS + 1;
         const float maxv = full ? h.key[2] : 0.0f;
-        uint32_t rej[GOFANN_MAX_DEGREE / kWarp], pbits[GOFANN_MAX_DEGREE / kWarp];
-#pragma unroll
-        for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
+#pragma unroll 1
+        for (int half = 0; half < (len + kWarp - 1) / kWarp; ++half) {
             const int i = half * kWarp + lane;
             bool reject = false, pass = false;
             if (i < len) {
@@ -533,10 +536,16 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
                 prio[i] = pr;
                 reject = full && maxv < pr;
             }
-            rej[half] = __ballot_sync(kFull, reject);
-            pbits[half] = __ballot_sync(kFull, pass);
+            const unsigned rm = __ballot_sync(kFull, reject);
+            const unsigned pm = __ballot_sync(kFull, pass);
+            if (lane == 0) {
+                st.rej[half] = rm;
+                st.pass[half] = pm;
+            }
         }
         __syncwarp();
+        const uint32_t rej[2] = {st.rej[0], len > kWarp ? st.rej[1] : 0u};
+        const uint32_t pbits[2] = {st.pass[0], len > kWarp ? st.pass[1] : 0u};
         // frontier admissions in list order (order dependent), the whole warp
         // on each insert / pop_max; the visited-table insertions of the
         // admitted rows follow, concurrently when the table cannot fill
@@ -812,7 +821,7 @@ int check_pq_mode(const gofann_search_params& p, const gofann_codes& c, const go
         if ((reinterpret_cast<uintptr_t>(prep.pq_query) & 3) != 0)
             return fail(GOFANN_ERR_INVALID, "%s: pq_query must be 4-byte aligned", who);
         if (prep.dim > 256) return fail(GOFANN_ERR_UNSUPPORTED, "%s: u8 PQ scoring needs dim <= 256", who);
-        w4 = prep.dim / c.pq_dim == 4;
+        w4 = prep.dim / c.pq_dim == 4 && c.pq_dim % 16 == 0;  // the chunked scorer
         return GOFANN_OK;
     }
     if (p.pq_mode != GOFANN_PQ_LUT_GLOBAL && p.pq_mode != GOFANN_PQ_LUT_SHARED)

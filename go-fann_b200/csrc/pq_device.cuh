@@ -192,7 +192,7 @@ __device__ __forceinline__ bool pack_u8_codebook(const float* __restrict__ cent,
 // integer (at most 4096 * 255^2 < 2^32; below 2^24 for dim <= 258, where it
 // equals the reference's float ADC bit for bit).  qw: query words
 // [pq_dim * wq] (shared memory), cbw: packed codebook (shared memory).
-template <int kW, int kMaxM>
+template <int kMaxM>
 __device__ __forceinline__ float pq_adc_u8(const uint32_t* qw, const uint32_t* cbw, const uint32_t (&cw)[kMaxM / 4],
                                            int pq_dim, int wq)
 {
@@ -201,16 +201,37 @@ __device__ __forceinline__ float pq_adc_u8(const uint32_t* qw, const uint32_t* c
     for (int m = 0; m < kMaxM; ++m) {
         if (m < pq_dim) {
             const uint32_t c = code_byte(cw, m);
-            if constexpr (kW == 4) {
-                const uint32_t d = __vabsdiffu4(qw[m], cbw[m * GOFANN_PQ_CENTROIDS + c]);
+            const uint32_t* e = cbw + (m * GOFANN_PQ_CENTROIDS + c) * wq;
+            for (int t = 0; t < wq; ++t) {
+                const uint32_t d = __vabsdiffu4(qw[m * wq + t], e[t]);
                 acc = __dp4a(d, d, acc);
-            } else {
-                const uint32_t* e = cbw + (m * GOFANN_PQ_CENTROIDS + c) * wq;
-                for (int t = 0; t < wq; ++t) {
-                    const uint32_t d = __vabsdiffu4(qw[m * wq + t], e[t]);
-                    acc = __dp4a(d, d, acc);
-                }
             }
+        }
+    }
+    return __uint2float_rn(acc);
+}
+
+// The same for 4-wide subvectors and pq_dim a multiple of 16 (48 at config
+// 2), reading the code row 16 bytes at a time inside a loop: one chunk's 16
+// subspaces are unrolled, the chunks are not, which keeps the traversal's
+// hot loop small (instruction fetch bounds it otherwise); the row's later
+// chunks come from L1.
+__device__ __forceinline__ float pq_adc_u8_chunked(const uint32_t* qw, const uint32_t* cbw,
+                                                   const uint8_t* __restrict__ code, int pq_dim, uint64_t pol)
+{
+    uint32_t acc = 0;
+    const uint4* row = reinterpret_cast<const uint4*>(code);
+#pragma unroll 1
+    for (int q = 0; q < (pq_dim >> 4); ++q) {
+        const uint4 x = ldg_u32x4(row + q, pol);
+        const uint32_t words[4] = {x.x, x.y, x.z, x.w};
+        const uint32_t* cb = cbw + q * 16 * GOFANN_PQ_CENTROIDS;
+        const uint32_t* qq = qw + q * 16;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const uint32_t c = (words[j >> 2] >> ((j & 3) * 8)) & 0xffu;
+            const uint32_t d = __vabsdiffu4(qq[j], cb[j * GOFANN_PQ_CENTROIDS + c]);
+            acc = __dp4a(d, d, acc);
         }
     }
     return __uint2float_rn(acc);

@@ -27,11 +27,11 @@ def cfg2_small(n=5000, vocab=120, n_queries=160, threshold=300, degree=64, pq_di
 
 
 @functools.lru_cache(maxsize=None)
-def cfg2_small_u8cb():
+def cfg2_small_u8cb(pq_dim=48):
     """cfg2_small with its codebook rounded to integers in 0..255 and the
     codes re-encoded against it: the preconditions of GOFANN_PQ_U8."""
     from oracle import oracle as O
-    w, idx, plan = cfg2_small()
+    w, idx, plan = cfg2_small(pq_dim=pq_dim)
     cent = np.clip(np.rint(idx.pq_centroids), 0, 255).astype(np.float32)
     idx2 = copy.copy(idx)
     idx2.pq_centroids = cent

@@ -229,12 +229,14 @@ def test_beam_search_pq_bitexact(L, wl, vi):
         assert np.array_equal(g, o), f"{name} differ in {np.count_nonzero(np.any(np.atleast_2d(g != o), axis=-1))} routes"
 
 
-@pytest.mark.parametrize("vi", range(len(BEAM_VARIANTS)))
-def test_beam_search_pq_u8_bitexact(L, vi):
+@pytest.mark.parametrize("vi,pq_dim", [(v, 48) for v in range(len(BEAM_VARIANTS))] + [(1, 24), (6, 24)])
+def test_beam_search_pq_u8_bitexact(L, vi, pq_dim):
     """GOFANN_PQ_U8 (integer codebook, u8 queries) against the oracle's float
     table + float ADC on the same codebook: the same bits.  Integer
-    distances tie often, so the exact-heap fallback runs here too."""
-    w, idx, plan = cfg2_small_u8cb()
+    distances tie often, which the reference heap resolves by its layout.
+    pq_dim 48 takes the 16-byte-chunk scorer, 24 (8-byte subvectors) the
+    generic one."""
+    w, idx, plan = cfg2_small_u8cb(pq_dim)
     params = dict(BEAM_VARIANTS[vi], scorer=A.SCORER_PQ, pq_mode=A.PQ_U8)
     lut = O.pq_build_lut(w.queries.astype(np.float32), idx.pq_centroids, idx.pq_codes.shape[1])
     want = O.beam_search(idx.graph(), idx.attrs(), idx.codes(), {"pq_lut": lut}, plan.graph_routes, threads=8,
