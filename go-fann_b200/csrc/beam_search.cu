@@ -204,8 +204,15 @@ struct Scorer {
     int wq;                // PQ_U8: words per subvector
     __device__ __forceinline__ float operator()(const gofann_codes& c, uint32_t sample) const
     {
+        if constexpr (kScorer == GOFANN_SCORER_PQ)
+            return code_row(c, c.pq_codes + static_cast<size_t>(sample) * c.pq_dim);
+        else
+            return rq_estimate(c, rq, sample);
+    }
+    // PQ distance of the code row at `code` (the codes array or a row record)
+    __device__ __forceinline__ float code_row(const gofann_codes& c, const uint8_t* code) const
+    {
         if constexpr (kScorer == GOFANN_SCORER_PQ) {
-            const uint8_t* code = c.pq_codes + static_cast<size_t>(sample) * c.pq_dim;
             if constexpr (kMode == GOFANN_PQ_DIRECT) {
                 return pq_adc_direct<kW, kMaxM>(lut_row, cent, dim, code, static_cast<int>(c.pq_dim), keep, stream);
             } else if constexpr (kMode == GOFANN_PQ_U8) {
@@ -225,7 +232,7 @@ struct Scorer {
                     return pq_adc_words<kMaxM>(lut_row, cw, static_cast<int>(c.pq_dim));
             }
         } else {
-            return rq_estimate(c, rq, sample);
+            return 0.0f;  // RaBitQ scores by sample (operator())
         }
     }
 };
@@ -297,6 +304,7 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
 {
     const gofann_search_params& p = a.p;
     const int QS = p.queue_size, SW = p.stop_width, RW = p.result_width;
+    const uint32_t meta_off = GOFANN_RECORD_META(a.codes.pq_dim);
     WarpState& st = *w.st;
     const Smmh& h = w.heap;
     RPair* topk = w.topk;
@@ -511,11 +519,19 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
         __syncwarp();
         if (st.brk) break;
 
-        // score every listed candidate, one candidate per lane
+        // score every listed candidate, one candidate per lane (from its row
+        // record when the graph has them: one line per candidate)
+        const bool use_rec = kScorer == GOFANN_SCORER_PQ && a.graph.records != nullptr;
         for (int i = lane; i < len; i += kWarp) {
-            const uint32_t s = ldg_u32(a.graph.row_to_sample + label_offset + list[i], stream);
-            slist[i] = s;
-            dist[i] = score(a.codes, s);
+            if (use_rec) {
+                const uint8_t* rec = a.graph.records + static_cast<size_t>(label_offset + list[i]) * a.graph.record_stride;
+                slist[i] = ldg_u32(reinterpret_cast<const uint32_t*>(rec + meta_off), stream);
+                dist[i] = score.code_row(a.codes, rec);
+            } else {
+                const uint32_t s = ldg_u32(a.graph.row_to_sample + label_offset + list[i], stream);
+                slist[i] = s;
+                dist[i] = score(a.codes, s);
+            }
         }
         __syncwarp();
         // priorities, pass bits and the candidates certainly rejected (above
@@ -530,7 +546,15 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
             if (i < len) {
                 float pr = dist[i];
                 if (kBias && pred_on) {
-                    pass = pred_matches(a.routes, a.attrs, route, slist[i]);
+                    if (use_rec) {
+                        const uint4 meta = ldg_u32x4(reinterpret_cast<const uint4*>(
+                            a.graph.records + static_cast<size_t>(label_offset + list[i]) * a.graph.record_stride +
+                            meta_off), stream);
+                        pass = pred_matches_row(a.routes, a.attrs, route, meta.x, meta.y,
+                                                static_cast<uint64_t>(meta.y) + meta.z);
+                    } else {
+                        pass = pred_matches(a.routes, a.attrs, route, slist[i]);
+                    }
                     pr = pred_priority(dist[i], st.penalty, pass);
                 }
                 prio[i] = pr;
@@ -906,6 +930,11 @@ int gofann_beam_search(const gofann_graph* graph, const gofann_attrs* attrs, con
         return fail(GOFANN_ERR_INVALID, "beam_search: resident_warps %d is negative", p.resident_warps);
     if (!graph->adjacency || !graph->row_to_sample || !graph->label_offset || graph->degree == 0)
         return fail(GOFANN_ERR_INVALID, "beam_search: graph arrays missing");
+    if (graph->records && p.scorer == GOFANN_SCORER_PQ &&
+        ((graph->record_stride & 15u) != 0 || (reinterpret_cast<uintptr_t>(graph->records) & 15) != 0 ||
+         graph->record_stride < GOFANN_RECORD_META(codes->pq_dim) + 12u))
+        return fail(GOFANN_ERR_INVALID, "beam_search: row records need 16-byte alignment and a stride of at least %u",
+                    GOFANN_RECORD_META(codes->pq_dim) + 12u);
     if (!routes->query_row || !routes->group_id || !routes->start_local || !out->ids || !out->dists)
         return fail(GOFANN_ERR_INVALID, "beam_search: route or output arrays missing");
     const bool needs_attrs = routes->pred_offsets != nullptr || p.full_label_check != 0 ||
@@ -1073,6 +1102,11 @@ int gofann_beam_search_noalloc(const gofann_graph* graph, const gofann_attrs* at
         return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: resident_warps %d is negative", p.resident_warps);
     if (!graph->adjacency || !graph->row_to_sample || !graph->label_offset || graph->degree == 0)
         return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: graph arrays missing");
+    if (graph->records && p.scorer == GOFANN_SCORER_PQ &&
+        ((graph->record_stride & 15u) != 0 || (reinterpret_cast<uintptr_t>(graph->records) & 15) != 0 ||
+         graph->record_stride < GOFANN_RECORD_META(codes->pq_dim) + 12u))
+        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: row records need 16-byte alignment and a stride of at least %u",
+                    GOFANN_RECORD_META(codes->pq_dim) + 12u);
     if (!routes->query_row || !routes->group_id || !routes->start_local || !out->ids || !out->dists)
         return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: route or output arrays missing");
     const bool needs_attrs = routes->pred_offsets != nullptr || p.full_label_check != 0 ||

@@ -415,15 +415,20 @@ struct AttrView {
     uint32_t range_count;
 };
 
-__device__ __forceinline__ bool csr_contains(const AttrView& a, uint32_t sample, uint32_t label)
+// Is `label` in the sorted label row indices[begin, end)?
+__device__ __forceinline__ bool row_contains(const uint32_t* indices, uint64_t begin, uint64_t end, uint32_t label)
 {
-    uint64_t lo = a.indptr[sample], hi = a.indptr[sample + 1];
+    uint64_t lo = begin, hi = end;
     while (lo < hi) {
         const uint64_t mid = lo + ((hi - lo) >> 1);
-        const uint32_t v = a.indices[mid];
+        const uint32_t v = indices[mid];
         if (v < label) lo = mid + 1; else hi = mid;
     }
-    return lo < a.indptr[sample + 1] && a.indices[lo] == label;
+    return lo < end && indices[lo] == label;
+}
+__device__ __forceinline__ bool csr_contains(const AttrView& a, uint32_t sample, uint32_t label)
+{
+    return row_contains(a.indices, a.indptr[sample], a.indptr[sample + 1], label);
 }
 __device__ __forceinline__ bool range_match(uint32_t mode, float lo, float hi, float v)
 {
@@ -439,6 +444,28 @@ __device__ __forceinline__ bool pred_enabled(const gofann_routes& r, uint32_t ro
 {
     if (!r.pred_offsets) return false;
     return r.pred_enabled ? r.pred_enabled[route] != 0 : true;
+}
+// gpu_predicate::matches with clauses (gpu_predicate_index.cuh:109-136),
+// given the sample's label row [lbegin, lend) of the CSR.
+__device__ __forceinline__ bool pred_matches_row(const gofann_routes& r, const AttrView& a, uint32_t route,
+                                                 uint32_t sample, uint64_t lbegin, uint64_t lend)
+{
+    if (sample >= a.n_samples) return false;
+    const uint32_t e = r.pred_offsets[route + 1];
+    for (uint32_t i = r.pred_offsets[route]; i < e; ++i) {
+        const gofann_clause c = r.clauses[i];
+        bool pass = true;
+        for (uint32_t j = c.label_begin; pass && j < c.label_end; ++j)
+            pass = row_contains(a.indices, lbegin, lend, r.pred_handles[j]);
+        for (uint32_t j = c.range_begin; pass && j < c.range_end; ++j) {
+            const gofann_range_atom at = r.pred_ranges[j];
+            pass = a.ranges != nullptr && at.dimension < a.range_count &&
+                   range_match(at.mode, at.lower, at.upper,
+                               a.ranges[static_cast<uint64_t>(sample) * a.range_count + at.dimension]);
+        }
+        if (pass) return true;
+    }
+    return false;
 }
 // gpu_predicate::matches with clauses (gpu_predicate_index.cuh:109-136).
 __device__ __forceinline__ bool pred_matches(const gofann_routes& r, const AttrView& a,

@@ -47,7 +47,8 @@ RANGE_ATOM_DTYPE = np.dtype([("dimension", "<u4"), ("mode", "<u4"), ("lower", "<
 
 class Graph(C.Structure):
     _fields_ = [("adjacency", P), ("row_to_sample", P), ("row_filter_mask", P), ("label_offset", P),
-                ("total_rows", U32), ("degree", U32), ("group_count", U32), ("reserved", U32)]
+                ("total_rows", U32), ("degree", U32), ("group_count", U32), ("reserved", U32),
+                ("records", P), ("record_stride", U32), ("reserved2", U32)]
 
 
 class Attrs(C.Structure):
@@ -114,6 +115,10 @@ def fill_graph(g: dict) -> Graph:
     s.total_rows = int(g["adjacency"].shape[0])
     s.degree = int(g["adjacency"].shape[1])
     s.group_count = int(g["label_offset"].shape[0])
+    rec = g.get("records")
+    if rec is not None:
+        s.records = ptr(rec)
+        s.record_stride = int(rec.shape[1])
     return s
 
 
@@ -224,6 +229,7 @@ def lib() -> C.CDLL:
         "gofann_route_merge": [sp, sp, U32, sp, sp, U32, I32, sp, sp, sp],
         "gofann_shard_merge": [sp, sp, U32, U32, I32, sp, sp, sp],
         "gofann_offset_ids": [sp, C.c_size_t, U32, sp],
+        "gofann_build_row_records": [C.POINTER(Graph), C.POINTER(Attrs), C.POINTER(Codes), sp, sp, sp],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -231,6 +237,8 @@ def lib() -> C.CDLL:
         fn.restype = C.c_int
     L.gofann_beam_search_scratch_bytes.argtypes = [U32]
     L.gofann_beam_search_scratch_bytes.restype = C.c_size_t
+    L.gofann_row_record_stride.argtypes = [U32]
+    L.gofann_row_record_stride.restype = C.c_size_t
     _LIB = L
     return L
 
@@ -252,7 +260,7 @@ EXPORTED = ("gofann_abi_version", "gofann_last_error", "gofann_device_sm_count",
             "gofann_rabitq_score", "gofann_beam_search_scratch_bytes", "gofann_beam_search",
             "gofann_beam_search_noalloc",
             "gofann_posting_scan", "gofann_rerank", "gofann_route_merge", "gofann_shard_merge",
-            "gofann_offset_ids")
+            "gofann_row_record_stride", "gofann_build_row_records", "gofann_offset_ids")
 
 
 def header_symbols(header: str | os.PathLike | None = None) -> list[str]:

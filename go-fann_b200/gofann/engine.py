@@ -72,7 +72,7 @@ class SearchConfig:
 class DeviceIndex:
     """Index arrays resident in HBM."""
 
-    def __init__(self, index, device="cuda"):
+    def __init__(self, index, device="cuda", row_records: bool = True):
         self.device = torch.device(device)
         d = self.device
         self.dim = index.dim
@@ -90,6 +90,24 @@ class DeviceIndex:
         self.graph_s.degree = int(index.adjacency.shape[1])
         self.attrs_s = A.fill_attrs(self.attrs)
         self.codes_s = A.fill_codes(self.codes)
+        if row_records:
+            self.build_row_records()
+
+    def build_row_records(self) -> None:
+        """Per-row records (code row + sample + label-row range, one line per
+        graph row) read by the traversal instead of row -> sample -> code."""
+        L = A.lib()
+        stride = int(L.gofann_row_record_stride(self.pq_dim))
+        rows = int(self.graph_s.total_rows)
+        rec = torch.empty((max(rows, 1), stride), dtype=torch.uint8, device=self.device)
+        status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        A.check(L.gofann_build_row_records(C.byref(self.graph_s), C.byref(self.attrs_s), C.byref(self.codes_s),
+                                           A.ptr(rec), A.ptr(status), stream_handle()), "gofann_build_row_records")
+        if int(status.item()) != 0:
+            raise A.GofannError(int(status.item()), "gofann_build_row_records (device)")
+        self.graph["records"] = rec
+        self.graph_s.records = A.ptr(rec)
+        self.graph_s.record_stride = stride
 
     def hbm_bytes(self) -> int:
         ts = list(self.graph.values()) + list(self.attrs.values()) + [self.codes["pq_codes"], self.base,

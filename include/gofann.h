@@ -103,7 +103,20 @@ typedef struct gofann_graph {
     uint32_t degree;
     uint32_t group_count;
     uint32_t reserved;
+    /* Optional per-row records (gofann_build_row_records), or NULL: row r at
+     * records + r * record_stride holds the PQ code row of its sample
+     * (pq_dim bytes), then at byte GOFANN_RECORD_META(pq_dim) three uint32:
+     * the sample id, the start and the length of its label-CSR row.  One
+     * 64-byte line per row at config-2 shape: scoring and predicate checks of
+     * a candidate read one line instead of following row -> sample -> code
+     * and sample -> CSR offsets.  Results are the same with or without. */
+    const uint8_t* records;
+    uint32_t record_stride;          /* bytes, a multiple of 16 */
+    uint32_t reserved2;
 } gofann_graph;
+
+/* Byte offset of a record's (sample, label start, label length) words. */
+#define GOFANN_RECORD_META(pq_dim) ((((pq_dim) + 15u) / 16u) * 16u)
 
 /* Per-sample attributes: sample-major label CSR (sorted, unique per row) and
  * float range values (SparseLabelMatrix / base_range_values). */
@@ -322,6 +335,15 @@ GOFANN_API int gofann_route_merge(const uint32_t* route_ids, const float* route_
 GOFANN_API int gofann_shard_merge(const uint32_t* shard_ids, const float* shard_dists, uint32_t n_shards,
                        uint32_t n_queries, int32_t topk, uint32_t* out_ids, float* out_dists,
                        void* stream);
+
+/* Per-row records for the traversal (see gofann_graph.records): record_stride
+ * = GOFANN_RECORD_META(pq_dim) + 16 rounded to 16 (64 bytes at pq_dim 48);
+ * out: device [total_rows][record_stride].  Label CSR offsets must fit in
+ * 32 bits (fails with GOFANN_ERR_UNSUPPORTED otherwise, checked on the
+ * device through `status`, which may be NULL). */
+GOFANN_API size_t gofann_row_record_stride(uint32_t pq_dim);
+GOFANN_API int gofann_build_row_records(const gofann_graph* graph, const gofann_attrs* attrs,
+                                        const gofann_codes* codes, uint8_t* out, int32_t* status, void* stream);
 
 /* Adds base to every id that is not UINT32_MAX (local -> global shard ids). */
 GOFANN_API int gofann_offset_ids(uint32_t* ids, size_t n, uint32_t base, void* stream);

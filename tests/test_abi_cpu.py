@@ -42,7 +42,7 @@ int main(void) {
   S(gofann_prepared) S(gofann_routes) S(gofann_search_params) S(gofann_search_out)
   O(gofann_codes, rq_codes) O(gofann_codes, padded_dim) O(gofann_routes, query_row)
   O(gofann_routes, route_compiled) O(gofann_search_params, alpha) O(gofann_search_params, pq_mode) O(gofann_search_params, resident_warps) O(gofann_prepared, dim) O(gofann_prepared, pq_query)
-  O(gofann_graph, total_rows) O(gofann_attrs, n_samples) O(gofann_prepared, n_rows)
+  O(gofann_graph, total_rows) O(gofann_graph, records) O(gofann_graph, record_stride) O(gofann_attrs, n_samples) O(gofann_prepared, n_rows)
   return 0; }
 '''
     with tempfile.TemporaryDirectory() as d:

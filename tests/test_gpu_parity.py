@@ -249,6 +249,56 @@ def test_beam_search_pq_u8_bitexact(L, vi, pq_dim):
         assert np.array_equal(g, o), f"{name} differ in {np.count_nonzero(np.any(np.atleast_2d(g != o), axis=-1))} routes"
 
 
+def _with_records(L, graph, attrs, codes):
+    """graph dict + per-row records built on the device."""
+    dg, da, dc = dev_dict(graph), dev_dict(attrs), dev_dict(codes)
+    gs, at, cs = A.fill_graph(dg), A.fill_attrs(da), A.fill_codes(dc)
+    stride = int(L.gofann_row_record_stride(cs.pq_dim))
+    rec = torch.empty((gs.total_rows, stride), dtype=torch.uint8, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    A.check(L.gofann_build_row_records(C.byref(gs), C.byref(at), C.byref(cs), A.ptr(rec), A.ptr(status), stream()),
+            "build_row_records")
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    return dict(graph, records=rec), rec
+
+
+def test_row_records_layout(L):
+    """Record r = code row of sample row_to_sample[r], then (sample, label
+    start, label length) at GOFANN_RECORD_META(pq_dim)."""
+    w, idx, plan = cfg2_small()
+    g, rec = _with_records(L, idx.graph(), idx.attrs(), idx.codes())
+    rec = rec.cpu().numpy()
+    m = idx.pq_codes.shape[1]
+    meta = ((m + 15) // 16) * 16
+    r2s = idx.graph()["row_to_sample"].astype(np.int64)
+    ip = idx.attrs()["label_indptr"].astype(np.int64)
+    assert np.array_equal(rec[:, :m], idx.pq_codes[r2s])
+    words = rec[:, meta:meta + 12].copy().view(np.uint32)
+    assert np.array_equal(words[:, 0], r2s)
+    assert np.array_equal(words[:, 1], ip[r2s])
+    assert np.array_equal(words[:, 2], ip[r2s + 1] - ip[r2s])
+
+
+@pytest.mark.parametrize("vi,mode", [(0, A.PQ_U8), (5, A.PQ_U8), (6, A.PQ_U8), (1, A.PQ_LUT_GLOBAL),
+                                     (2, A.PQ_LUT_SHARED), (3, A.PQ_DIRECT)])
+def test_beam_search_row_records_bitexact(L, vi, mode):
+    """The traversal reading per-row records returns what the oracle (and
+    the record-less path) returns."""
+    w, idx, plan = cfg2_small_u8cb()
+    params = dict(BEAM_VARIANTS[vi], scorer=A.SCORER_PQ, pq_mode=mode)
+    lut = O.pq_build_lut(w.queries.astype(np.float32), idx.pq_centroids, idx.pq_codes.shape[1])
+    want = O.beam_search(idx.graph(), idx.attrs(), idx.codes(), {"pq_lut": lut}, plan.graph_routes, threads=8,
+                         trace_width=64, **params)
+    g, _ = _with_records(L, idx.graph(), idx.attrs(), idx.codes())
+    got = run_gpu_beam(L, g, idx.attrs(), idx.codes(), pq_prep(w, idx, mode), plan.graph_routes, trace_width=64,
+                       **params)
+    for name, gv, o in zip(("ids", "dists", "steps", "counters", "trace"), got, want):
+        if name == "dists":
+            gv, o = fbits(gv), fbits(o)
+        assert np.array_equal(gv, o), name
+
+
 def test_beam_search_pq_u8_rejects_fractional_codebook(L):
     """A codebook value that is not an integer in 0..255 sets the status word
     to GOFANN_ERR_INVALID (checked on the device) instead of searching."""
