@@ -61,8 +61,6 @@ struct WarpState {
     uint32_t adm[2];     // candidates admitted to the frontier this step
     int hash_count;      // values in the visited table
     int serial_hash;     // 1: this step's insertions could fill the table
-    uint32_t pf_row[2];  // local rows whose adjacency sits in the two prefetch slots
-    int pf_last;         // slot of the most recently issued prefetch (-1: none)
 };
 
 struct BeamArgs {
@@ -81,7 +79,7 @@ struct BeamArgs {
 };
 
 struct SmemLayout {
-    uint32_t frontier, topk, stop, list, sample, dist, prio, state, nadj, table, total;
+    uint32_t frontier, topk, stop, list, dist, prio, state, table, total;
 };
 
 __host__ __device__ inline uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
@@ -96,11 +94,9 @@ __host__ __device__ inline SmemLayout smem_layout(const gofann_search_params& p,
     s.topk = o; o = align16(o + (p.result_width + 1) * sizeof(RPair));
     s.stop = o; o = align16(o + (GOFANN_MAX_TOPK + 2) * sizeof(SPair));
     s.list = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
-    s.sample = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
     s.dist = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
     s.prio = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
     s.state = o; o = align16(o + sizeof(WarpState));
-    s.nadj = o; o = align16(o + 2 * GOFANN_MAX_DEGREE * 4);
     s.table = o;
     if (p.scorer == GOFANN_SCORER_PQ) {
         if (pq_mode == GOFANN_PQ_LUT_SHARED) o = align16(o + c.pq_dim * GOFANN_PQ_CENTROIDS * 4);
@@ -142,44 +138,21 @@ __device__ __forceinline__ bool stop_now(const gofann_search_params& p, const Wa
     return st.exhausted || es || step >= cap;
 }
 
-// Asynchronous copy of the adjacency row at `src` into a prefetch slot.  The
-// node expanded next is fixed one step ahead (the reference picks `next`
-// before processing `now`, backend_pq.cu:4257-4278), so its row is in flight
-// while the current step scores and admits candidates.
-__device__ __forceinline__ void prefetch_row(uint32_t* dst, const uint32_t* src, uint32_t deg, int lane,
-                                             uint64_t pol)
+// Adjacency row of local row `row`: ids of neighbours lane and lane + 32 in
+// registers (UINT32_MAX past the degree).  The node expanded next is fixed
+// one step ahead (the reference picks `next` before processing `now`,
+// backend_pq.cu:4257-4278), so its row is loaded while the current step
+// scores and admits candidates.
+__device__ __forceinline__ void load_row_ids(uint32_t (&ids)[GOFANN_MAX_DEGREE / kWarp], const uint32_t* adjacency,
+                                             uint32_t label_offset, uint32_t degree, uint32_t deg, uint32_t row,
+                                             int lane, uint64_t pol)
 {
-    const bool vec = (deg & 3u) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
-    const uint32_t n = vec ? deg / 4 : deg;
-    for (uint32_t i = lane; i < n; i += kWarp) {
-        const uint32_t sa = static_cast<uint32_t>(__cvta_generic_to_shared(dst + (vec ? 4 * i : i)));
-        if (vec)
-            asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 16, %2;\n" ::"r"(sa),
-                         "l"(src + 4 * i), "l"(pol));
-        else
-            asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 4, %2;\n" ::"r"(sa), "l"(src + i),
-                         "l"(pol));
+    const uint32_t* src = adjacency + static_cast<size_t>(label_offset + row) * degree;
+#pragma unroll
+    for (int h = 0; h < GOFANN_MAX_DEGREE / kWarp; ++h) {
+        const uint32_t i = h * kWarp + lane;
+        ids[h] = i < deg ? ldg_u32(src + i, pol) : kU32Max;
     }
-    asm volatile("cp.async.commit_group;\n" ::);
-}
-__device__ __forceinline__ void prefetch_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
-__device__ __forceinline__ void prefetch_wait_older() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
-
-// Issues the prefetch of `row` into the slot not holding the row expanded
-// now (double buffering across steps).
-__device__ __forceinline__ void prefetch_next(WarpState& st, uint32_t* nadj, const uint32_t* adjacency,
-                                              uint32_t label_offset, uint32_t degree, uint32_t deg, uint32_t row,
-                                              int lane, uint64_t pol)
-{
-    const int slot = st.pf_last < 0 ? 0 : (st.pf_last ^ 1);
-    prefetch_row(nadj + slot * GOFANN_MAX_DEGREE, adjacency + static_cast<size_t>(label_offset + row) * degree, deg,
-                 lane, pol);
-    __syncwarp();
-    if (lane == 0) {
-        st.pf_row[slot] = row;
-        st.pf_last = slot;
-    }
-    __syncwarp();
 }
 
 __device__ __forceinline__ uint32_t ordered_bits(float f)
@@ -287,11 +260,9 @@ struct WarpBufs {
     RPair* topk;
     SPair* stopk;
     uint32_t* list;
-    uint32_t* slist;
     float* dist;
     float* prio;
     WarpState* st;
-    uint32_t* nadj;
     uint32_t* hash;
 };
 
@@ -310,10 +281,8 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
     RPair* topk = w.topk;
     SPair* stopk = w.stopk;
     uint32_t* list = w.list;
-    uint32_t* slist = w.slist;
     float* dist = w.dist;
     float* prio = w.prio;
-    uint32_t* nadj = w.nadj;
     uint32_t* hash = w.hash;
 
     // visited table clear (native_visited_hash::clear)
@@ -356,11 +325,14 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
         st.heap_size = 2;
         hash_add(hash, begin_id);
         st.hash_count = 1;
-        st.pf_row[0] = st.pf_row[1] = kU32Max;
-        st.pf_last = -1;
     }
     __syncwarp();
     smmh_pickup(h, st.heap_size, &st.now, lane);
+    // adjacency ids of the node expanded now and of the one expanded next
+    uint32_t nb[GOFANN_MAX_DEGREE / kWarp], nb_next[GOFANN_MAX_DEGREE / kWarp];
+#pragma unroll
+    for (int h = 0; h < GOFANN_MAX_DEGREE / kWarp; ++h) nb_next[h] = kU32Max;
+    load_row_ids(nb, a.graph.adjacency, label_offset, a.graph.degree, deg, st.now.second & kRowMask, lane, stream);
 
     int step = 0;
     for (;;) {
@@ -389,8 +361,8 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
             }
             __syncwarp();
             if (found)
-                prefetch_next(st, nadj, a.graph.adjacency, label_offset, a.graph.degree, deg,
-                              st.next.second & kRowMask, lane, stream);
+                load_row_ids(nb_next, a.graph.adjacency, label_offset, a.graph.degree, deg,
+                             st.next.second & kRowMask, lane, stream);
         }
         if (st.exhausted) break;
         const uint32_t now_row = st.now.second & kRowMask;
@@ -484,28 +456,12 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
         __syncwarp();
         if (st.brk) break;
 
-        // neighbour list: parallel read + visited test, in-order compaction
-        const int pslot = st.pf_row[0] == now_row ? 0 : (st.pf_row[1] == now_row ? 1 : -1);
-        if (pslot >= 0) {
-            if (pslot == st.pf_last) prefetch_wait_all();
-            else prefetch_wait_older();  // the newer group (the next row) may stay in flight
-        }
-        __syncwarp();
-        const bool prefetched = pslot >= 0;
-        const uint32_t* adj = prefetched ? nadj + pslot * GOFANN_MAX_DEGREE
-                                         : a.graph.adjacency + static_cast<size_t>(grow) * a.graph.degree;
+        // neighbour list: visited test of the row's ids (in registers), in-order
+        // compaction
         int len = 0;
-        uint32_t nid[GOFANN_MAX_DEGREE / kWarp];
 #pragma unroll
         for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
-            const uint32_t i = half * kWarp + lane;
-            nid[half] = kU32Max;
-            if (i < deg) nid[half] = prefetched ? adj[i] : ldg_u32(adj + i, stream);
-            if (nid[half] != kU32Max) prefetch_l1(hash + hash_code(nid[half]));
-        }
-#pragma unroll
-        for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
-            const uint32_t idx = nid[half];
+            const uint32_t idx = nb[half];
             const bool keep = idx != kU32Max && !hash_test(hash, idx);
             const unsigned m = __ballot_sync(kFull, keep);
             if (keep) list[len + __popc(m & ((1u << lane) - 1u))] = idx;
@@ -519,24 +475,13 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
         __syncwarp();
         if (st.brk) break;
 
-        // score every listed candidate, one candidate per lane (from its row
-        // record when the graph has them: one line per candidate)
+        // score and predicate of every listed candidate, one candidate per
+        // lane (from its row record when the graph has them: the code row and
+        // the label-row range share one line, and the label read overlaps the
+        // distance arithmetic); priorities, pass bits and the candidates
+        // certainly rejected (above the heap maximum while the heap is full:
+        // the maximum only decreases within a step) as ballots
         const bool use_rec = kScorer == GOFANN_SCORER_PQ && a.graph.records != nullptr;
-        for (int i = lane; i < len; i += kWarp) {
-            if (use_rec) {
-                const uint8_t* rec = a.graph.records + static_cast<size_t>(label_offset + list[i]) * a.graph.record_stride;
-                slist[i] = ldg_u32(reinterpret_cast<const uint32_t*>(rec + meta_off), stream);
-                dist[i] = score.code_row(a.codes, rec);
-            } else {
-                const uint32_t s = ldg_u32(a.graph.row_to_sample + label_offset + list[i], stream);
-                slist[i] = s;
-                dist[i] = score(a.codes, s);
-            }
-        }
-        __syncwarp();
-        // priorities, pass bits and the candidates certainly rejected (above
-        // the heap maximum while the heap is full: the maximum only
-        // decreases within a step)
         const bool full = st.heap_size >= QS + 1;
         const float maxv = full ? h.key[2] : 0.0f;
 #pragma unroll 1
@@ -544,19 +489,22 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
             const int i = half * kWarp + lane;
             bool reject = false, pass = false;
             if (i < len) {
-                float pr = dist[i];
-                if (kBias && pred_on) {
-                    if (use_rec) {
-                        const uint4 meta = ldg_u32x4(reinterpret_cast<const uint4*>(
-                            a.graph.records + static_cast<size_t>(label_offset + list[i]) * a.graph.record_stride +
-                            meta_off), stream);
+                float d;
+                if (use_rec) {
+                    const uint8_t* rec =
+                        a.graph.records + static_cast<size_t>(label_offset + list[i]) * a.graph.record_stride;
+                    const uint4 meta = ldg_u32x4(reinterpret_cast<const uint4*>(rec + meta_off), stream);
+                    if (kBias && pred_on)
                         pass = pred_matches_row(a.routes, a.attrs, route, meta.x, meta.y,
                                                 static_cast<uint64_t>(meta.y) + meta.z);
-                    } else {
-                        pass = pred_matches(a.routes, a.attrs, route, slist[i]);
-                    }
-                    pr = pred_priority(dist[i], st.penalty, pass);
+                    d = score.code_row(a.codes, rec);
+                } else {
+                    const uint32_t smp = ldg_u32(a.graph.row_to_sample + label_offset + list[i], stream);
+                    if (kBias && pred_on) pass = pred_matches(a.routes, a.attrs, route, smp);
+                    d = score(a.codes, smp);
                 }
+                const float pr = (kBias && pred_on) ? pred_priority(d, st.penalty, pass) : d;
+                dist[i] = d;
                 prio[i] = pr;
                 reject = full && maxv < pr;
             }
@@ -634,15 +582,23 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
                 st.next = nx;
             }
             if (found)
-                prefetch_next(st, nadj, a.graph.adjacency, label_offset, a.graph.degree, deg,
-                              st.next.second & kRowMask, lane, stream);
+                load_row_ids(nb_next, a.graph.adjacency, label_offset, a.graph.degree, deg,
+                             st.next.second & kRowMask, lane, stream);
         }
         if (lane == 0) st.now = st.next;
+        // the next step's reads, fetched now: its visited-table lines (after
+        // this step's inserts) into L1, its neighbours' records into L2
+#pragma unroll
+        for (int h = 0; h < GOFANN_MAX_DEGREE / kWarp; ++h) {
+            nb[h] = nb_next[h];
+            if (nb[h] != kU32Max && !st.exhausted) {
+                prefetch_l1(hash + hash_code(nb[h]));
+                if (kScorer == GOFANN_SCORER_PQ && a.graph.records)
+                    prefetch_l2(a.graph.records + static_cast<size_t>(label_offset + nb[h]) * a.graph.record_stride);
+            }
+        }
         __syncwarp();
     }
-
-    prefetch_wait_all();  // no copy of this route may land in the next route's slots
-    __syncwarp();
 
     // emit the shortlist ascending (in-place heap sort of the result heap)
     if (lane == 0) {
@@ -712,11 +668,9 @@ __global__ void __launch_bounds__(block_warps<kMode>() * 32, min_blocks<kMode>()
     w.topk = reinterpret_cast<RPair*>(base + L.topk);
     w.stopk = reinterpret_cast<SPair*>(base + L.stop);
     w.list = reinterpret_cast<uint32_t*>(base + L.list);
-    w.slist = reinterpret_cast<uint32_t*>(base + L.sample);
     w.dist = reinterpret_cast<float*>(base + L.dist);
     w.prio = reinterpret_cast<float*>(base + L.prio);
     w.st = reinterpret_cast<WarpState*>(base + L.state);
-    w.nadj = reinterpret_cast<uint32_t*>(base + L.nadj);
     float* table = reinterpret_cast<float*>(base + L.table);
     const uint32_t gwarp = blockIdx.x * (blockDim.x >> 5) + warp;
     w.hash = a.hash + static_cast<size_t>(gwarp) * kHashCap;

@@ -89,12 +89,16 @@ __device__ __forceinline__ uint4 ldg_u32x4(const uint4* p, uint64_t pol)
     return v;
 }
 
-// Non-blocking fetch of the line holding p into L1 (PTX prefetch): issued for
-// every candidate of a step before any of them is evaluated, so that their
-// dependent loads overlap instead of running one candidate after another.
+// Non-blocking fetch of the line holding p into L1 or L2 (PTX prefetch): the
+// traversal issues them one step ahead for the rows the next step reads, so
+// that those reads do not wait on HBM or L2.
 __device__ __forceinline__ void prefetch_l1(const void* p)
 {
     asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+__device__ __forceinline__ void prefetch_l2(const void* p)
+{
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
 // --------------------------------------------------- float order helpers
