@@ -40,6 +40,13 @@ __device__ __forceinline__ void bitonic_sort_pairs(float* d, uint32_t* id, int n
     }
 }
 
+__device__ __forceinline__ uint32_t next_pow2(uint32_t x)
+{
+    return x <= 1 ? 1u : 1u << (32 - __clz(x - 1));
+}
+
+// One block per route (the hardware balances routes of very different
+// lengths); the sort spans only as many slots as the route has candidates.
 template <int kScorer>
 __global__ void __launch_bounds__(kScanThreads) posting_scan_kernel(
     gofann_codes codes, gofann_prepared prep, AttrView attrs, gofann_routes routes,
@@ -50,77 +57,87 @@ __global__ void __launch_bounds__(kScanThreads) posting_scan_kernel(
     float* sd = reinterpret_cast<float*>(smem_raw);
     uint32_t* sid = reinterpret_cast<uint32_t*>(smem_raw + kSortSize * sizeof(float));
     float* table = reinterpret_cast<float*>(smem_raw + kSortSize * (sizeof(float) + sizeof(uint32_t)));
-    const uint32_t route = blockIdx.x;
     const int tid = threadIdx.x;
-    const uint32_t row = routes.query_row[route];
-    const bool pred_on = pred_enabled(routes, route);
-
-    RqQueryView rq{};
-    if constexpr (kScorer == GOFANN_SCORER_PQ) {
-        if (prep.pq_lut) {
-            const float4* g = reinterpret_cast<const float4*>(prep.pq_lut + static_cast<size_t>(row) * codes.pq_dim *
-                                                                                GOFANN_PQ_CENTROIDS);
-            float4* t4 = reinterpret_cast<float4*>(table);
-            for (int i = tid; i < static_cast<int>(codes.pq_dim) * GOFANN_PQ_CENTROIDS / 4; i += kScanThreads)
-                t4[i] = __ldg(g + i);
-        } else {
-            // fused table build (computePQTable, backend_pq.cu:1999-2022, which
-            // the reference also runs inside its scan): query row to shared
-            // memory, then thread c evaluates column c of every subspace
+    const int pq_dim = static_cast<int>(codes.pq_dim);
+    {
+        const uint32_t route = blockIdx.x;
+        const uint32_t row = routes.query_row[route];
+        const bool pred_on = pred_enabled(routes, route);
+        RqQueryView rq{};
+        if constexpr (kScorer == GOFANN_SCORER_PQ) {
             const int dim = static_cast<int>(prep.dim);
-            float* q = table + codes.pq_dim * GOFANN_PQ_CENTROIDS;
-            if (prep.pq_query_dtype == GOFANN_DTYPE_U8) {
-                const uint8_t* qr = static_cast<const uint8_t*>(prep.pq_query) + static_cast<size_t>(row) * dim;
-                for (int i = tid; i < dim; i += kScanThreads) q[i] = static_cast<float>(qr[i]);
+            if (prep.pq_lut) {
+                const float4* g = reinterpret_cast<const float4*>(prep.pq_lut + static_cast<size_t>(row) * pq_dim *
+                                                                                    GOFANN_PQ_CENTROIDS);
+                float4* t4 = reinterpret_cast<float4*>(table);
+                for (int i = tid; i < pq_dim * GOFANN_PQ_CENTROIDS / 4; i += kScanThreads) t4[i] = __ldg(g + i);
             } else {
-                const float* qr = static_cast<const float*>(prep.pq_query) + static_cast<size_t>(row) * dim;
-                for (int i = tid; i < dim; i += kScanThreads) q[i] = qr[i];
+                // fused table build (computePQTable, backend_pq.cu:1999-2022, which
+                // the reference also runs inside its scan): query row to shared
+                // memory, then thread c evaluates column c of every subspace
+                float* q = table + pq_dim * GOFANN_PQ_CENTROIDS;
+                if (prep.pq_query_dtype == GOFANN_DTYPE_U8) {
+                    const uint8_t* qr = static_cast<const uint8_t*>(prep.pq_query) + static_cast<size_t>(row) * dim;
+                    for (int i = tid; i < dim; i += kScanThreads) q[i] = static_cast<float>(qr[i]);
+                } else {
+                    const float* qr = static_cast<const float*>(prep.pq_query) + static_cast<size_t>(row) * dim;
+                    for (int i = tid; i < dim; i += kScanThreads) q[i] = qr[i];
+                }
+                __syncthreads();
+                const int w = dim / pq_dim;
+                const float* crow = prep.pq_centroids + static_cast<size_t>(tid) * dim;  // kScanThreads == 256
+                const uint64_t keep = l2_keep_policy();  // the codebook is shared by every route
+                for (int m = 0; m < pq_dim; ++m)
+                    table[m * GOFANN_PQ_CENTROIDS + tid] = pq_entry<0>(q + m * w, crow + m * w, w, keep);
+            }
+        } else {
+            rq_build_planes(prep.rq_q8 + static_cast<size_t>(row) * codes.padded_dim,
+                            static_cast<int>(codes.padded_dim), reinterpret_cast<uint32_t*>(table), tid,
+                            kScanThreads);
+            rq.planes = reinterpret_cast<const uint32_t*>(table);
+            rq.scale = prep.rq_scale[row];
+            rq.k1 = prep.rq_k1xsumq[row];
+            rq.gdist = prep.rq_centroid_dist + static_cast<size_t>(row) * codes.num_anchors;
+        }
+        const uint64_t begin = route_begin[route];
+        const uint32_t count = route_count[route];
+        // one chunk: candidates at [0, count), the sort spans the next power of
+        // two; several: the running top-k at [0, kKeep), chunks after it
+        const bool single = count <= static_cast<uint32_t>(kChunk);
+        const int keep_slots = single ? 0 : kKeep;
+        const int chunk = single ? static_cast<int>(count) : kChunk;
+        const int n_sort = single ? static_cast<int>(next_pow2(count)) : kSortSize;
+        for (int i = tid; i < keep_slots; i += kScanThreads) { sd[i] = FLT_MAX; sid[i] = kU32Max; }
+        __syncthreads();
+        for (uint32_t c0 = 0; c0 < count; c0 += static_cast<uint32_t>(chunk)) {
+            for (int j = tid; j < n_sort - keep_slots; j += kScanThreads) {
+                const uint32_t i = c0 + j;
+                float dist = FLT_MAX;
+                uint32_t s = kU32Max;
+                if (j < chunk && i < count) {
+                    s = posting_ids[begin + i];
+                    if (s != kU32Max && pred_on && !pred_matches(routes, attrs, route, s)) s = kU32Max;
+                    if (s != kU32Max) {
+                        if constexpr (kScorer == GOFANN_SCORER_PQ) {
+                            dist = pq_adc_sequential(table, codes.pq_codes + static_cast<size_t>(s) * pq_dim,
+                                                     pq_dim);
+                        } else {
+                            dist = rq_estimate(codes, rq, s);
+                        }
+                    }
+                }
+                sd[keep_slots + j] = s == kU32Max ? FLT_MAX : dist;
+                sid[keep_slots + j] = s;
             }
             __syncthreads();
-            const int w = dim / static_cast<int>(codes.pq_dim);
-            const float* crow = prep.pq_centroids + static_cast<size_t>(tid) * dim;  // kScanThreads == 256
-            const uint64_t keep = l2_keep_policy();  // the codebook is shared by every route
-            for (int m = 0; m < static_cast<int>(codes.pq_dim); ++m)
-                table[m * GOFANN_PQ_CENTROIDS + tid] = pq_entry<0>(q + m * w, crow + m * w, w, keep);
+            bitonic_sort_pairs(sd, sid, n_sort, tid, kScanThreads);
         }
-    } else {
-        rq_build_planes(prep.rq_q8 + static_cast<size_t>(row) * codes.padded_dim, static_cast<int>(codes.padded_dim),
-                        reinterpret_cast<uint32_t*>(table), tid, kScanThreads);
-        rq.planes = reinterpret_cast<const uint32_t*>(table);
-        rq.scale = prep.rq_scale[row];
-        rq.k1 = prep.rq_k1xsumq[row];
-        rq.gdist = prep.rq_centroid_dist + static_cast<size_t>(row) * codes.num_anchors;
-    }
-    for (int i = tid; i < kKeep; i += kScanThreads) { sd[i] = FLT_MAX; sid[i] = kU32Max; }
-    __syncthreads();
-
-    const uint64_t begin = route_begin[route];
-    const uint32_t count = route_count[route];
-    for (uint32_t c0 = 0; c0 < count; c0 += kChunk) {
-        for (int j = tid; j < kChunk; j += kScanThreads) {
-            const uint32_t i = c0 + j;
-            float dist = FLT_MAX;
-            uint32_t s = kU32Max;
-            if (i < count) {
-                s = posting_ids[begin + i];
-                if (s != kU32Max && pred_on && !pred_matches(routes, attrs, route, s)) s = kU32Max;
-                if (s != kU32Max) {
-                    if constexpr (kScorer == GOFANN_SCORER_PQ)
-                        dist = pq_adc_sequential(table, codes.pq_codes + static_cast<size_t>(s) * codes.pq_dim,
-                                                 static_cast<int>(codes.pq_dim));
-                    else
-                        dist = rq_estimate(codes, rq, s);
-                }
-            }
-            sd[kKeep + j] = s == kU32Max ? FLT_MAX : dist;
-            sid[kKeep + j] = s;
+        for (int i = tid; i < k; i += kScanThreads) {
+            const bool have = i < n_sort && count > 0;
+            const uint32_t id = have ? sid[i] : kU32Max;
+            out_ids[static_cast<size_t>(route) * k + i] = id;
+            out_d[static_cast<size_t>(route) * k + i] = id == kU32Max ? FLT_MAX : sd[i];
         }
-        __syncthreads();
-        bitonic_sort_pairs(sd, sid, kSortSize, tid, kScanThreads);
-    }
-    for (int i = tid; i < k; i += kScanThreads) {
-        out_ids[static_cast<size_t>(route) * k + i] = sid[i];
-        out_d[static_cast<size_t>(route) * k + i] = sid[i] == kU32Max ? FLT_MAX : sd[i];
     }
 }
 
@@ -175,15 +192,12 @@ int gofann_posting_scan(const gofann_codes* codes, const gofann_prepared* prep, 
     }
     const size_t smem = static_cast<size_t>(kSortSize) * 8 + table_bytes;
     cudaStream_t s = as_stream(stream);
-    if (scorer == GOFANN_SCORER_PQ) {
-        cudaFuncSetAttribute(posting_scan_kernel<GOFANN_SCORER_PQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        posting_scan_kernel<GOFANN_SCORER_PQ><<<routes->n_routes, kScanThreads, smem, s>>>(
-            *codes, *prep, av, *routes, posting_ids, route_begin, route_count, shortlist_k, out_ids, out_dists);
-    } else {
-        cudaFuncSetAttribute(posting_scan_kernel<GOFANN_SCORER_RABITQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        posting_scan_kernel<GOFANN_SCORER_RABITQ><<<routes->n_routes, kScanThreads, smem, s>>>(
-            *codes, *prep, av, *routes, posting_ids, route_begin, route_count, shortlist_k, out_ids, out_dists);
-    }
+    const auto kern = scorer == GOFANN_SCORER_PQ ? posting_scan_kernel<GOFANN_SCORER_PQ>
+                                                 : posting_scan_kernel<GOFANN_SCORER_RABITQ>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_status(e, "posting_scan: shared memory attribute");
+    kern<<<routes->n_routes, kScanThreads, smem, s>>>(*codes, *prep, av, *routes, posting_ids, route_begin,
+                                                      route_count, shortlist_k, out_ids, out_dists);
     GOFANN_CHECK_LAUNCH("posting_scan_kernel");
     return GOFANN_OK;
 }

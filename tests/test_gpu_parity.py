@@ -408,6 +408,28 @@ def test_posting_scan_pq_bitexact(L, k, fused):
     assert np.array_equal(fbits(got[1]), fbits(want[1]))
 
 
+@pytest.mark.parametrize("k,pq_dim", [(10, 48), (100, 48), (400, 48), (100, 24)])
+def test_posting_scan_pq_u8_codebook_bitexact(L, k, pq_dim):
+    """The index's integer codebook with u8 queries and no prebuilt table (the
+    traversal's GOFANN_PQ_U8 inputs): the scan builds its table itself and
+    matches the oracle's float table + sequential float ADC bit for bit, for
+    4- and 8-byte subvectors, multi-chunk postings and an empty posting."""
+    from gofann.planner import concat_routes, subset_routes
+    w, idx, plan = cfg2_small_u8cb(pq_dim)
+    lut = O.pq_build_lut(w.queries.astype(np.float32), idx.pq_centroids, idx.pq_codes.shape[1])
+    big = np.argsort(idx.posting_count)[-3:]
+    extra = subset_routes(plan.graph_routes, np.arange(4))
+    routes = concat_routes(plan.posting_routes, extra)
+    begin = np.concatenate([plan.posting_begin, idx.posting_begin[big], [0]]).astype(np.uint64)
+    count = np.concatenate([plan.posting_count, idx.posting_count[big], [0]]).astype(np.uint32)
+    want = O.posting_scan(idx.codes(), {"pq_lut": lut}, idx.attrs(), routes, A.SCORER_PQ, idx.posting_ids, begin,
+                          count, k)
+    got = run_gpu_posting(L, idx.codes(), pq_prep(w, idx, A.PQ_U8), idx.attrs(), routes, A.SCORER_PQ,
+                          idx.posting_ids, begin, count, k)
+    assert np.array_equal(got[0], want[0])
+    assert np.array_equal(fbits(got[1]), fbits(want[1]))
+
+
 def test_posting_scan_rabitq_bitexact(L):
     w, idx, plan, rq, anchors, qr = rabitq_artifacts()
     dprep, hprep = _rq_prepared(L, qr, anchors)
