@@ -494,9 +494,14 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
                     const uint8_t* rec =
                         a.graph.records + static_cast<size_t>(label_offset + list[i]) * a.graph.record_stride;
                     const uint4 meta = ldg_u32x4(reinterpret_cast<const uint4*>(rec + meta_off), stream);
-                    if (kBias && pred_on)
-                        pass = pred_matches_row(a.routes, a.attrs, route, meta.x, meta.y,
-                                                static_cast<uint64_t>(meta.y) + meta.z);
+                    if (kBias && pred_on) {
+                        // the label row from the record when it is stored there
+                        const bool inl = meta.z <= GOFANN_RECORD_INLINE_LABELS;
+                        const uint32_t* lab = inl ? reinterpret_cast<const uint32_t*>(rec + meta_off + 16)
+                                                  : a.attrs.indices;
+                        const uint64_t lb = inl ? 0ull : meta.y;
+                        pass = pred_matches_row(a.routes, a.attrs, route, meta.x, lab, lb, lb + meta.z);
+                    }
                     d = score.code_row(a.codes, rec);
                 } else {
                     const uint32_t smp = ldg_u32(a.graph.row_to_sample + label_offset + list[i], stream);
@@ -886,9 +891,9 @@ int gofann_beam_search(const gofann_graph* graph, const gofann_attrs* attrs, con
         return fail(GOFANN_ERR_INVALID, "beam_search: graph arrays missing");
     if (graph->records && p.scorer == GOFANN_SCORER_PQ &&
         ((graph->record_stride & 15u) != 0 || (reinterpret_cast<uintptr_t>(graph->records) & 15) != 0 ||
-         graph->record_stride < GOFANN_RECORD_META(codes->pq_dim) + 12u))
+         graph->record_stride < GOFANN_RECORD_META(codes->pq_dim) + 16u + 4u * GOFANN_RECORD_INLINE_LABELS))
         return fail(GOFANN_ERR_INVALID, "beam_search: row records need 16-byte alignment and a stride of at least %u",
-                    GOFANN_RECORD_META(codes->pq_dim) + 12u);
+                    GOFANN_RECORD_META(codes->pq_dim) + 16u + 4u * GOFANN_RECORD_INLINE_LABELS);
     if (!routes->query_row || !routes->group_id || !routes->start_local || !out->ids || !out->dists)
         return fail(GOFANN_ERR_INVALID, "beam_search: route or output arrays missing");
     const bool needs_attrs = routes->pred_offsets != nullptr || p.full_label_check != 0 ||
@@ -1058,9 +1063,9 @@ int gofann_beam_search_noalloc(const gofann_graph* graph, const gofann_attrs* at
         return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: graph arrays missing");
     if (graph->records && p.scorer == GOFANN_SCORER_PQ &&
         ((graph->record_stride & 15u) != 0 || (reinterpret_cast<uintptr_t>(graph->records) & 15) != 0 ||
-         graph->record_stride < GOFANN_RECORD_META(codes->pq_dim) + 12u))
+         graph->record_stride < GOFANN_RECORD_META(codes->pq_dim) + 16u + 4u * GOFANN_RECORD_INLINE_LABELS))
         return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: row records need 16-byte alignment and a stride of at least %u",
-                    GOFANN_RECORD_META(codes->pq_dim) + 12u);
+                    GOFANN_RECORD_META(codes->pq_dim) + 16u + 4u * GOFANN_RECORD_INLINE_LABELS);
     if (!routes->query_row || !routes->group_id || !routes->start_local || !out->ids || !out->dists)
         return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: route or output arrays missing");
     const bool needs_attrs = routes->pred_offsets != nullptr || p.full_label_check != 0 ||

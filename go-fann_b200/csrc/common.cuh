@@ -450,9 +450,11 @@ __device__ __forceinline__ bool pred_enabled(const gofann_routes& r, uint32_t ro
     return r.pred_enabled ? r.pred_enabled[route] != 0 : true;
 }
 // gpu_predicate::matches with clauses (gpu_predicate_index.cuh:109-136),
-// given the sample's label row [lbegin, lend) of the CSR.
+// given the sample's sorted label row labels[lbegin, lend) (the CSR's
+// indices, or a copy of the row).
 __device__ __forceinline__ bool pred_matches_row(const gofann_routes& r, const AttrView& a, uint32_t route,
-                                                 uint32_t sample, uint64_t lbegin, uint64_t lend)
+                                                 uint32_t sample, const uint32_t* labels, uint64_t lbegin,
+                                                 uint64_t lend)
 {
     if (sample >= a.n_samples) return false;
     const uint32_t e = r.pred_offsets[route + 1];
@@ -460,7 +462,7 @@ __device__ __forceinline__ bool pred_matches_row(const gofann_routes& r, const A
         const gofann_clause c = r.clauses[i];
         bool pass = true;
         for (uint32_t j = c.label_begin; pass && j < c.label_end; ++j)
-            pass = row_contains(a.indices, lbegin, lend, r.pred_handles[j]);
+            pass = row_contains(labels, lbegin, lend, r.pred_handles[j]);
         for (uint32_t j = c.range_begin; pass && j < c.range_end; ++j) {
             const gofann_range_atom at = r.pred_ranges[j];
             pass = a.ranges != nullptr && at.dimension < a.range_count &&

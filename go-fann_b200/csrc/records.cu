@@ -5,7 +5,8 @@
 // (GraphMetadata::row_to_sample, pq.codes.bin, SparseLabelMatrix): two
 // dependent reads each.  A record stores, per graph row and in row order,
 // the sample's code row followed by (sample id, label-row start, label-row
-// length), so the traversal reads one line per candidate.  The records are
+// length) and, for rows of at most GOFANN_RECORD_INLINE_LABELS labels, the
+// labels, so the traversal reads one line per candidate.  The records are
 // derived data; a traversal gives the same results with or without them.
 #include "common.cuh"
 
@@ -40,6 +41,13 @@ __global__ void build_records_kernel(gofann_graph g, AttrView at, const uint8_t*
             w[0] = sample;
             w[1] = static_cast<uint32_t>(lo);
             w[2] = static_cast<uint32_t>(hi - lo);
+        } else {
+            // inline label row (short rows only)
+            const uint64_t lo = at.indptr[sample], hi = at.indptr[sample + 1];
+            const uint32_t base = (c - meta_chunk - 1) * 4;
+            if (hi - lo <= GOFANN_RECORD_INLINE_LABELS)
+                for (uint32_t b = 0; b < 4; ++b)
+                    if (base + b < hi - lo) w[b] = at.indices[lo + base + b];
         }
         reinterpret_cast<uint4*>(out + row * stride)[c] = make_uint4(w[0], w[1], w[2], w[3]);
     }
@@ -52,13 +60,17 @@ using namespace gofann;
 
 extern "C" {
 
-size_t gofann_row_record_stride(uint32_t pq_dim) { return GOFANN_RECORD_META(pq_dim) + 16u; }
+size_t gofann_row_record_stride(uint32_t pq_dim)
+{
+    return GOFANN_RECORD_META(pq_dim) + 16u + 4u * GOFANN_RECORD_INLINE_LABELS;
+}
 
 int gofann_build_row_records(const gofann_graph* graph, const gofann_attrs* attrs, const gofann_codes* codes,
                              uint8_t* out, int32_t* status, void* stream)
 {
     if (!graph || !attrs || !codes || !out) return fail(GOFANN_ERR_INVALID, "build_row_records: null argument");
-    if (!graph->row_to_sample || !attrs->label_indptr || !codes->pq_codes || codes->pq_dim == 0)
+    if (!graph->row_to_sample || !attrs->label_indptr || !attrs->label_indices || !codes->pq_codes ||
+        codes->pq_dim == 0)
         return fail(GOFANN_ERR_INVALID, "build_row_records: row_to_sample, label CSR and PQ codes required");
     if ((reinterpret_cast<uintptr_t>(out) & 15) != 0)
         return fail(GOFANN_ERR_INVALID, "build_row_records: output must be 16-byte aligned");

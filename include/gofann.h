@@ -106,10 +106,12 @@ typedef struct gofann_graph {
     /* Optional per-row records (gofann_build_row_records), or NULL: row r at
      * records + r * record_stride holds the PQ code row of its sample
      * (pq_dim bytes), then at byte GOFANN_RECORD_META(pq_dim) three uint32:
-     * the sample id, the start and the length of its label-CSR row.  One
-     * 64-byte line per row at config-2 shape: scoring and predicate checks of
-     * a candidate read one line instead of following row -> sample -> code
-     * and sample -> CSR offsets.  Results are the same with or without. */
+     * the sample id, the start and the length of its label-CSR row, then,
+     * 16 bytes further, the label row itself when it has at most
+     * GOFANN_RECORD_INLINE_LABELS labels.  One 128-byte line per row at
+     * config-2 shape: scoring and predicate checks of a candidate read one
+     * line instead of following row -> sample -> code and sample -> CSR
+     * offsets -> labels.  Results are the same with or without. */
     const uint8_t* records;
     uint32_t record_stride;          /* bytes, a multiple of 16 */
     uint32_t reserved2;
@@ -117,6 +119,8 @@ typedef struct gofann_graph {
 
 /* Byte offset of a record's (sample, label start, label length) words. */
 #define GOFANN_RECORD_META(pq_dim) ((((pq_dim) + 15u) / 16u) * 16u)
+/* Label rows of at most this many labels are stored in the record. */
+#define GOFANN_RECORD_INLINE_LABELS 16u
 
 /* Per-sample attributes: sample-major label CSR (sorted, unique per row) and
  * float range values (SparseLabelMatrix / base_range_values). */
@@ -337,7 +341,8 @@ GOFANN_API int gofann_shard_merge(const uint32_t* shard_ids, const float* shard_
                        void* stream);
 
 /* Per-row records for the traversal (see gofann_graph.records): record_stride
- * = GOFANN_RECORD_META(pq_dim) + 16 rounded to 16 (64 bytes at pq_dim 48);
+ * = GOFANN_RECORD_META(pq_dim) + 16 + 4 * GOFANN_RECORD_INLINE_LABELS (128
+ * bytes at pq_dim 48);
  * out: device [total_rows][record_stride].  Label CSR offsets must fit in
  * 32 bits (fails with GOFANN_ERR_UNSUPPORTED otherwise, checked on the
  * device through `status`, which may be NULL). */

@@ -265,7 +265,8 @@ def _with_records(L, graph, attrs, codes):
 
 def test_row_records_layout(L):
     """Record r = code row of sample row_to_sample[r], then (sample, label
-    start, label length) at GOFANN_RECORD_META(pq_dim)."""
+    start, label length) at GOFANN_RECORD_META(pq_dim), then the label row
+    itself when it has at most 16 labels."""
     w, idx, plan = cfg2_small()
     g, rec = _with_records(L, idx.graph(), idx.attrs(), idx.codes())
     rec = rec.cpu().numpy()
@@ -278,6 +279,17 @@ def test_row_records_layout(L):
     assert np.array_equal(words[:, 0], r2s)
     assert np.array_equal(words[:, 1], ip[r2s])
     assert np.array_equal(words[:, 2], ip[r2s + 1] - ip[r2s])
+    assert rec.shape[1] == meta + 16 + 4 * 16
+    labels = rec[:, meta + 16:meta + 16 + 64].copy().view(np.uint32)
+    ind = idx.attrs()["label_indices"]
+    checked = 0
+    for r in range(0, rec.shape[0], max(1, rec.shape[0] // 500)):
+        n_lab = int(ip[r2s[r] + 1] - ip[r2s[r]])
+        if n_lab <= 16:
+            assert np.array_equal(labels[r, :n_lab], ind[ip[r2s[r]]:ip[r2s[r] + 1]])
+            assert not labels[r, n_lab:].any()
+            checked += 1
+    assert checked > 0
 
 
 @pytest.mark.parametrize("vi,mode", [(0, A.PQ_U8), (5, A.PQ_U8), (6, A.PQ_U8), (1, A.PQ_LUT_GLOBAL),
