@@ -79,7 +79,7 @@ struct BeamArgs {
 };
 
 struct SmemLayout {
-    uint32_t frontier, topk, stop, list, dist, prio, state, table, total;
+    uint32_t frontier, topk, stop, list, dist, prio, cbucket, cfree, state, table, total;
 };
 
 __host__ __device__ inline uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
@@ -96,6 +96,8 @@ __host__ __device__ inline SmemLayout smem_layout(const gofann_search_params& p,
     s.list = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
     s.dist = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
     s.prio = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
+    s.cbucket = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
+    s.cfree = o; o = align16(o + GOFANN_MAX_DEGREE * 4);
     s.state = o; o = align16(o + sizeof(WarpState));
     s.table = o;
     if (p.scorer == GOFANN_SCORER_PQ) {
@@ -262,6 +264,8 @@ struct WarpBufs {
     uint32_t* list;
     float* dist;
     float* prio;
+    uint32_t* cbucket;  // per listed candidate: the bucket its test ended in
+    uint32_t* cfree;    // ... and that bucket's free-slot mask
     WarpState* st;
     uint32_t* hash;
 };
@@ -462,9 +466,16 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
 #pragma unroll
         for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
             const uint32_t idx = nb[half];
-            const bool keep = idx != kU32Max && !hash_test(hash, idx);
+            BucketProbe pr{kU32Max, 0u, true};
+            if (idx != kU32Max) pr = bucket_probe(hash, idx);
+            const bool keep = !pr.found;
             const unsigned m = __ballot_sync(kFull, keep);
-            if (keep) list[len + __popc(m & ((1u << lane) - 1u))] = idx;
+            if (keep) {
+                const int pos = len + __popc(m & ((1u << lane) - 1u));
+                list[pos] = idx;
+                w.cbucket[pos] = pr.bucket;
+                w.cfree[pos] = pr.free_mask;
+            }
             len += __popc(m);
         }
         __syncwarp();
@@ -573,9 +584,38 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
             __syncwarp();
         }
         if (!st.serial_hash) {
+            // each admitted row takes the free slot its test saw, ranked among
+            // the admitted rows whose tests ended in the same bucket (nothing
+            // else wrote the table since): plain stores; a bucket that runs out
+            // sends the rest to the atomic walk, after the stores
+            const uint32_t adm0 = st.adm[0], adm1 = st.adm[1];
+            bool overflow[GOFANN_MAX_DEGREE / kWarp] = {false, false};
+#pragma unroll
+            for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
+                const int i = half * kWarp + lane;
+                if (((half == 0 ? adm0 : adm1) >> lane) & 1u) {
+                    const uint32_t b = w.cbucket[i];
+                    int rank = 0;
+#pragma unroll
+                    for (int h2 = 0; h2 < GOFANN_MAX_DEGREE / kWarp; ++h2) {
+                        uint32_t before = h2 == 0 ? adm0 : adm1;
+                        if (h2 > half) before = 0u;
+                        else if (h2 == half) before &= (1u << lane) - 1u;
+                        while (before) {
+                            const int j = h2 * kWarp + __ffs(before) - 1;
+                            before &= before - 1;
+                            rank += w.cbucket[j] == b ? 1 : 0;
+                        }
+                    }
+                    const int slot = b == kU32Max ? -1 : nth_set_bit(w.cfree[i], rank);
+                    if (slot >= 0) hash[b * kBucketSlots + slot] = list[i];
+                    else overflow[half] = true;
+                }
+            }
+            __syncwarp();
 #pragma unroll
             for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half)
-                if ((st.adm[half] >> lane) & 1u) hash_add_concurrent(hash, list[half * kWarp + lane]);
+                if (overflow[half]) hash_add_concurrent(hash, list[half * kWarp + lane]);
         }
         __syncwarp();
         if (step == 1) {
@@ -597,7 +637,7 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
         for (int h = 0; h < GOFANN_MAX_DEGREE / kWarp; ++h) {
             nb[h] = nb_next[h];
             if (nb[h] != kU32Max && !st.exhausted) {
-                prefetch_l1(hash + hash_code(nb[h]));
+                prefetch_l1(hash + home_bucket(nb[h]) * kBucketSlots);
                 if (kScorer == GOFANN_SCORER_PQ && a.graph.records)
                     prefetch_l2(a.graph.records + static_cast<size_t>(label_offset + nb[h]) * a.graph.record_stride);
             }
@@ -675,6 +715,8 @@ __global__ void __launch_bounds__(block_warps<kMode>() * 32, min_blocks<kMode>()
     w.list = reinterpret_cast<uint32_t*>(base + L.list);
     w.dist = reinterpret_cast<float*>(base + L.dist);
     w.prio = reinterpret_cast<float*>(base + L.prio);
+    w.cbucket = reinterpret_cast<uint32_t*>(base + L.cbucket);
+    w.cfree = reinterpret_cast<uint32_t*>(base + L.cfree);
     w.st = reinterpret_cast<WarpState*>(base + L.state);
     float* table = reinterpret_cast<float*>(base + L.table);
     const uint32_t gwarp = blockIdx.x * (blockDim.x >> 5) + warp;

@@ -117,8 +117,8 @@ __device__ __forceinline__ float butterfly_sum32(float (&v)[32])
 }
 
 // ------------------------------------------------------------ visited hash
-// native_visited_hash.cuh:11-61: multiplicative mix modulo 4096, linear
-// probing, UINT32_MAX = empty, a full table silently drops the insert.
+// native_visited_hash.cuh:11-61: multiplicative mix modulo 4096, UINT32_MAX
+// = empty, a full table silently drops the insert.
 __device__ __forceinline__ uint32_t hash_code(uint32_t v)
 {
     const uint64_t mixed = static_cast<uint64_t>(v) ^
@@ -126,42 +126,75 @@ __device__ __forceinline__ uint32_t hash_code(uint32_t v)
                            0xa0ab69ccd854fc0aULL;
     return static_cast<uint32_t>(mixed % kHashCap);
 }
-__device__ __forceinline__ bool hash_test(const uint32_t* t, uint32_t v)
+// The traversal's tables use a bucketed layout of the same 4,096 slots.  The
+// reference's table answers one question -- was this row inserted -- and
+// drops an insert exactly when all 4,096 slots are taken; any exact set of
+// 4,096 slots with that rule answers identically.  Here the slots form 512
+// buckets of 8 (one 32-byte sector); a value's home bucket is
+// hash_code(v) / 8, and a value lives in the first bucket of its probe
+// sequence (home, home + 1, ... mod 512) that had a free slot when it was
+// inserted.  Nothing is ever removed, so a bucket holding a free slot ends
+// every probe sequence that reaches it: a test reads one sector, and the
+// free-slot mask it sees tells where the value would go.
+constexpr int kBucketSlots = 8;
+constexpr int kBuckets = kHashCap / kBucketSlots;
+
+__device__ __forceinline__ uint32_t home_bucket(uint32_t v) { return hash_code(v) / kBucketSlots; }
+
+struct BucketProbe {
+    uint32_t bucket;     // bucket holding v, or the first with a free slot (kU32Max: table full)
+    uint32_t free_mask;  // free slots of that bucket (bit j = slot j)
+    bool found;
+};
+__device__ __forceinline__ BucketProbe bucket_probe(const uint32_t* t, uint32_t v)
 {
-    uint32_t s = hash_code(v);
-    for (int p = 0; p < kHashCap; ++p) {
-        const uint32_t x = t[s];
-        if (x == kU32Max) return false;
-        if (x == v) return true;
-        s = (s + 1) & (kHashCap - 1);
+    uint32_t b = home_bucket(v);
+    for (int n = 0; n < kBuckets; ++n) {
+        const uint4* q = reinterpret_cast<const uint4*>(t + b * kBucketSlots);
+        const uint4 x = q[0], y = q[1];
+        const uint32_t w[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
+        uint32_t fm = 0;
+        bool hit = false;
+#pragma unroll
+        for (int j = 0; j < kBucketSlots; ++j) {
+            hit = hit || w[j] == v;
+            fm |= (w[j] == kU32Max ? 1u : 0u) << j;
+        }
+        if (hit) return {b, fm, true};
+        if (fm) return {b, fm, false};
+        b = (b + 1) & (kBuckets - 1);
     }
-    return false;
+    return {kU32Max, 0u, false};
 }
+__device__ __forceinline__ bool hash_test(const uint32_t* t, uint32_t v) { return bucket_probe(t, v).found; }
 // Returns true when v was inserted (false: already present, or table full).
 __device__ __forceinline__ bool hash_add(uint32_t* t, uint32_t v)
 {
-    uint32_t s = hash_code(v);
-    for (int p = 0; p < kHashCap; ++p) {
-        const uint32_t x = t[s];
-        if (x == v) return false;
-        if (x == kU32Max) { t[s] = v; return true; }
-        s = (s + 1) & (kHashCap - 1);
-    }
-    return false;
+    const BucketProbe pr = bucket_probe(t, v);
+    if (pr.found || pr.bucket == kU32Max) return false;
+    t[pr.bucket * kBucketSlots + __ffs(pr.free_mask) - 1] = v;
+    return true;
 }
-// Concurrent insertion of distinct absent values by several lanes.  The slot
-// a value lands in can differ from the one-at-a-time order, but membership --
-// the only thing hash_test reads -- is the same as long as the table cannot
-// fill (with linear probing over all slots an insertion fails only when every
-// slot is taken), which the caller guarantees.
+// Concurrent insertion of distinct absent values by several lanes, with
+// atomics: the slot a value lands in can differ from the one-at-a-time
+// order, but membership -- the only thing a test reads -- is the same as long
+// as the table cannot fill, which the caller guarantees.
 __device__ __forceinline__ void hash_add_concurrent(uint32_t* t, uint32_t v)
 {
-    uint32_t s = hash_code(v);
-    for (int p = 0; p < kHashCap; ++p) {
-        const uint32_t x = atomicCAS(t + s, kU32Max, v);
-        if (x == kU32Max || x == v) return;
-        s = (s + 1) & (kHashCap - 1);
+    uint32_t b = home_bucket(v);
+    for (int n = 0; n < kBuckets; ++n) {
+        for (int j = 0; j < kBucketSlots; ++j) {
+            const uint32_t x = atomicCAS(t + b * kBucketSlots + j, kU32Max, v);
+            if (x == kU32Max || x == v) return;
+        }
+        b = (b + 1) & (kBuckets - 1);
     }
+}
+// k-th set bit (0-based) of m, or -1.
+__device__ __forceinline__ int nth_set_bit(uint32_t m, int k)
+{
+    for (int r = 0; r < k; ++r) m &= m - 1;
+    return m ? __ffs(m) - 1 : -1;
 }
 
 // ---------------------------------------------------------------- frontier

@@ -347,6 +347,46 @@ def test_beam_search_pq_ties_bitexact(L, share, vi):
         assert np.array_equal(g, o), f"{name} differ in {np.count_nonzero(np.any(np.atleast_2d(g != o), axis=-1))} routes"
 
 
+def _chain_graph(n=12000, fwd=48, back=16):
+    """Row r scores 65535 - r (codes (r >> 8, r & 255) against a table whose
+    entries are exact integers) and links the next `fwd` and the previous
+    `back` rows: every expansion admits fresh rows, so a route admits far
+    more than 4,096 rows, and the backward links meet rows whose inserts a
+    full visited table dropped."""
+    deg = fwd + back
+    r = np.arange(n, dtype=np.int64)[:, None]
+    off = np.concatenate([np.arange(1, fwd + 1), -np.arange(1, back + 1)])[None, :]
+    adj = r + off
+    adj = np.where((adj >= 0) & (adj < n), adj, 0xFFFFFFFF).astype(np.uint32)
+    graph = {"adjacency": adj, "row_to_sample": np.arange(n, dtype=np.uint32),
+             "label_offset": np.zeros(1, np.uint32)}
+    attrs = {"label_indptr": np.arange(n + 1, dtype=np.uint64), "label_indices": np.zeros(n, np.uint32)}
+    codes = {"pq_codes": np.stack([np.arange(n) >> 8, np.arange(n) & 255], 1).astype(np.uint8)}
+    lut = np.zeros((1, 2, 256), np.float32)
+    lut[0, 0] = 256.0 * (255 - np.arange(256))
+    lut[0, 1] = 255 - np.arange(256)
+    starts = np.array([0, 5, 300, 1000], np.uint32)
+    routes = {"query_row": np.zeros(len(starts), np.uint32), "group_id": np.zeros(len(starts), np.uint32),
+              "start_local": starts}
+    return graph, attrs, codes, lut, routes
+
+
+@pytest.mark.parametrize("queue_size", [64, 512])
+def test_beam_search_visited_table_fills(L, queue_size):
+    """Routes that admit more than 4,096 rows: the visited table fills and
+    drops later inserts exactly as the reference's does."""
+    graph, attrs, codes, lut, routes = _chain_graph()
+    params = dict(queue_size=queue_size, predicate_bias=0, early_stop_mode=A.EARLY_STOP_OFF, max_steps=400,
+                  result_width=100, scorer=A.SCORER_PQ, pq_mode=A.PQ_LUT_GLOBAL)
+    want = O.beam_search(graph, attrs, codes, {"pq_lut": lut}, routes, threads=4, trace_width=64, **params)
+    assert want[3][:, 3].min() > 4096, "a route did not fill its visited table"
+    got = run_gpu_beam(L, graph, attrs, codes, {"pq_lut": dev(lut)}, routes, trace_width=64, **params)
+    for name, g, o in zip(("ids", "dists", "steps", "counters", "trace"), got, want):
+        if name == "dists":
+            g, o = fbits(g), fbits(o)
+        assert np.array_equal(g, o), name
+
+
 @pytest.mark.parametrize("vi", [0, 1, 3])
 def test_beam_search_rabitq_bitexact(L, vi):
     w, idx, plan, rq, anchors, qr = rabitq_artifacts()
