@@ -324,18 +324,26 @@ def run_gofann(args):
                        "graph_rows": idx.stats.get("graph_rows"), "label_graphs": idx.stats.get("groups"),
                        "pq_mode": PQ_MODE_NAMES.get(args.pq_mode, str(args.pq_mode)),
                        "l2_flush": "inputs larger than L2 (index ~25 GB resident, rows read at random)",
+                       "planning": "route planning runs before the timed region, as the reference's query "
+                                   "preparation does (validate_and_prepare_queries runs before qps_start)",
                        "parallelism": f"shard{world}" if world > 1 else "single"},
             "e2e": {"value": round(nq / (e_ms / 1e3), 1), "unit": "queries/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(nq * k * 8)},
             "gpu_launches": int(pipe.launches_per_run * args.steps + (2 * args.steps if world > 1 else 0)),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                         "traffic_source": ("scaled: DRAM bytes per algorithmic byte of an ncu capture of the same "
+                                            "kernel at n=1M (profiles/beam_search_config2_traffic.json) x this "
+                                            "launch's algorithmic bytes") if traffic is not None else None,
                          "kernel": "beam_search_kernel", "kernel_ms": round(beam_ms, 3),
                          "algorithmic_bytes_per_launch": int(bytes_launch), "peak_source": peaks["source"]},
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(args, data, idx, plan, chosen, t0)
+            gpu_res = {"final_ids": pipe.out_ids.cpu().numpy().view(np.uint32), "final_d": pipe.out_d.cpu().numpy(),
+                       "beam_ids": pipe.g_ids[:dplan.n_graph].cpu().numpy().view(np.uint32),
+                       "beam_d": pipe.g_d[:dplan.n_graph].cpu().numpy()}
+            line["cpu_baseline"], line["parity"] = cpu_baseline(args, data, idx, plan, chosen, t0, gpu_res)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -358,8 +366,10 @@ def host_index(idx):
 
 def cpu_search(hidx, plan, qv, sel, qs, threads):
     """The reference's path on host cores for the queries `sel`: LUT build,
-    traversal, posting scans, exact rerank (oracle restatement).  Route
-    tables are re-based onto the compact query sample."""
+    traversal, posting scans, exact rerank and the route -> query merge
+    (oracle restatement).  Route tables are re-based onto the compact query
+    sample.  Returns the traversal shortlists and the merged top-10 of the
+    sample (rows in `sel` order)."""
     from gofann.planner import subset_routes
     from oracle import oracle as O
     from gofann import _abi as A
@@ -373,14 +383,19 @@ def cpu_search(hidx, plan, qv, sel, qs, threads):
     gr["query_row"] = pos[plan.graph_query[gsel]].astype(np.uint32)
     pr = subset_routes(plan.posting_routes, psel)
     pr["query_row"] = pos[plan.posting_query[psel]].astype(np.uint32)
-    ids, _, _, _ = O.beam_search(hidx["graph"], hidx["attrs"], hidx["codes"], {"pq_lut": lut}, gr, threads=threads,
-                                 queue_size=qs, result_width=100, predicate_bias=1, alpha=0.15,
-                                 early_stop_mode=A.EARLY_STOP_ADAPTIVE)
+    ids, bd, _, _ = O.beam_search(hidx["graph"], hidx["attrs"], hidx["codes"], {"pq_lut": lut}, gr, threads=threads,
+                                  queue_size=qs, result_width=100, predicate_bias=1, alpha=0.15,
+                                  early_stop_mode=A.EARLY_STOP_ADAPTIVE)
     ri, rd = O.rerank(hidx["base"], A.DTYPE_U8, qs_v, hidx["attrs"], gr, ids, 10)
     pi, _ = O.posting_scan(hidx["codes"], {"pq_lut": lut}, hidx["attrs"], pr, A.SCORER_PQ, hidx["posting_ids"],
                            plan.posting_begin[psel], plan.posting_count[psel], 100)
     pri, prd = O.rerank(hidx["base"], A.DTYPE_U8, qs_v, hidx["attrs"], pr, pi, 10)
-    return ri, pri
+    r2q = np.concatenate([gr["query_row"], pr["query_row"]]).astype(np.int64)
+    order = np.argsort(r2q, kind="stable").astype(np.uint32)
+    qoff = np.zeros(len(sel) + 1, np.uint32)
+    qoff[1:] = np.cumsum(np.bincount(r2q, minlength=len(sel)))
+    fi, fd = O.route_merge(np.concatenate([ri, pri]), np.concatenate([rd, prd]), qoff, order, 10)
+    return {"gsel": gsel, "beam_ids": ids, "beam_d": bd, "final_ids": fi, "final_d": fd}
 
 
 def sized_sample(hidx, plan, qv, qs, threads, target_s=12.0, first=400, seed=1):
@@ -394,9 +409,12 @@ def sized_sample(hidx, plan, qv, qs, threads, target_s=12.0, first=400, seed=1):
     return np.sort(rng.choice(qv.shape[0], size=n, replace=False))
 
 
-def cpu_baseline(args, data, idx, plan, qs, t0):
+def cpu_baseline(args, data, idx, plan, qs, t0, gpu=None):
     """Oracle restatement of the reference path, timed on this box's host
-    cores over a query sample sized to ~12 s of CPU work."""
+    cores over a query sample sized to ~12 s of CPU work.  With `gpu` (the
+    GPU arm's final top-10 ids and distances for every query, and its
+    traversal shortlists per graph route), the sample's results are also
+    compared with the GPU arm's: full-size parity on the benchmark index."""
     from oracle import oracle as O
     from gofann import workload_gpu as W
     threads = O.cpu_count()
@@ -406,12 +424,29 @@ def cpu_baseline(args, data, idx, plan, qs, t0):
     sel = (np.sort(np.random.default_rng(1).choice(qv.shape[0], args.cpu_sample, replace=False))
            if args.cpu_sample else sized_sample(hidx, plan, qv, qs, threads))
     tt = time.perf_counter()
-    cpu_search(hidx, plan, qv, sel, qs, threads)
+    res = cpu_search(hidx, plan, qv, sel, qs, threads)
     el = time.perf_counter() - tt
     W._log(f"CPU baseline: {len(sel)} queries in {el:.1f} s", t0)
-    return {"value": round(len(sel) / el, 1), "unit": "queries/s", "cores": threads, "kind": "port",
+    base = {"value": round(len(sel) / el, 1), "unit": "queries/s", "cores": threads, "kind": "port",
             "sample": f"{len(sel)} of {qv.shape[0]} config-2 queries, queue {qs}; LUT build + traversal + "
-                      f"posting scans + exact rerank, {el:.1f} s on {threads} threads"}
+                      f"posting scans + exact rerank + route merge, {el:.1f} s on {threads} threads"}
+    parity = None
+    if gpu is not None:
+        gi, gd = gpu["final_ids"][sel], gpu["final_d"][sel]
+        bi, bdist = gpu["beam_ids"][res["gsel"]], gpu["beam_d"][res["gsel"]]
+        parity = {"checked_queries": int(len(sel)),
+                  "id_mismatches": int(np.any(gi != res["final_ids"], axis=1).sum()),
+                  "dist_bit_mismatches": int(np.any(gd.view(np.uint32) != res["final_d"].view(np.uint32), axis=1).sum()),
+                  "checked_graph_routes": int(len(res["gsel"])),
+                  "shortlist_id_mismatches": int(np.any(bi != res["beam_ids"], axis=1).sum()),
+                  "shortlist_dist_bit_mismatches": int(np.any(bdist.view(np.uint32) != res["beam_d"].view(np.uint32),
+                                                              axis=1).sum()),
+                  "oracle": "CPU restatement of the reference path (oracle/), same index and queries"}
+        parity["status"] = "green" if (parity["id_mismatches"] + parity["dist_bit_mismatches"] +
+                                       parity["shortlist_id_mismatches"] + parity["shortlist_dist_bit_mismatches"]) == 0 \
+            else "red"
+        W._log(f"full-size parity: {parity}", t0)
+    return base, parity
 
 
 def run_reference(args):

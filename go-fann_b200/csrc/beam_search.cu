@@ -212,28 +212,35 @@ struct Scorer {
     }
 };
 
-// Cooperative pickup (backend_pq.cu:844-893): the unused entry with the
-// smallest key, lowest heap index on ties; lane 0 copies and marks it.  The
-// order is taken as one 64-bit key (order-preserving float bits, with -0
-// folded onto +0, above the index) reduced by an xor-shuffle min: exact for
-// every finite or infinite key and NaN-safe.  (The reference's tie clause
-// `!(b < a) && !(a < b) && ia < ib` inside a shfl_down tree was observed to
-// keep the larger index on sm_100a with nvcc 12.9 -O3.)
+// Cooperative pickup (backend_pq.cu:844-893; RaBitQ backend_rabitq.cu:
+// 924-970): lane l scans entries l+1, l+33, ... keeping its first unused
+// entry of smallest key, then a shfl_down tree merges lane l+off into lane l
+// for off = 16..1.  In the reference as compiled for sm_100a a merge replaces
+// the receiving lane's candidate only by a strictly smaller key (run on a
+// B200 on tie-heavy frontiers: the source's equal-key index tie-break never
+// takes effect), so among lanes holding the minimum the tree's merge order
+// decides: lane 0 absorbs lanes 16, 8, 24, 4, 20, ... -- the order of the
+// 5-bit-reversed lane index.  The pick is therefore the minimum of (key,
+// bit-reversed lane, position within the lane), found here with two warp
+// min-reductions; keys compare by their order-preserving bit pattern (equal
+// to float order for the non-NaN keys a frontier holds, -0 folded onto +0).
 __device__ __forceinline__ bool smmh_pickup(const Smmh& h, int size, FPair* out, int lane)
 {
-    unsigned long long best = ~0ull;
-    for (int i = lane + 1; i < size; i += kWarp) {
+    uint32_t best = kU32Max, pos = 0;
+    int k = 0;
+    for (int i = lane + 1; i < size; i += kWarp, ++k) {
         if (h.val[i] & kPoolUsed) continue;
-        const unsigned long long k = (static_cast<unsigned long long>(ordered_bits(h.key[i])) << 32) |
-                                     static_cast<uint32_t>(i);
-        best = k < best ? k : best;
+        const uint32_t kb = ordered_bits(h.key[i]);
+        if (kb < best) {
+            best = kb;
+            pos = static_cast<uint32_t>(k);
+        }
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-        const unsigned long long o = __shfl_xor_sync(kFull, best, off);
-        best = o < best ? o : best;
-    }
-    const int bi = best == ~0ull ? -1 : static_cast<int>(best & 0xffffffffu);
+    const uint32_t m = __reduce_min_sync(kFull, best);
+    const uint32_t rank = best == m && m != kU32Max ? ((__brev(static_cast<uint32_t>(lane)) >> 27) << 16) | pos
+                                                    : kU32Max;
+    const uint32_t w = __reduce_min_sync(kFull, rank);
+    const int bi = w == kU32Max ? -1 : static_cast<int>((__brev(w >> 16) >> 27) + 1 + kWarp * (w & 0xffffu));
     if (lane == 0 && bi >= 0) {
         out->first = h.key[bi];
         out->second = h.val[bi];
@@ -587,14 +594,21 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
             // each admitted row takes the free slot its test saw, ranked among
             // the admitted rows whose tests ended in the same bucket (nothing
             // else wrote the table since): plain stores; a bucket that runs out
-            // sends the rest to the atomic walk, after the stores
+            // sends the rest to the atomic walk, after the stores.  An
+            // adjacency row that lists an id twice admits both copies (as the
+            // reference does: both pass the same step's visited test) but the
+            // reference's second insert of it is a no-op; equal ids end their
+            // tests in the same bucket, so a repeat shows up in the rank scan,
+            // and a step with one inserts one by one in list order instead.
             const uint32_t adm0 = st.adm[0], adm1 = st.adm[1];
-            bool overflow[GOFANN_MAX_DEGREE / kWarp] = {false, false};
+            int slot[GOFANN_MAX_DEGREE / kWarp] = {-1, -1};
+            bool repeat = false;
 #pragma unroll
             for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half) {
                 const int i = half * kWarp + lane;
                 if (((half == 0 ? adm0 : adm1) >> lane) & 1u) {
                     const uint32_t b = w.cbucket[i];
+                    const uint32_t v = list[i];
                     int rank = 0;
 #pragma unroll
                     for (int h2 = 0; h2 < GOFANN_MAX_DEGREE / kWarp; ++h2) {
@@ -604,18 +618,32 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
                         while (before) {
                             const int j = h2 * kWarp + __ffs(before) - 1;
                             before &= before - 1;
-                            rank += w.cbucket[j] == b ? 1 : 0;
+                            if (w.cbucket[j] == b) {
+                                ++rank;
+                                repeat |= list[j] == v;
+                            }
                         }
                     }
-                    const int slot = b == kU32Max ? -1 : nth_set_bit(w.cfree[i], rank);
-                    if (slot >= 0) hash[b * kBucketSlots + slot] = list[i];
-                    else overflow[half] = true;
+                    slot[half] = b == kU32Max ? -1 : nth_set_bit(w.cfree[i], rank);
+                    if (slot[half] < 0) slot[half] = -2;  // bucket ran out: atomic walk
                 }
             }
-            __syncwarp();
+            if (__any_sync(kFull, repeat)) {
+                if (lane == 0) {
+                    int added = 0;
+                    for (int i = 0; i < len; ++i)
+                        if (((i < kWarp ? adm0 : adm1) >> (i & 31)) & 1u) added += hash_add(hash, list[i]) ? 1 : 0;
+                    st.hash_count += added - (__popc(adm0) + __popc(adm1));  // n_adm was counted already
+                }
+            } else {
 #pragma unroll
-            for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half)
-                if (overflow[half]) hash_add_concurrent(hash, list[half * kWarp + lane]);
+                for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half)
+                    if (slot[half] >= 0) hash[w.cbucket[half * kWarp + lane] * kBucketSlots + slot[half]] = list[half * kWarp + lane];
+                __syncwarp();
+#pragma unroll
+                for (int half = 0; half < GOFANN_MAX_DEGREE / kWarp; ++half)
+                    if (slot[half] == -2) hash_add_concurrent(hash, list[half * kWarp + lane]);
+            }
         }
         __syncwarp();
         if (step == 1) {
@@ -890,6 +918,129 @@ uint32_t cap_blocks(uint32_t blocks, const gofann_search_params& p, int wpb, int
 
 constexpr size_t kCounterBytes = 256;  // route counter, kept 256-byte aligned
 
+// A validated traversal call, sized for launch: the kernel arguments (the
+// scratch pointers still unset), the variant, its block shape and shared
+// memory, and the persistent grid before any scratch cap.
+struct LaunchPlan {
+    BeamArgs args;
+    KernelFn kern;
+    int wpb;
+    size_t smem;
+    uint32_t blocks;
+};
+
+// Checks a call's arguments (both traversal entry points share the rules and
+// the messages, prefixed with `who`) and, when there are routes, picks the
+// kernel variant and sizes its launch.
+int plan_launch(const gofann_graph* graph, const gofann_attrs* attrs, const gofann_codes* codes,
+                const gofann_prepared* prep, const gofann_routes* routes, const gofann_search_params* params,
+                const gofann_search_out* out, const char* who, LaunchPlan& lp)
+{
+    if (!graph || !codes || !prep || !routes || !params || !out) return fail(GOFANN_ERR_INVALID, "%s: null argument", who);
+    const gofann_search_params& p = *params;
+    if (p.queue_size < 2 || p.queue_size > GOFANN_MAX_QUEUE)
+        return fail(GOFANN_ERR_INVALID, "%s: queue_size %d outside 2..%d", who, p.queue_size, GOFANN_MAX_QUEUE);
+    if (p.stop_width < 1 || p.stop_width > GOFANN_MAX_TOPK)
+        return fail(GOFANN_ERR_INVALID, "%s: stop_width %d outside 1..%d", who, p.stop_width, GOFANN_MAX_TOPK);
+    if (p.result_width < 1 || p.result_width > GOFANN_MAX_RESULT_WIDTH)
+        return fail(GOFANN_ERR_INVALID, "%s: result_width %d outside 1..%d", who, p.result_width,
+                    GOFANN_MAX_RESULT_WIDTH);
+    if (p.early_stop_mode < 0 || p.early_stop_mode > 2)
+        return fail(GOFANN_ERR_INVALID, "%s: unknown early_stop_mode %d", who, p.early_stop_mode);
+    if (p.resident_warps < 0)
+        return fail(GOFANN_ERR_INVALID, "%s: resident_warps %d is negative", who, p.resident_warps);
+    if (!graph->adjacency || !graph->row_to_sample || !graph->label_offset || graph->degree == 0)
+        return fail(GOFANN_ERR_INVALID, "%s: graph arrays missing", who);
+    const uint32_t min_stride = GOFANN_RECORD_META(codes->pq_dim) + 16u + 4u * GOFANN_RECORD_INLINE_LABELS;
+    if (graph->records && p.scorer == GOFANN_SCORER_PQ &&
+        ((graph->record_stride & 15u) != 0 || (reinterpret_cast<uintptr_t>(graph->records) & 15) != 0 ||
+         graph->record_stride < min_stride))
+        return fail(GOFANN_ERR_INVALID, "%s: row records need 16-byte alignment and a stride of at least %u", who,
+                    min_stride);
+    if (!routes->query_row || !routes->group_id || !routes->start_local || !out->ids || !out->dists)
+        return fail(GOFANN_ERR_INVALID, "%s: route or output arrays missing", who);
+    const bool needs_attrs = routes->pred_offsets != nullptr || p.full_label_check != 0 ||
+                             routes->range_modes != nullptr;
+    if (needs_attrs && (!attrs || !attrs->label_indptr || !attrs->label_indices))
+        return fail(GOFANN_ERR_INVALID, "%s: predicates need the sample label CSR", who);
+    if (routes->pred_offsets && (!routes->clauses || !routes->pred_handles))
+        return fail(GOFANN_ERR_INVALID, "%s: predicate clause arrays missing", who);
+    int pq_mode = GOFANN_PQ_LUT_GLOBAL;
+    bool w4 = false, small_m = true;
+    if (p.scorer == GOFANN_SCORER_PQ) {
+        if (!codes->pq_codes) return fail(GOFANN_ERR_INVALID, "%s: PQ codes missing", who);
+        if (codes->pq_dim == 0 || codes->pq_dim > static_cast<uint32_t>(kMaxPqDim))
+            return fail(GOFANN_ERR_UNSUPPORTED, "%s: pq_dim %u outside 1..%d", who, codes->pq_dim, kMaxPqDim);
+        const int st = check_pq_mode(p, *codes, *prep, w4, small_m, who);
+        if (st != GOFANN_OK) return st;
+        pq_mode = p.pq_mode;
+    } else if (p.scorer == GOFANN_SCORER_RABITQ) {
+        if (!codes->rq_codes || !codes->rq_factors || !codes->rq_anchor_ids || !prep->rq_q8 || !prep->rq_scale ||
+            !prep->rq_k1xsumq || !prep->rq_centroid_dist)
+            return fail(GOFANN_ERR_INVALID, "%s: RaBitQ arrays missing", who);
+        if (codes->padded_dim == 0 || codes->padded_dim % 64 != 0 || codes->padded_dim > 4096)
+            return fail(GOFANN_ERR_UNSUPPORTED, "%s: padded_dim %u unsupported", who, codes->padded_dim);
+    } else {
+        return fail(GOFANN_ERR_INVALID, "%s: unknown scorer %d", who, p.scorer);
+    }
+    lp = LaunchPlan{};
+    if (routes->n_routes == 0) return GOFANN_OK;
+
+    BeamArgs& args = lp.args;
+    args.graph = *graph;
+    if (attrs) {
+        args.attrs.indptr = attrs->label_indptr;
+        args.attrs.indices = attrs->label_indices;
+        args.attrs.ranges = attrs->range_values;
+        args.attrs.n_samples = attrs->n_samples;
+        args.attrs.range_count = attrs->range_count;
+    }
+    args.codes = *codes;
+    args.prep = *prep;
+    args.routes = *routes;
+    args.p = p;
+    args.out = *out;
+    args.status = out->status;
+    const SmemLayout L = smem_layout(p, *codes, pq_mode, prep->dim);
+    args.warp_smem = L.total;
+    // GOFANN_PQ_U8: the packed codebook ahead of the warps' areas
+    const bool u8 = pq_mode == GOFANN_PQ_U8 && p.scorer == GOFANN_SCORER_PQ;
+    args.block_smem = u8 ? static_cast<uint32_t>(codes->pq_dim * GOFANN_PQ_CENTROIDS * (prep->dim / codes->pq_dim))
+                         : 0u;
+    constexpr size_t kMaxSmem = 227 * 1024;
+    int wpb = u8 ? kU8BlockWarps : kWarpsPerBlock;
+    while (wpb > 1 && args.block_smem + static_cast<size_t>(L.total) * wpb > kMaxSmem) --wpb;
+    const size_t smem = args.block_smem + static_cast<size_t>(L.total) * wpb;
+    if (smem > kMaxSmem)
+        return fail(GOFANN_ERR_UNSUPPORTED, "%s: %zu bytes of shared memory per warp exceed 227 KB", who, smem);
+    const KernelFn kern = pick_kernel(p.scorer, p.predicate_bias != 0, pq_mode, w4, small_m);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_status(e, "beam_search: shared memory attribute");
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, wpb * 32, smem);
+    if (e != cudaSuccess) return cuda_status(e, "beam_search: occupancy query");
+    if (per_sm <= 0) return fail(GOFANN_ERR_UNSUPPORTED, "%s: kernel does not fit on an SM", who);
+    lp.kern = kern;
+    lp.wpb = wpb;
+    lp.smem = smem;
+    lp.blocks = cap_blocks(grid_blocks(routes->n_routes, wpb, per_sm), p, wpb, pq_mode, codes->pq_dim);
+    return GOFANN_OK;
+}
+
+// Clears the route counter at the head of `scratch` and launches `blocks`
+// persistent blocks whose warps take visited tables from after it.
+int launch_planned(LaunchPlan& lp, uint32_t blocks, void* scratch, void* stream, const char* what)
+{
+    lp.args.route_counter = static_cast<uint32_t*>(scratch);
+    lp.args.hash = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(scratch) + kCounterBytes);
+    cudaStream_t s = as_stream(stream);
+    cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(uint32_t), s);
+    if (e != cudaSuccess) return cuda_status(e, "beam_search: counter reset");
+    lp.kern<<<blocks, lp.wpb * 32, lp.smem, s>>>(lp.args);
+    GOFANN_CHECK_LAUNCH(what);
+    return GOFANN_OK;
+}
+
 }  // namespace
 }  // namespace gofann
 
@@ -915,102 +1066,14 @@ int gofann_beam_search(const gofann_graph* graph, const gofann_attrs* attrs, con
                        const gofann_search_params* params, const gofann_search_out* out, void* scratch,
                        size_t scratch_bytes, void* stream)
 {
-    if (!graph || !codes || !prep || !routes || !params || !out || !scratch)
-        return fail(GOFANN_ERR_INVALID, "beam_search: null argument");
-    const gofann_search_params& p = *params;
-    if (p.queue_size < 2 || p.queue_size > GOFANN_MAX_QUEUE)
-        return fail(GOFANN_ERR_INVALID, "beam_search: queue_size %d outside 2..%d", p.queue_size, GOFANN_MAX_QUEUE);
-    if (p.stop_width < 1 || p.stop_width > GOFANN_MAX_TOPK)
-        return fail(GOFANN_ERR_INVALID, "beam_search: stop_width %d outside 1..%d", p.stop_width, GOFANN_MAX_TOPK);
-    if (p.result_width < 1 || p.result_width > GOFANN_MAX_RESULT_WIDTH)
-        return fail(GOFANN_ERR_INVALID, "beam_search: result_width %d outside 1..%d", p.result_width,
-                    GOFANN_MAX_RESULT_WIDTH);
-    if (p.early_stop_mode < 0 || p.early_stop_mode > 2)
-        return fail(GOFANN_ERR_INVALID, "beam_search: unknown early_stop_mode %d", p.early_stop_mode);
-    if (p.resident_warps < 0)
-        return fail(GOFANN_ERR_INVALID, "beam_search: resident_warps %d is negative", p.resident_warps);
-    if (!graph->adjacency || !graph->row_to_sample || !graph->label_offset || graph->degree == 0)
-        return fail(GOFANN_ERR_INVALID, "beam_search: graph arrays missing");
-    if (graph->records && p.scorer == GOFANN_SCORER_PQ &&
-        ((graph->record_stride & 15u) != 0 || (reinterpret_cast<uintptr_t>(graph->records) & 15) != 0 ||
-         graph->record_stride < GOFANN_RECORD_META(codes->pq_dim) + 16u + 4u * GOFANN_RECORD_INLINE_LABELS))
-        return fail(GOFANN_ERR_INVALID, "beam_search: row records need 16-byte alignment and a stride of at least %u",
-                    GOFANN_RECORD_META(codes->pq_dim) + 16u + 4u * GOFANN_RECORD_INLINE_LABELS);
-    if (!routes->query_row || !routes->group_id || !routes->start_local || !out->ids || !out->dists)
-        return fail(GOFANN_ERR_INVALID, "beam_search: route or output arrays missing");
-    const bool needs_attrs = routes->pred_offsets != nullptr || p.full_label_check != 0 ||
-                             routes->range_modes != nullptr;
-    if (needs_attrs && (!attrs || !attrs->label_indptr || !attrs->label_indices))
-        return fail(GOFANN_ERR_INVALID, "beam_search: predicates need the sample label CSR");
-    if (routes->pred_offsets && (!routes->clauses || !routes->pred_handles))
-        return fail(GOFANN_ERR_INVALID, "beam_search: predicate clause arrays missing");
-    int pq_mode = GOFANN_PQ_LUT_GLOBAL;
-    bool w4 = false, small_m = true;
-    if (p.scorer == GOFANN_SCORER_PQ) {
-        if (!codes->pq_codes) return fail(GOFANN_ERR_INVALID, "beam_search: PQ codes missing");
-        if (codes->pq_dim == 0 || codes->pq_dim > static_cast<uint32_t>(kMaxPqDim))
-            return fail(GOFANN_ERR_UNSUPPORTED, "beam_search: pq_dim %u outside 1..%d", codes->pq_dim, kMaxPqDim);
-        const int st = check_pq_mode(p, *codes, *prep, w4, small_m, "beam_search");
-        if (st != GOFANN_OK) return st;
-        pq_mode = p.pq_mode;
-    } else if (p.scorer == GOFANN_SCORER_RABITQ) {
-        if (!codes->rq_codes || !codes->rq_factors || !codes->rq_anchor_ids || !prep->rq_q8 || !prep->rq_scale ||
-            !prep->rq_k1xsumq || !prep->rq_centroid_dist)
-            return fail(GOFANN_ERR_INVALID, "beam_search: RaBitQ arrays missing");
-        if (codes->padded_dim == 0 || codes->padded_dim % 64 != 0 || codes->padded_dim > 4096)
-            return fail(GOFANN_ERR_UNSUPPORTED, "beam_search: padded_dim %u unsupported", codes->padded_dim);
-    } else {
-        return fail(GOFANN_ERR_INVALID, "beam_search: unknown scorer %d", p.scorer);
-    }
-    if (routes->n_routes == 0) return GOFANN_OK;
-
-    BeamArgs args{};
-    args.graph = *graph;
-    if (attrs) {
-        args.attrs.indptr = attrs->label_indptr;
-        args.attrs.indices = attrs->label_indices;
-        args.attrs.ranges = attrs->range_values;
-        args.attrs.n_samples = attrs->n_samples;
-        args.attrs.range_count = attrs->range_count;
-    }
-    args.codes = *codes;
-    args.prep = *prep;
-    args.routes = *routes;
-    args.p = p;
-    args.out = *out;
-    args.status = out->status;
-    const SmemLayout L = smem_layout(p, *codes, pq_mode, prep->dim);
-    args.warp_smem = L.total;
-    // GOFANN_PQ_U8: the packed codebook ahead of the warps' areas
-    args.block_smem = pq_mode == GOFANN_PQ_U8 && p.scorer == GOFANN_SCORER_PQ
-                          ? static_cast<uint32_t>(codes->pq_dim * GOFANN_PQ_CENTROIDS * (prep->dim / codes->pq_dim))
-                          : 0u;
-    constexpr size_t kMaxSmem = 227 * 1024;
-    int wpb = pq_mode == GOFANN_PQ_U8 && p.scorer == GOFANN_SCORER_PQ ? kU8BlockWarps : kWarpsPerBlock;
-    while (wpb > 1 && args.block_smem + static_cast<size_t>(L.total) * wpb > kMaxSmem) --wpb;
-    const size_t smem = args.block_smem + static_cast<size_t>(L.total) * wpb;
-    if (smem > kMaxSmem)
-        return fail(GOFANN_ERR_UNSUPPORTED, "beam_search: %zu bytes of shared memory per warp exceed 227 KB", smem);
-    const bool bias = p.predicate_bias != 0;
-    const KernelFn kern = pick_kernel(p.scorer, bias, pq_mode, w4, small_m);
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return cuda_status(e, "beam_search: shared memory attribute");
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, wpb * 32, smem);
-    if (e != cudaSuccess) return cuda_status(e, "beam_search: occupancy query");
-    if (per_sm <= 0) return fail(GOFANN_ERR_UNSUPPORTED, "beam_search: kernel does not fit on an SM");
-    const uint32_t blocks = cap_blocks(grid_blocks(routes->n_routes, wpb, per_sm), p, wpb, pq_mode, codes->pq_dim);
-    const size_t need = kCounterBytes + static_cast<size_t>(blocks) * wpb * kHashCap * sizeof(uint32_t);
+    if (!scratch) return fail(GOFANN_ERR_INVALID, "beam_search: null argument");
+    LaunchPlan lp;
+    const int st = plan_launch(graph, attrs, codes, prep, routes, params, out, "beam_search", lp);
+    if (st != GOFANN_OK || routes->n_routes == 0) return st;
+    const size_t need = kCounterBytes + static_cast<size_t>(lp.blocks) * lp.wpb * kHashCap * sizeof(uint32_t);
     if (scratch_bytes < need)
         return fail(GOFANN_ERR_CAPACITY, "beam_search: scratch of %zu bytes, %zu needed", scratch_bytes, need);
-    args.route_counter = static_cast<uint32_t*>(scratch);
-    args.hash = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(scratch) + kCounterBytes);
-    cudaStream_t s = as_stream(stream);
-    e = cudaMemsetAsync(scratch, 0, sizeof(uint32_t), s);
-    if (e != cudaSuccess) return cuda_status(e, "beam_search: counter reset");
-    kern<<<blocks, wpb * 32, smem, s>>>(args);
-    GOFANN_CHECK_LAUNCH("beam_search_kernel");
-    return GOFANN_OK;
+    return launch_planned(lp, lp.blocks, scratch, stream, "beam_search_kernel");
 }
 
 }  // extern "C"
@@ -1032,12 +1095,20 @@ int gofann_beam_search(const gofann_graph* graph, const gofann_attrs* attrs, con
 // 16 MiB + 256 B, allocated once per device by the CUDA runtime when this
 // library is loaded and held until the process exits.  At most 1,024 warps
 // run at once in this mode (the grid is capped to that; any number of routes
-// is still processed, since warps pull routes from the counter).  Every call
-// on a device uses the same array, which keeps the previous call's contents:
-// the counter is cleared before each launch and each warp clears its visited
-// table per route, so nothing stale is read.  Calls whose kernels overlap on
-// the GPU (different streams, or different host threads) race on the array
-// and must be serialised by the caller.
+// is still processed, since warps pull routes from the counter): with the
+// 24-warp blocks of GOFANN_PQ_U8 that is 42 blocks, so 42 of a B200's 148
+// SMs do the work and a large batch takes about 3.5x as long as through
+// gofann_beam_search; the 4-warp blocks of the other modes fill 256 blocks.
+// Every call on a device uses the same array, which keeps the previous
+// call's contents: the counter is cleared before each launch and each warp
+// clears its visited table per route, so nothing stale is read.  Calls
+// whose kernels overlap on the GPU (different streams, or different host
+// threads) race on the array and must be serialised by the caller.
+//
+// The array's device address is looked up once per device and cached for
+// the life of the process; a device reset (cudaDeviceReset, or destroying
+// the primary context) invalidates it and is not supported while this
+// library is loaded.
 namespace gofann {
 namespace {
 constexpr int kNoAllocTables = 1024;
@@ -1085,112 +1156,20 @@ int gofann_beam_search_noalloc(const gofann_graph* graph, const gofann_attrs* at
                                const gofann_prepared* prep, const gofann_routes* routes,
                                const gofann_search_params* params, const gofann_search_out* out, void* stream)
 {
-    if (!graph || !codes || !prep || !routes || !params || !out)
-        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: null argument");
-    const gofann_search_params& p = *params;
-    if (p.queue_size < 2 || p.queue_size > GOFANN_MAX_QUEUE)
-        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: queue_size %d outside 2..%d", p.queue_size,
-                    GOFANN_MAX_QUEUE);
-    if (p.stop_width < 1 || p.stop_width > GOFANN_MAX_TOPK)
-        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: stop_width %d outside 1..%d", p.stop_width,
-                    GOFANN_MAX_TOPK);
-    if (p.result_width < 1 || p.result_width > GOFANN_MAX_RESULT_WIDTH)
-        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: result_width %d outside 1..%d", p.result_width,
-                    GOFANN_MAX_RESULT_WIDTH);
-    if (p.early_stop_mode < 0 || p.early_stop_mode > 2)
-        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: unknown early_stop_mode %d", p.early_stop_mode);
-    if (p.resident_warps < 0)
-        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: resident_warps %d is negative", p.resident_warps);
-    if (!graph->adjacency || !graph->row_to_sample || !graph->label_offset || graph->degree == 0)
-        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: graph arrays missing");
-    if (graph->records && p.scorer == GOFANN_SCORER_PQ &&
-        ((graph->record_stride & 15u) != 0 || (reinterpret_cast<uintptr_t>(graph->records) & 15) != 0 ||
-         graph->record_stride < GOFANN_RECORD_META(codes->pq_dim) + 16u + 4u * GOFANN_RECORD_INLINE_LABELS))
-        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: row records need 16-byte alignment and a stride of at least %u",
-                    GOFANN_RECORD_META(codes->pq_dim) + 16u + 4u * GOFANN_RECORD_INLINE_LABELS);
-    if (!routes->query_row || !routes->group_id || !routes->start_local || !out->ids || !out->dists)
-        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: route or output arrays missing");
-    const bool needs_attrs = routes->pred_offsets != nullptr || p.full_label_check != 0 ||
-                             routes->range_modes != nullptr;
-    if (needs_attrs && (!attrs || !attrs->label_indptr || !attrs->label_indices))
-        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: predicates need the sample label CSR");
-    if (routes->pred_offsets && (!routes->clauses || !routes->pred_handles))
-        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: predicate clause arrays missing");
-    int pq_mode = GOFANN_PQ_LUT_GLOBAL;
-    bool w4 = false, small_m = true;
-    if (p.scorer == GOFANN_SCORER_PQ) {
-        if (!codes->pq_codes) return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: PQ codes missing");
-        if (codes->pq_dim == 0 || codes->pq_dim > static_cast<uint32_t>(kMaxPqDim))
-            return fail(GOFANN_ERR_UNSUPPORTED, "beam_search_noalloc: pq_dim %u outside 1..%d", codes->pq_dim,
-                        kMaxPqDim);
-        const int cst = check_pq_mode(p, *codes, *prep, w4, small_m, "beam_search_noalloc");
-        if (cst != GOFANN_OK) return cst;
-        pq_mode = p.pq_mode;
-    } else if (p.scorer == GOFANN_SCORER_RABITQ) {
-        if (!codes->rq_codes || !codes->rq_factors || !codes->rq_anchor_ids || !prep->rq_q8 || !prep->rq_scale ||
-            !prep->rq_k1xsumq || !prep->rq_centroid_dist)
-            return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: RaBitQ arrays missing");
-        if (codes->padded_dim == 0 || codes->padded_dim % 64 != 0 || codes->padded_dim > 4096)
-            return fail(GOFANN_ERR_UNSUPPORTED, "beam_search_noalloc: padded_dim %u unsupported", codes->padded_dim);
-    } else {
-        return fail(GOFANN_ERR_INVALID, "beam_search_noalloc: unknown scorer %d", p.scorer);
-    }
-    void* scratch = nullptr;
-    const int st = noalloc_scratch_address(&scratch);
+    LaunchPlan lp;
+    int st = plan_launch(graph, attrs, codes, prep, routes, params, out, "beam_search_noalloc", lp);
     if (st != GOFANN_OK) return st;
-    if (routes->n_routes == 0) return GOFANN_OK;
-
-    BeamArgs args{};
-    args.graph = *graph;
-    if (attrs) {
-        args.attrs.indptr = attrs->label_indptr;
-        args.attrs.indices = attrs->label_indices;
-        args.attrs.ranges = attrs->range_values;
-        args.attrs.n_samples = attrs->n_samples;
-        args.attrs.range_count = attrs->range_count;
-    }
-    args.codes = *codes;
-    args.prep = *prep;
-    args.routes = *routes;
-    args.p = p;
-    args.out = *out;
-    args.status = out->status;
-    const SmemLayout L = smem_layout(p, *codes, pq_mode, prep->dim);
-    args.warp_smem = L.total;
-    // GOFANN_PQ_U8: the packed codebook ahead of the warps' areas
-    args.block_smem = pq_mode == GOFANN_PQ_U8 && p.scorer == GOFANN_SCORER_PQ
-                          ? static_cast<uint32_t>(codes->pq_dim * GOFANN_PQ_CENTROIDS * (prep->dim / codes->pq_dim))
-                          : 0u;
-    constexpr size_t kMaxSmem = 227 * 1024;
-    int wpb = pq_mode == GOFANN_PQ_U8 && p.scorer == GOFANN_SCORER_PQ ? kU8BlockWarps : kWarpsPerBlock;
-    while (wpb > 1 && args.block_smem + static_cast<size_t>(L.total) * wpb > kMaxSmem) --wpb;
-    const size_t smem = args.block_smem + static_cast<size_t>(L.total) * wpb;
-    if (smem > kMaxSmem)
-        return fail(GOFANN_ERR_UNSUPPORTED, "beam_search_noalloc: %zu bytes of shared memory per warp exceed 227 KB",
-                    smem);
-    const KernelFn kern = pick_kernel(p.scorer, p.predicate_bias != 0, pq_mode, w4, small_m);
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return cuda_status(e, "beam_search_noalloc: shared memory attribute");
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, wpb * 32, smem);
-    if (e != cudaSuccess) return cuda_status(e, "beam_search_noalloc: occupancy query");
-    if (per_sm <= 0) return fail(GOFANN_ERR_UNSUPPORTED, "beam_search_noalloc: kernel does not fit on an SM");
-    uint32_t blocks = cap_blocks(grid_blocks(routes->n_routes, wpb, per_sm), p, wpb, pq_mode, codes->pq_dim);
-    const uint32_t max_blocks = static_cast<uint32_t>(kNoAllocTables / wpb);
-    if (blocks > max_blocks) blocks = max_blocks;
-    const size_t need = kCounterBytes + static_cast<size_t>(blocks) * wpb * kHashCap * sizeof(uint32_t);
+    void* scratch = nullptr;
+    st = noalloc_scratch_address(&scratch);
+    if (st != GOFANN_OK || routes->n_routes == 0) return st;
+    const uint32_t max_blocks = static_cast<uint32_t>(kNoAllocTables / lp.wpb);
+    const uint32_t blocks = lp.blocks < max_blocks ? lp.blocks : max_blocks;
+    const size_t need = kCounterBytes + static_cast<size_t>(blocks) * lp.wpb * kHashCap * sizeof(uint32_t);
     if (blocks == 0 || need > kNoAllocBytes)
         return fail(GOFANN_ERR_CAPACITY,
                     "beam_search_noalloc: %zu bytes of scratch needed, the static scratch holds %zu (%d visited tables)",
                     need, kNoAllocBytes, kNoAllocTables);
-    args.route_counter = static_cast<uint32_t*>(scratch);
-    args.hash = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(scratch) + kCounterBytes);
-    cudaStream_t s = as_stream(stream);
-    e = cudaMemsetAsync(scratch, 0, sizeof(uint32_t), s);
-    if (e != cudaSuccess) return cuda_status(e, "beam_search_noalloc: counter reset");
-    kern<<<blocks, wpb * 32, smem, s>>>(args);
-    GOFANN_CHECK_LAUNCH("beam_search_kernel (no-alloc)");
-    return GOFANN_OK;
+    return launch_planned(lp, blocks, scratch, stream, "beam_search_kernel (no-alloc)");
 }
 
 }  // extern "C"

@@ -206,72 +206,9 @@ struct FPair {
     float base;
 };
 
-__device__ __forceinline__ void fswap(FPair& a, FPair& b) { FPair t = a; a = b; b = t; }
-
-// Symmetric min-max heap, include/smmh2.h:8-148 (index 0 unused, 1 = min,
-// 2 = max; entries compare by `first`).
-__device__ __forceinline__ int smmh_adjust_sibling(FPair* h, int y, int size)
-{
-    if (y & 1) {
-        const int s = y + 1;
-        if (s >= size) return y;
-        if (h[y].first > h[s].first) { fswap(h[y], h[s]); return s; }
-    } else {
-        const int s = y - 1;
-        if (h[y].first < h[s].first) { fswap(h[y], h[s]); return s; }
-    }
-    return y;
-}
-__device__ __forceinline__ int smmh_adjust_grandparent(FPair* h, int y)
-{
-    if (y <= 2) return y;
-    const int g = (y - 3) >> 2;
-    const int gl = 2 * g + 1, gr = 2 * g + 2;
-    if (h[gl].first > h[y].first) { fswap(h[gl], h[y]); return gl; }
-    if (h[gr].first < h[y].first) { fswap(h[gr], h[y]); return gr; }
-    return y;
-}
-__device__ __forceinline__ void smmh_insert(FPair* h, int& size, const FPair& e)
-{
-    int y = size;
-    h[size++] = e;
-    for (;;) {
-        y = smmh_adjust_sibling(h, y, size);
-        const int x = smmh_adjust_grandparent(h, y);
-        if (x == y) break;
-        y = x;
-    }
-}
-__device__ __forceinline__ int smmh_adjust_grandchild(FPair* h, int y, int size)
-{
-    if (y & 1) {
-        if (2 * y + 1 >= size) return y;
-        const int cl = 2 * y + 1, cr = 2 * (y + 1) + 1;
-        int c = cl;
-        if (cr < size && h[cr].first < h[cl].first) c = cr;
-        if (h[c].first < h[y].first) { fswap(h[c], h[y]); return c; }
-    } else {
-        const int cl = 2 * (y - 1) + 2, cr = 2 * y + 2;
-        if (cl >= size) return y;
-        int c = cl;
-        if (cr < size && h[cr].first > h[cl].first) c = cr;
-        if (h[c].first > h[y].first) { fswap(h[c], h[y]); return c; }
-    }
-    return y;
-}
-__device__ __forceinline__ void smmh_pop_max(FPair* h, int& size)
-{
-    h[2] = h[--size];
-    int y = 2;
-    for (;;) {
-        smmh_adjust_sibling(h, y, size);
-        const int x = smmh_adjust_grandchild(h, y, size);
-        if (x == y) break;
-        y = x;
-    }
-}
-
-// The same heap stored as three arrays (key = `first`, val = payload, base =
+// The reference's frontier is a symmetric min-max heap (include/smmh2.h:
+// 8-148: index 0 unused, 1 = min, 2 = max, entries compared by `first`).
+// Here it is stored as three arrays (key = `first`, val = payload, base =
 // unbiased score) and operated on by a whole warp.  Every lane runs the
 // same, warp-uniform sequence of the reference's decisions on broadcast
 // shared-memory reads; lane 0 writes.  Only the fetching is parallel:

@@ -27,7 +27,11 @@ __global__ void build_records_kernel(gofann_graph g, AttrView at, const uint8_t*
         const uint32_t c = static_cast<uint32_t>(t - row * chunks);
         const uint32_t sample = g.row_to_sample[row];
         uint32_t w[4] = {0u, 0u, 0u, 0u};
-        if (c < meta_chunk) {
+        if (sample >= at.n_samples) {
+            // padding row or corrupt row -> sample entry: an all-zero record
+            // (sample 0 with an empty label row) and an error status
+            if (c == 0 && status) atomicExch(status, GOFANN_ERR_INVALID);
+        } else if (c < meta_chunk) {
             const uint8_t* src = codes + static_cast<uint64_t>(sample) * pq_dim;
             for (uint32_t b = 0; b < 16; ++b) {
                 const uint32_t m = c * 16 + b;

@@ -345,7 +345,9 @@ GOFANN_API int gofann_shard_merge(const uint32_t* shard_ids, const float* shard_
  * bytes at pq_dim 48);
  * out: device [total_rows][record_stride].  Label CSR offsets must fit in
  * 32 bits (fails with GOFANN_ERR_UNSUPPORTED otherwise, checked on the
- * device through `status`, which may be NULL). */
+ * device through `status`, which may be NULL); a row whose row_to_sample
+ * entry is not below attrs->n_samples gets an all-zero record and sets
+ * `status` to GOFANN_ERR_INVALID. */
 GOFANN_API size_t gofann_row_record_stride(uint32_t pq_dim);
 GOFANN_API int gofann_build_row_records(const gofann_graph* graph, const gofann_attrs* attrs,
                                         const gofann_codes* codes, uint8_t* out, int32_t* status, void* stream);

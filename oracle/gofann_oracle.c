@@ -577,23 +577,40 @@ static int early_stop(int mode, int bad, int fixed, int queue_limit, int expande
 /* ---------------------------------------------------------- traversal */
 
 /* pickup_next_unused_from_native_frontier<kCooperative=true>,
- * backend_pq.cu:844-893: minimum `first` among unused entries 1..size-1,
- * lowest array index on ties; marks the entry used.  Distances are ordered
- * by their order-preserving bit pattern (-0 folded onto +0), which equals
- * float order for every non-NaN value and places NaN after +inf. */
-static uint32_t ordered_bits(float x)
-{
-    if (x == 0.0f) x = 0.0f;
-    const uint32_t b = f2u(x);
-    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
+ * backend_pq.cu:844-893 (RaBitQ twin backend_rabitq.cu:924-970): lane l
+ * scans entries l+1, l+33, ... and keeps the first unused entry of smallest
+ * `first`; a shfl_down tree (offsets 16..1) then merges lane l+off into lane
+ * l, replacing lane l's candidate only by a strictly smaller distance.  The
+ * source also replaces on equal distances when the other index is smaller,
+ * but the reference compiled for sm_100a (nvcc 12.9, run on a B200 through
+ * oracle/ref_kernels.cu on 600 tie-heavy frontiers and 8 traversal cases,
+ * tests/golden/reference_pq_kernel.npz) never does: on ties the receiving
+ * lane keeps its candidate.  This restates that observed behaviour lane by
+ * lane; the result is lane 0's candidate, which lane 0 copies and marks. */
 static int pickup(fpair* f, int size, fpair* out)
 {
-    int best = -1;
-    for (int i = 1; i < size; ++i) {
-        if (f[i].second & POOL_USED) continue;
-        if (best < 0 || ordered_bits(f[i].first) < ordered_bits(f[best].first)) best = i;
+    int bi[32];
+    float bd[32];
+    for (int l = 0; l < 32; ++l) {
+        bi[l] = -1;
+        bd[l] = FLT_MAX;
+        for (int i = l + 1; i < size; i += 32) {
+            if (f[i].second & POOL_USED) continue;
+            if (bi[l] < 0 || f[i].first < bd[l]) { bi[l] = i; bd[l] = f[i].first; }
+        }
     }
+    for (int off = 16; off > 0; off >>= 1) {
+        int oi[32];
+        float od[32];
+        for (int l = 0; l < 32; ++l) {  /* shfl_down: lanes past the end read their own value */
+            const int src = l + off < 32 ? l + off : l;
+            oi[l] = bi[src];
+            od[l] = bd[src];
+        }
+        for (int l = 0; l < 32; ++l)
+            if (oi[l] >= 0 && (bi[l] < 0 || od[l] < bd[l])) { bi[l] = oi[l]; bd[l] = od[l]; }
+    }
+    const int best = bi[0];
 #ifdef ORACLE_DEBUG_PICKUP
     printf("PICK size=%d idx=%d row=%u first=%.9g\n", size, best,
            best >= 0 ? (f[best].second & ~POOL_USED) : 0xffffffffu, best >= 0 ? (double)f[best].first : 0.0);
@@ -602,6 +619,19 @@ static int pickup(fpair* f, int size, fpair* out)
     *out = f[best];
     f[best].second |= POOL_USED;
     return 1;
+}
+
+/* The entry pickup() takes from a frontier of `size` entries (index 0
+ * unused; vals carry the used bit), or -1; nothing is modified. */
+int oracle_pickup_index(const float* keys, const uint32_t* vals, int size)
+{
+    fpair* f = (fpair*)calloc((size_t)(size > 1 ? size : 1), sizeof(fpair));
+    for (int i = 0; i < size; ++i) { f[i].first = keys[i]; f[i].second = vals[i]; f[i].base = keys[i]; }
+    fpair out;
+    int idx = -1;
+    if (pickup(f, size, &out)) idx = (int)(out.second & ~POOL_USED);
+    free(f);
+    return idx;
 }
 
 static float route_distance(const gofann_codes* c, const gofann_prepared* p, int scorer,

@@ -73,6 +73,8 @@ def olib() -> C.CDLL:
         L.oracle_sl_insert.argtypes = [C.c_float, U32, sp, sp, C.c_int]
         L.oracle_sl_sort.argtypes = [sp, sp, C.c_int]
         L.oracle_hash_test.argtypes = [sp, U32]
+        L.oracle_pickup_index.argtypes = [sp, sp, C.c_int]
+        L.oracle_pickup_index.restype = C.c_int
         L.oracle_pred_matches.argtypes = [C.POINTER(A.Routes), C.POINTER(A.Attrs), U32, U32]
         L.oracle_labels_match.argtypes = [C.POINTER(A.Routes), C.POINTER(A.Attrs), U32, U32]
         for fn in ("oracle_beam_search", "oracle_posting_scan", "oracle_rerank", "oracle_route_merge",
@@ -323,6 +325,13 @@ def pred_matches(routes: dict, attrs: dict, pair_route, pair_sample):
     L = olib()
     return np.array([L.oracle_pred_matches(C.byref(rs), C.byref(at), int(r), int(s))
                      for r, s in zip(pair_route, pair_sample)], np.uint8)
+
+
+def pickup_index(keys, vals, size: int) -> int:
+    """The frontier entry the traversal's pickup takes (index, or -1)."""
+    k = _c(keys, np.float32)
+    v = _c(vals, np.uint32)
+    return int(olib().oracle_pickup_index(P(k), P(v), int(size)))
 
 
 def cpu_count() -> int:

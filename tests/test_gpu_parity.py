@@ -387,6 +387,50 @@ def test_beam_search_visited_table_fills(L, queue_size):
         assert np.array_equal(g, o), name
 
 
+@pytest.mark.parametrize("queue_size", [64, 512])
+def test_beam_search_repeated_neighbour_ids(L, queue_size):
+    """Adjacency rows that list an id twice: both copies pass the step's
+    visited test and enter the frontier, as in the reference, but the visited
+    table takes the id once -- so the table fills (routes admit more than
+    4,096 rows) at exactly the reference's point."""
+    graph, attrs, codes, lut, routes = _chain_graph()
+    adj = graph["adjacency"].copy()
+    adj[:, 5] = adj[:, 0]          # a forward neighbour listed twice
+    adj[::3, 40] = adj[::3, 2]     # and another on every third row
+    graph = dict(graph, adjacency=adj)
+    params = dict(queue_size=queue_size, predicate_bias=0, early_stop_mode=A.EARLY_STOP_OFF, max_steps=400,
+                  result_width=100, scorer=A.SCORER_PQ, pq_mode=A.PQ_LUT_GLOBAL)
+    want = O.beam_search(graph, attrs, codes, {"pq_lut": lut}, routes, threads=4, trace_width=64, **params)
+    assert want[3][:, 3].min() > 4096, "a route did not fill its visited table"
+    got = run_gpu_beam(L, graph, attrs, codes, {"pq_lut": dev(lut)}, routes, trace_width=64, **params)
+    for name, g, o in zip(("ids", "dists", "steps", "counters", "trace"), got, want):
+        if name == "dists":
+            g, o = fbits(g), fbits(o)
+        assert np.array_equal(g, o), name
+
+
+def test_row_records_reject_out_of_range_sample(L):
+    """A row whose row -> sample entry is past the attribute table gets an
+    all-zero record and the status word reports GOFANN_ERR_INVALID."""
+    w, idx, plan = cfg2_small()
+    g = dict(idx.graph())
+    r2s = g["row_to_sample"].copy()
+    r2s[7] = w.n + 3
+    g["row_to_sample"] = r2s
+    dg, da, dc = dev_dict(g), dev_dict(idx.attrs()), dev_dict(idx.codes())
+    gs, at, cs = A.fill_graph(dg), A.fill_attrs(da), A.fill_codes(dc)
+    stride = int(L.gofann_row_record_stride(cs.pq_dim))
+    rec = torch.full((gs.total_rows, stride), 0xAB, dtype=torch.uint8, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    A.check(L.gofann_build_row_records(C.byref(gs), C.byref(at), C.byref(cs), A.ptr(rec), A.ptr(status), stream()),
+            "build_row_records")
+    torch.cuda.synchronize()
+    assert int(status.item()) == A.ERR_INVALID
+    r = rec.cpu().numpy()
+    assert not r[7].any()
+    assert r[8].any()
+
+
 @pytest.mark.parametrize("vi", [0, 1, 3])
 def test_beam_search_rabitq_bitexact(L, vi):
     w, idx, plan, rq, anchors, qr = rabitq_artifacts()

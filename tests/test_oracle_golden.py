@@ -116,3 +116,59 @@ def test_fp16_decode_and_l2():
         got = L.oracle_exact_l2(O.P(rows), A.DTYPE_F16, rows.shape[1], r, O.P(G["f16_query"]), 0)
         # reference scalar loop accumulates without fma: relative 1e-6 agreement
         assert abs(got - G["f16_l2"][r]) <= 1e-5 * max(1.0, abs(G["f16_l2"][r]))
+
+
+# ------------------------------------------------ reference device traversal
+# tests/golden/reference_pq_kernel.npz holds the outputs of the reference's
+# own device-resident PQ traversal (backend_pq.cu compiled in place for
+# sm_100a, run on a B200 by tests/golden/make_ref_kernel_golden.py) on the
+# numpy-built cases of tests/ref_kernel_cases.py.  The oracle's traversal
+# restatement must reproduce every one of them bit for bit, and its PQ table
+# must hash to the table the reference kernel built.
+import hashlib  # noqa: E402
+
+import ref_kernel_cases as RC  # noqa: E402
+
+_KG = Path.parent / "reference_pq_kernel.npz"  # Path: tests/golden/reference_structures.npz
+
+
+@pytest.mark.skipif(not _KG.exists(), reason="reference kernel golden vectors not recorded yet")
+@pytest.mark.parametrize("name", RC.CASE_NAMES)
+def test_oracle_replays_reference_kernel(name):
+    K = np.load(_KG)
+    case = RC.build_case(name)
+    assert RC.case_digest(case) == bytes(K[f"{name}/digest"]).hex(), "case generator drifted from the recording"
+    pq_dim = case["codes"]["pq_codes"].shape[1]
+    lut = O.pq_build_lut(case["queries"].astype(np.float32), case["centroids"], pq_dim)
+    assert hashlib.sha256(np.ascontiguousarray(lut, np.float32).tobytes()).digest() == bytes(K[f"{name}/table_sha256"])
+    ids, d, steps, _, trace = O.beam_search(case["graph"], case["attrs"], case["codes"], {"pq_lut": lut},
+                                            case["routes"], threads=8, trace_width=64, scorer=A.SCORER_PQ,
+                                            **case["params"])
+    assert np.array_equal(ids, K[f"{name}/ids"])
+    assert np.array_equal(bits(d), K[f"{name}/dist_bits"])
+    assert np.array_equal(steps, K[f"{name}/steps"])
+    assert np.array_equal(trace, K[f"{name}/trace"])
+
+
+@pytest.mark.skipif(not _KG.exists(), reason="reference kernel golden vectors not recorded yet")
+def test_oracle_pickup_matches_reference_device_pickup():
+    """The reference's cooperative pickup, run on a B200 on 600 frontiers of
+    2..520 entries with keys from six values (many ties) and 30 % of the
+    entries used: the oracle picks the same entry every time."""
+    K = np.load(_KG)
+    keys, used, sizes, picked = K["pickup/keys"], K["pickup/used"], K["pickup/sizes"], K["pickup/picked"]
+    vals = (np.arange(keys.shape[1], dtype=np.uint32)[None, :] | (used.astype(np.uint32) << 31)).astype(np.uint32)
+    got = np.array([O.pickup_index(keys[c], vals[c], int(sizes[c])) for c in range(keys.shape[0])])
+    assert np.array_equal(got, picked)
+
+
+@pytest.mark.skipif(not _KG.exists(), reason="reference kernel golden vectors not recorded yet")
+@pytest.mark.parametrize("cap", [1, 10, 33, 100, 200])
+def test_oracle_result_heap_matches_reference_device_heap(cap):
+    """The reference's binary result heap on the device (push / pop of
+    bin_heap.h, then emptied into ascending slots) against the oracle's."""
+    K = np.load(_KG)
+    hk, f, p = K[f"rheap{cap}/keys"], K[f"rheap{cap}/first"], K[f"rheap{cap}/payload"]
+    for c in range(hk.shape[0]):
+        of, op = O.seq_result_heap(hk[c], np.arange(hk.shape[1], dtype=np.uint32), cap)
+        assert np.array_equal(bits(of[:cap][::-1]), bits(f[c])) and np.array_equal(op[:cap][::-1], p[c])
