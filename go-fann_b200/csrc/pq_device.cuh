@@ -219,7 +219,7 @@ __device__ __forceinline__ float pq_adc_u8(const uint32_t* qw, const uint32_t* c
 __device__ __forceinline__ float pq_adc_u8_chunked(const uint32_t* qw, const uint32_t* cbw,
                                                    const uint8_t* __restrict__ code, int pq_dim, uint64_t pol)
 {
-    uint32_t acc = 0;
+    uint32_t acc = 0, acc2 = 0;
     const uint4* row = reinterpret_cast<const uint4*>(code);
 #pragma unroll 1
     for (int q = 0; q < (pq_dim >> 4); ++q) {
@@ -227,14 +227,19 @@ __device__ __forceinline__ float pq_adc_u8_chunked(const uint32_t* qw, const uin
         const uint32_t words[4] = {x.x, x.y, x.z, x.w};
         const uint32_t* cb = cbw + q * 16 * GOFANN_PQ_CENTROIDS;
         const uint32_t* qq = qw + q * 16;
+        // two independent accumulators halve the dependent dp4a chain
+        // (integer sums: any order gives the same value)
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const uint32_t c = (words[j >> 2] >> ((j & 3) * 8)) & 0xffu;
-            const uint32_t d = __vabsdiffu4(qq[j], cb[j * GOFANN_PQ_CENTROIDS + c]);
-            acc = __dp4a(d, d, acc);
+        for (int j = 0; j < 16; j += 2) {
+            const uint32_t c0 = (words[j >> 2] >> ((j & 3) * 8)) & 0xffu;
+            const uint32_t c1 = (words[j >> 2] >> (((j + 1) & 3) * 8)) & 0xffu;
+            const uint32_t d0 = __vabsdiffu4(qq[j], cb[j * GOFANN_PQ_CENTROIDS + c0]);
+            const uint32_t d1 = __vabsdiffu4(qq[j + 1], cb[(j + 1) * GOFANN_PQ_CENTROIDS + c1]);
+            acc = __dp4a(d0, d0, acc);
+            acc2 = __dp4a(d1, d1, acc2);
         }
     }
-    return __uint2float_rn(acc);
+    return __uint2float_rn(acc + acc2);
 }
 
 // Posting-scan order: sequential over subspaces (backend_pq.cu:2101-2104).

@@ -5,8 +5,9 @@
 // (GraphMetadata::row_to_sample, pq.codes.bin, SparseLabelMatrix): two
 // dependent reads each.  A record stores, per graph row and in row order,
 // the sample's code row followed by (sample id, label-row start, label-row
-// length) and, for rows of at most GOFANN_RECORD_INLINE_LABELS labels, the
-// labels, so the traversal reads one line per candidate.  The records are
+// length, label signature) and, for rows of at most
+// GOFANN_RECORD_INLINE_LABELS labels, the labels, so the traversal reads one
+// line per candidate.  The records are
 // derived data; a traversal gives the same results with or without them.
 #include "common.cuh"
 
@@ -42,9 +43,12 @@ __global__ void build_records_kernel(gofann_graph g, AttrView at, const uint8_t*
             if (hi > 0xffffffffull) {
                 if (status) atomicExch(status, GOFANN_ERR_UNSUPPORTED);
             }
+            uint32_t sig = 0;
+            for (uint64_t k = lo; k < hi; ++k) sig |= GOFANN_LABEL_SIG_BIT(at.indices[k]);
             w[0] = sample;
             w[1] = static_cast<uint32_t>(lo);
             w[2] = static_cast<uint32_t>(hi - lo);
+            w[3] = sig;
         } else {
             // inline label row (short rows only)
             const uint64_t lo = at.indptr[sample], hi = at.indptr[sample + 1];

@@ -39,7 +39,7 @@
 extern "C" {
 #endif
 
-#define GOFANN_ABI_VERSION 1
+#define GOFANN_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define GOFANN_API __attribute__((visibility("default")))
@@ -105,22 +105,31 @@ typedef struct gofann_graph {
     uint32_t reserved;
     /* Optional per-row records (gofann_build_row_records), or NULL: row r at
      * records + r * record_stride holds the PQ code row of its sample
-     * (pq_dim bytes), then at byte GOFANN_RECORD_META(pq_dim) three uint32:
-     * the sample id, the start and the length of its label-CSR row, then,
-     * 16 bytes further, the label row itself when it has at most
-     * GOFANN_RECORD_INLINE_LABELS labels.  One 128-byte line per row at
+     * (pq_dim bytes), then at byte GOFANN_RECORD_META(pq_dim) four uint32:
+     * the sample id, the start and the length of its label-CSR row, and the
+     * row's label signature (GOFANN_LABEL_SIG_BIT of every label OR-ed
+     * together), then, 16 bytes further, the label row itself when it has at
+     * most GOFANN_RECORD_INLINE_LABELS labels.  One 128-byte line per row at
      * config-2 shape: scoring and predicate checks of a candidate read one
      * line instead of following row -> sample -> code and sample -> CSR
-     * offsets -> labels.  Results are the same with or without. */
+     * offsets -> labels, and a candidate whose signature lacks a bit of the
+     * route's clause skips the label row.  Results are the same with or
+     * without records; records must come from gofann_build_row_records of
+     * this ABI version. */
     const uint8_t* records;
     uint32_t record_stride;          /* bytes, a multiple of 16 */
     uint32_t reserved2;
 } gofann_graph;
 
-/* Byte offset of a record's (sample, label start, label length) words. */
+/* Byte offset of a record's (sample, label start, label length, label
+ * signature) words. */
 #define GOFANN_RECORD_META(pq_dim) ((((pq_dim) + 15u) / 16u) * 16u)
 /* Label rows of at most this many labels are stored in the record. */
 #define GOFANN_RECORD_INLINE_LABELS 16u
+/* Signature bit of a label: one of 32, from a multiplicative hash.  A row
+ * can carry every label of a clause only if its signature holds all their
+ * bits. */
+#define GOFANN_LABEL_SIG_BIT(label) (1u << ((((uint32_t)(label)) * 0x9E3779B1u) >> 27))
 
 /* Per-sample attributes: sample-major label CSR (sorted, unique per row) and
  * float range values (SparseLabelMatrix / base_range_values). */

@@ -265,8 +265,8 @@ def _with_records(L, graph, attrs, codes):
 
 def test_row_records_layout(L):
     """Record r = code row of sample row_to_sample[r], then (sample, label
-    start, label length) at GOFANN_RECORD_META(pq_dim), then the label row
-    itself when it has at most 16 labels."""
+    start, label length, label signature) at GOFANN_RECORD_META(pq_dim), then
+    the label row itself when it has at most 16 labels."""
     w, idx, plan = cfg2_small()
     g, rec = _with_records(L, idx.graph(), idx.attrs(), idx.codes())
     rec = rec.cpu().numpy()
@@ -275,10 +275,15 @@ def test_row_records_layout(L):
     r2s = idx.graph()["row_to_sample"].astype(np.int64)
     ip = idx.attrs()["label_indptr"].astype(np.int64)
     assert np.array_equal(rec[:, :m], idx.pq_codes[r2s])
-    words = rec[:, meta:meta + 12].copy().view(np.uint32)
+    words = rec[:, meta:meta + 16].copy().view(np.uint32)
     assert np.array_equal(words[:, 0], r2s)
     assert np.array_equal(words[:, 1], ip[r2s])
     assert np.array_equal(words[:, 2], ip[r2s + 1] - ip[r2s])
+    ind = idx.attrs()["label_indices"].astype(np.uint64)
+    bit = (np.uint64(1) << (((ind * np.uint64(0x9E3779B1)) & np.uint64(0xFFFFFFFF)) >> np.uint64(27))).astype(np.uint32)
+    sig = np.bitwise_or.reduceat(bit, ip[:-1].astype(np.int64)) if ind.size else np.zeros(0, np.uint32)
+    sig = np.where(ip[1:] > ip[:-1], sig, 0).astype(np.uint32)
+    assert np.array_equal(words[:, 3], sig[r2s]), "label signature word"
     assert rec.shape[1] == meta + 16 + 4 * 16
     labels = rec[:, meta + 16:meta + 16 + 64].copy().view(np.uint32)
     ind = idx.attrs()["label_indices"]
