@@ -23,6 +23,7 @@ SCORER_PQ, SCORER_RABITQ = 0, 1
 DTYPE_U8, DTYPE_F32, DTYPE_F16 = 0, 1, 2
 PQ_LUT_GLOBAL, PQ_LUT_SHARED, PQ_DIRECT, PQ_U8 = 0, 1, 2, 3
 TABLE_MODES = (PQ_LUT_GLOBAL, PQ_LUT_SHARED)  # modes that read a per-query table batch
+GEMM_TF32, GEMM_TF32X3 = 0, 1
 MAX_DEGREE, MAX_QUEUE, MAX_TOPK, MAX_RESULT_WIDTH, MAX_SHORTLIST = 64, 512, 10, 512, 400
 PQ_CENTROIDS, HASH_CAPACITY = 256, 4096
 U32MAX = 0xFFFFFFFF
@@ -216,6 +217,8 @@ def lib() -> C.CDLL:
         "gofann_pq_encode": [sp, C.c_int, U32, U32, sp, U32, sp, sp],
         "gofann_rabitq_quantize": [sp, U32, U32, sp, sp, sp, sp],
         "gofann_rabitq_centroid_dist": [sp, U32, sp, U32, U32, sp, sp],
+        "gofann_rabitq_rotate": [sp, U32, U32, sp, U32, C.c_int, sp, sp, C.c_size_t, sp, sp],
+        "gofann_rabitq_centroid_dist_tc": [sp, U32, sp, U32, U32, C.c_int, sp, sp, C.c_size_t, sp, sp],
         "gofann_rabitq_score": [C.POINTER(Codes), C.POINTER(Prepared), sp, sp, U32, sp, sp, sp],
         "gofann_beam_search": [C.POINTER(Graph), C.POINTER(Attrs), C.POINTER(Codes), C.POINTER(Prepared),
                                C.POINTER(Routes), C.POINTER(SearchParams), C.POINTER(SearchOut), sp, C.c_size_t,
@@ -237,6 +240,8 @@ def lib() -> C.CDLL:
         fn.restype = C.c_int
     L.gofann_beam_search_scratch_bytes.argtypes = [U32]
     L.gofann_beam_search_scratch_bytes.restype = C.c_size_t
+    L.gofann_rabitq_gemm_scratch_bytes.argtypes = [U32, U32, U32, C.c_int]
+    L.gofann_rabitq_gemm_scratch_bytes.restype = C.c_size_t
     L.gofann_row_record_stride.argtypes = [U32]
     L.gofann_row_record_stride.restype = C.c_size_t
     _LIB = L
@@ -257,7 +262,8 @@ def check(status: int, where: str) -> None:
 
 EXPORTED = ("gofann_abi_version", "gofann_last_error", "gofann_device_sm_count", "gofann_pq_build_lut",
             "gofann_pq_adc", "gofann_pq_encode", "gofann_rabitq_quantize", "gofann_rabitq_centroid_dist",
-            "gofann_rabitq_score", "gofann_beam_search_scratch_bytes", "gofann_beam_search",
+            "gofann_rabitq_score", "gofann_rabitq_gemm_scratch_bytes", "gofann_rabitq_rotate",
+            "gofann_rabitq_centroid_dist_tc", "gofann_beam_search_scratch_bytes", "gofann_beam_search",
             "gofann_beam_search_noalloc",
             "gofann_posting_scan", "gofann_rerank", "gofann_route_merge", "gofann_shard_merge",
             "gofann_row_record_stride", "gofann_build_row_records", "gofann_offset_ids")

@@ -15,6 +15,8 @@
  *   gofann_pq_encode          pq::transform (encode)  tools/quantization/pq_builder.cu:125-151
  *   gofann_rabitq_quantize    quantize_rabitq_queries_int8_kernel + compute_rabitq_query_factors_kernel
  *                                                     src/search/rabitq/backend_rabitq.cu:2898-2964
+ *   gofann_rabitq_rotate      RabitqQueryRotation::apply  src/search/rabitq/rabitq_query_rotation.cuh:71-87
+ *   gofann_rabitq_centroid_dist_tc  RabitqQueryRotation::centroid_distances  rabitq_query_rotation.cuh:89-113
  *   gofann_rabitq_score       score_rabitq_code_device<kUseInt8Score=true>
  *                                                     src/search/rabitq/backend_rabitq.cu:3100-3200
  *   gofann_beam_search        native_warp_independent_search_kernel_impl (device-resident)
@@ -273,6 +275,37 @@ GOFANN_API int gofann_rabitq_quantize(const float* rotated, uint32_t n, uint32_t
 GOFANN_API int gofann_rabitq_centroid_dist(const float* rotated, uint32_t n, const float* anchors,
                                 uint32_t num_anchors, uint32_t padded_dim, float* gdist_out,
                                 void* stream);
+
+/* Precision of the tensor-core preparation GEMMs: GOFANN_GEMM_TF32 = one
+ * TF32 pass (index-time use), GOFANN_GEMM_TF32X3 = three TF32 passes on the
+ * split operands (x = tf32(x) + tf32(x - tf32(x))), FP32-accurate to the
+ * reference's tolerance (rabitq_query_rotation_test.cu:30-32, 48-50). */
+enum { GOFANN_GEMM_TF32 = 0, GOFANN_GEMM_TF32X3 = 1 };
+
+/* Bytes of device scratch (256-byte aligned) for one preparation GEMM of
+ * `rows` x `k` by `cols` x `k`: the prepared operands and two norm vectors. */
+GOFANN_API size_t gofann_rabitq_gemm_scratch_bytes(uint32_t rows, uint32_t k, uint32_t cols, int precision);
+
+/* Query rotation q' = q . R (RabitqQueryRotation::apply,
+ * rabitq_query_rotation.cuh:71-87) on the tensor cores (tcgen05, TMA):
+ * queries device [n][dim] f32, rotation device [dim][padded_dim] f32 (row
+ * major, as the reference stores it; padded_dim >= dim), rotated_out device
+ * [n][padded_dim].  scratch (256-byte aligned): gofann_rabitq_gemm_scratch_bytes(n, dim,
+ * padded_dim, precision).  status (device, may be NULL) is set to
+ * GOFANN_ERR_TIMEOUT if a bounded device wait ran out. */
+GOFANN_API int gofann_rabitq_rotate(const float* queries, uint32_t n, uint32_t dim, const float* rotation,
+                                    uint32_t padded_dim, int precision, float* rotated_out, void* scratch,
+                                    size_t scratch_bytes, int32_t* status, void* stream);
+
+/* Centroid distances on the tensor cores (RabitqQueryRotation::
+ * centroid_distances, rabitq_query_rotation.cuh:89-113): gdist[q][a] =
+ * max(0, -2 q'.c_a + |q'|^2 + |c_a|^2) for rotated queries [n][padded_dim]
+ * and anchors [num_anchors][padded_dim].  scratch:
+ * gofann_rabitq_gemm_scratch_bytes(n, padded_dim, num_anchors, precision). */
+GOFANN_API int gofann_rabitq_centroid_dist_tc(const float* rotated, uint32_t n, const float* anchors,
+                                              uint32_t num_anchors, uint32_t padded_dim, int precision,
+                                              float* gdist_out, void* scratch, size_t scratch_bytes,
+                                              int32_t* status, void* stream);
 
 /* 1-bit int8 estimator for pairs (backend_rabitq.cu:3100-3200):
  * est = (f_add + gdist) + f_rescale * (float(ip_int) * scale + k1xsumq). */
