@@ -75,6 +75,63 @@ __global__ void __launch_bounds__(256) rq_centroid_dist_kernel(const float* __re
     }
 }
 
+// 1-bit RaBitQ encoder (index time; the quantizer of the reference's RaBitQ
+// artefacts, third_party/cuvs_rabitq/.../quantizer_gpu_fast.cu:180-270, with
+// the MSB-first packing of quantizer_gpu.cu:31-46): one warp per vector.  For
+// the residual r = (x - c) R and the rotated centroid c of its anchor, bit d
+// = (r_d > 0), xu_d = bit - 1/2, and over the padded dimensions
+//   rr = sum r^2, rxu = sum r xu, cxu = sum c xu, xuxu = P / 4:
+//   f_add = rr + 2 rr cxu / rxu,  f_rescale = -2 rr / rxu,
+//   f_err = 2 * 1.9 * sqrt(rr) * sqrt(max(0, (rr xuxu / rxu^2 - 1) / (P - 1)))
+// (rxu = 0 is replaced by 1e-30).  FP32 throughout in a fixed order: lane l
+// accumulates dimensions l, l + 32, ... (rr by fma), the lane partials are
+// combined by an xor butterfly 16..1, and the factor formulas run as written
+// left to right with correctly rounded division and square root.  Code word
+// w holds dimensions 32w..32w+31 with dimension 32w+j at bit 31-j: the
+// bit-reversed ballot of the lanes' bits.
+__global__ void __launch_bounds__(256) rq_encode_kernel(const float* __restrict__ residual,
+                                                        const float* __restrict__ rotated_centroids,
+                                                        const uint32_t* __restrict__ anchor_ids, uint32_t n,
+                                                        uint32_t padded_dim, uint32_t* __restrict__ codes,
+                                                        float* __restrict__ factors)
+{
+    const uint32_t v = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (v >= n) return;
+    const float* r = residual + static_cast<size_t>(v) * padded_dim;
+    const float* c = rotated_centroids + static_cast<size_t>(anchor_ids[v]) * padded_dim;
+    uint32_t* code = codes + static_cast<size_t>(v) * (padded_dim / 32);
+    float rr = 0.0f, rxu = 0.0f, cxu = 0.0f;
+    for (uint32_t w = 0; w < padded_dim / 32; ++w) {
+        const uint32_t d = w * 32 + lane;
+        const float x = r[d];
+        const bool bit = x > 0.0f;
+        const float xu = bit ? 0.5f : -0.5f;
+        rr = __fmaf_rn(x, x, rr);
+        rxu = __fadd_rn(rxu, __fmul_rn(x, xu));
+        cxu = __fadd_rn(cxu, __fmul_rn(c[d], xu));
+        const unsigned b = __ballot_sync(kFull, bit);
+        if (lane == 0) code[w] = __brev(b);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        rr = __fadd_rn(rr, __shfl_xor_sync(kFull, rr, off));
+        rxu = __fadd_rn(rxu, __shfl_xor_sync(kFull, rxu, off));
+        cxu = __fadd_rn(cxu, __shfl_xor_sync(kFull, cxu, off));
+    }
+    if (lane == 0) {
+        const float xuxu = __fmul_rn(static_cast<float>(padded_dim), 0.25f);
+        if (rxu == 0.0f) rxu = 1e-30f;
+        float* f = factors + static_cast<size_t>(v) * 3;
+        f[0] = __fadd_rn(rr, __fdiv_rn(__fmul_rn(__fmul_rn(2.0f, rr), cxu), rxu));
+        f[1] = __fdiv_rn(__fmul_rn(-2.0f, rr), rxu);
+        float t = __fdiv_rn(__fsub_rn(__fdiv_rn(__fmul_rn(rr, xuxu), __fmul_rn(rxu, rxu)), 1.0f),
+                            static_cast<float>(padded_dim - 1));
+        if (!(t > 0.0f)) t = 0.0f;
+        f[2] = __fmul_rn(__fmul_rn(3.8f, __fsqrt_rn(rr)), __fsqrt_rn(t));
+    }
+}
+
 // One warp per pair: lanes split the code words; the integer partials are
 // exact, then the combine runs on lane 0.
 __global__ void rq_score_pairs_kernel(gofann_codes codes, gofann_prepared prep,
@@ -143,6 +200,23 @@ int gofann_rabitq_centroid_dist(const float* rotated, uint32_t n, const float* a
     rq_centroid_dist_kernel<<<dim3(n, ay), 256, smem, as_stream(stream)>>>(rotated, anchors, num_anchors,
                                                                            padded_dim, gdist_out);
     GOFANN_CHECK_LAUNCH("rq_centroid_dist_kernel");
+    return GOFANN_OK;
+}
+
+int gofann_rabitq_encode(const float* residual, const float* rotated_centroids, const uint32_t* anchor_ids,
+                         uint32_t n, uint32_t padded_dim, uint8_t* codes_out, float* factors_out, void* stream)
+{
+    if (!residual || !rotated_centroids || !anchor_ids || !codes_out || !factors_out)
+        return fail(GOFANN_ERR_INVALID, "rabitq_encode: null pointer");
+    if (padded_dim < 64 || padded_dim % 64 != 0)
+        return fail(GOFANN_ERR_INVALID, "rabitq_encode: padded_dim %u must be a positive multiple of 64", padded_dim);
+    if ((reinterpret_cast<uintptr_t>(codes_out) & 3) != 0)
+        return fail(GOFANN_ERR_INVALID, "rabitq_encode: codes must be 4-byte aligned");
+    if (n == 0) return GOFANN_OK;
+    const uint64_t threads = static_cast<uint64_t>(n) * 32;
+    rq_encode_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, as_stream(stream)>>>(
+        residual, rotated_centroids, anchor_ids, n, padded_dim, reinterpret_cast<uint32_t*>(codes_out), factors_out);
+    GOFANN_CHECK_LAUNCH("rq_encode_kernel");
     return GOFANN_OK;
 }
 

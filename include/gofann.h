@@ -17,6 +17,8 @@
  *                                                     src/search/rabitq/backend_rabitq.cu:2898-2964
  *   gofann_rabitq_rotate      RabitqQueryRotation::apply  src/search/rabitq/rabitq_query_rotation.cuh:71-87
  *   gofann_rabitq_centroid_dist_tc  RabitqQueryRotation::centroid_distances  rabitq_query_rotation.cuh:89-113
+ *   gofann_rabitq_encode      RaBitQ quantizer (cuVS fork) third_party/cuvs_rabitq/src/neighbors/ivf_rabitq/
+ *                                                     gpu_index/quantizer_gpu_fast.cu:180-270
  *   gofann_rabitq_score       score_rabitq_code_device<kUseInt8Score=true>
  *                                                     src/search/rabitq/backend_rabitq.cu:3100-3200
  *   gofann_beam_search        native_warp_independent_search_kernel_impl (device-resident)
@@ -306,6 +308,17 @@ GOFANN_API int gofann_rabitq_centroid_dist_tc(const float* rotated, uint32_t n, 
                                               uint32_t num_anchors, uint32_t padded_dim, int precision,
                                               float* gdist_out, void* scratch, size_t scratch_bytes,
                                               int32_t* status, void* stream);
+
+/* 1-bit RaBitQ encoder (index time; quantizer_gpu_fast.cu:180-270 of the
+ * reference's cuVS RaBitQ fork): residuals [n][padded_dim] = (x - c) R,
+ * rotated centroids [num_anchors][padded_dim] and each vector's anchor ->
+ * codes [n][padded_dim/8] (4-byte aligned; layout of gofann_codes) and
+ * factors [n][3] = (f_add, f_rescale, f_err).  FP32 in a fixed order (lane
+ * partials over dimensions l, l+32, ..., xor butterfly, formulas left to
+ * right), bit-exact to the CPU oracle given the residuals. */
+GOFANN_API int gofann_rabitq_encode(const float* residual, const float* rotated_centroids,
+                                    const uint32_t* anchor_ids, uint32_t n, uint32_t padded_dim,
+                                    uint8_t* codes_out, float* factors_out, void* stream);
 
 /* 1-bit int8 estimator for pairs (backend_rabitq.cu:3100-3200):
  * est = (f_add + gdist) + f_rescale * (float(ip_int) * scale + k1xsumq). */

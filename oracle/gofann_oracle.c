@@ -248,6 +248,58 @@ void oracle_rabitq_encode(const float* residual, const float* rotated_centroid, 
     }
 }
 
+/* The device encoder's FP32 arithmetic (gofann_rabitq_encode): 32 lane
+ * partials over dimensions l, l+32, ..., an xor butterfly, the factor
+ * formulas left to right; code word w = dimensions 32w..32w+31 MSB first
+ * (the RaBitQ quantizer, quantizer_gpu_fast.cu:180-270, packing
+ * quantizer_gpu.cu:31-46). */
+void oracle_rabitq_encode_f32(const float* residual, const float* rotated_centroid, uint32_t n,
+                              uint32_t padded_dim, const uint32_t* anchor_ids, uint32_t* codes, float* factors)
+{
+    const uint32_t words = padded_dim / 32;
+    for (uint32_t i = 0; i < n; ++i) {
+        const float* r = residual + (size_t)i * padded_dim;
+        const float* c = rotated_centroid + (size_t)anchor_ids[i] * padded_dim;
+        float rr[32], rxu[32], cxu[32];
+        for (int l = 0; l < 32; ++l) rr[l] = rxu[l] = cxu[l] = 0.0f;
+        for (uint32_t w = 0; w < words; ++w) {
+            uint32_t word = 0;
+            for (int l = 0; l < 32; ++l) {
+                const uint32_t d = w * 32 + (uint32_t)l;
+                const float x = r[d];
+                const int bit = x > 0.0f;
+                const float xu = bit ? 0.5f : -0.5f;
+                rr[l] = fmaf(x, x, rr[l]);
+                rxu[l] = rxu[l] + x * xu;
+                cxu[l] = cxu[l] + c[d] * xu;
+                if (bit) word |= 0x80000000u >> l;
+            }
+            codes[(size_t)i * words + w] = word;
+        }
+        for (int off = 16; off > 0; off >>= 1) {
+            float nrr[32], nrxu[32], ncxu[32];
+            for (int l = 0; l < 32; ++l) {
+                nrr[l] = rr[l] + rr[l ^ off];
+                nrxu[l] = rxu[l] + rxu[l ^ off];
+                ncxu[l] = cxu[l] + cxu[l ^ off];
+            }
+            memcpy(rr, nrr, sizeof rr);
+            memcpy(rxu, nrxu, sizeof rxu);
+            memcpy(cxu, ncxu, sizeof cxu);
+        }
+        const float R = rr[0], C = cxu[0];
+        float X = rxu[0];
+        const float xuxu = (float)padded_dim * 0.25f;
+        if (X == 0.0f) X = 1e-30f;
+        float* f = factors + (size_t)i * 3;
+        f[0] = R + ((2.0f * R) * C) / X;
+        f[1] = (-2.0f * R) / X;
+        float t = ((R * xuxu) / (X * X) - 1.0f) / (float)(padded_dim - 1);
+        if (!(t > 0.0f)) t = 0.0f;
+        f[2] = (3.8f * sqrtf(R)) * sqrtf(t);
+    }
+}
+
 /* ------------------------------------------------------- visited hash */
 /* native_visited_hash.cuh:11-61 */
 static uint32_t hash_code(uint32_t v)

@@ -29,6 +29,8 @@ void oracle_rabitq_encode(const float* residual, const float* rotated_centroid, 
                           float* factors);
 int oracle_hash_test(const uint32_t* t, uint32_t v);
 int oracle_pickup_index(const float* keys, const uint32_t* vals, int size);
+void oracle_rabitq_encode_f32(const float* residual, const float* rotated_centroid, uint32_t n,
+                              uint32_t padded_dim, const uint32_t* anchor_ids, uint32_t* codes, float* factors);
 int oracle_hash_add(uint32_t* t, uint32_t v);
 int oracle_pred_enabled(const gofann_routes* r, uint32_t route);
 int oracle_pred_matches(const gofann_routes* r, const gofann_attrs* a, uint32_t route, uint32_t sample);

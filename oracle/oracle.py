@@ -74,6 +74,7 @@ def olib() -> C.CDLL:
         L.oracle_sl_sort.argtypes = [sp, sp, C.c_int]
         L.oracle_hash_test.argtypes = [sp, U32]
         L.oracle_pickup_index.argtypes = [sp, sp, C.c_int]
+        L.oracle_rabitq_encode_f32.argtypes = [sp, sp, U32, U32, sp, sp, sp]
         L.oracle_pickup_index.restype = C.c_int
         L.oracle_pred_matches.argtypes = [C.POINTER(A.Routes), C.POINTER(A.Attrs), U32, U32]
         L.oracle_labels_match.argtypes = [C.POINTER(A.Routes), C.POINTER(A.Attrs), U32, U32]
@@ -325,6 +326,19 @@ def pred_matches(routes: dict, attrs: dict, pair_route, pair_sample):
     L = olib()
     return np.array([L.oracle_pred_matches(C.byref(rs), C.byref(at), int(r), int(s))
                      for r, s in zip(pair_route, pair_sample)], np.uint8)
+
+
+def rabitq_encode_f32(residual, rotated_centroids, anchor_ids):
+    """The device encoder's FP32 arithmetic: codes [n][padded_dim/8] (u8,
+    words little-endian) and factors [n][3]."""
+    r = _c(residual, np.float32)
+    c = _c(rotated_centroids, np.float32)
+    a = _c(anchor_ids, np.uint32)
+    n, pd = r.shape
+    words = np.empty((n, pd // 32), np.uint32)
+    factors = np.empty((n, 3), np.float32)
+    olib().oracle_rabitq_encode_f32(P(r), P(c), n, pd, P(a), P(words), P(factors))
+    return words.view(np.uint8).reshape(n, pd // 8), factors
 
 
 def pickup_index(keys, vals, size: int) -> int:

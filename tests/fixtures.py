@@ -11,8 +11,8 @@ from gofann import _abi as A, index_build, planner, synth
 
 
 @functools.lru_cache(maxsize=None)
-def cfg1_small(n=6000, n_labels=16, n_queries=160, threshold=400, degree=32, pq_dim=32, seed=0):
-    w = synth.config1(seed=seed, n=n, n_labels=n_labels, n_queries=n_queries)
+def cfg1_small(n=6000, n_labels=16, n_queries=160, threshold=400, degree=32, pq_dim=32, seed=0, dim=128):
+    w = synth.config1(seed=seed, n=n, n_labels=n_labels, n_queries=n_queries, dim=dim)
     idx = index_build.build_index(w, threshold=threshold, degree=degree, pq_dim=pq_dim, seed=seed)
     plan = planner.plan_queries(idx, w.query_labels)
     return w, idx, plan
@@ -47,11 +47,12 @@ def random_orthogonal(p: int, seed: int) -> np.ndarray:
 
 
 @functools.lru_cache(maxsize=None)
-def rabitq_artifacts(n=6000, n_labels=16, n_queries=160, n_anchors=16, seed=3):
-    """RaBitQ codes for a config-1 style workload: rotation, anchors, 1-bit
-    codes and factors from the oracle's encoder; rotated queries."""
+def rabitq_artifacts(n=6000, n_labels=16, n_queries=160, n_anchors=16, seed=3, dim=128):
+    """RaBitQ codes for a config-1 style workload of `dim` dimensions:
+    rotation, anchors, 1-bit codes and factors from the oracle's encoder;
+    rotated queries."""
     from oracle import oracle as O
-    w, idx, plan = cfg1_small(n=n, n_labels=n_labels, n_queries=n_queries)
+    w, idx, plan = cfg1_small(n=n, n_labels=n_labels, n_queries=n_queries, dim=dim)
     rng = np.random.default_rng(seed)
     p = ((w.dim + 63) // 64) * 64
     rot = random_orthogonal(p, seed)

@@ -436,9 +436,33 @@ def test_row_records_reject_out_of_range_sample(L):
     assert r[8].any()
 
 
-@pytest.mark.parametrize("vi", [0, 1, 3])
-def test_beam_search_rabitq_bitexact(L, vi):
-    w, idx, plan, rq, anchors, qr = rabitq_artifacts()
+@pytest.mark.parametrize("pd", [64, 512, 4096])
+def test_rabitq_encode_bitexact(L, pd):
+    """Device 1-bit encoder against the oracle's restatement of its FP32
+    order, given the residuals: codes and factor bits equal (exact zeros and
+    -0.0 give bit 0; a vector of zeros takes the rxu = 0 guard)."""
+    rng = np.random.default_rng(pd)
+    n, a = 777, 13
+    r = rng.standard_normal((n, pd)).astype(np.float32)
+    r[5, ::3] = 0.0
+    r[6, 1::4] = -0.0
+    r[7] = 0.0
+    c = rng.standard_normal((a, pd)).astype(np.float32)
+    aid = rng.integers(0, a, size=n).astype(np.uint32)
+    want_c, want_f = O.rabitq_encode_f32(r, c, aid)
+    codes = torch.empty((n, pd // 8), dtype=torch.uint8, device="cuda")
+    f = torch.empty((n, 3), dtype=torch.float32, device="cuda")
+    A.check(L.gofann_rabitq_encode(dptr(r), dptr(c), dptr(aid), n, pd, A.ptr(codes), A.ptr(f), stream()), "encode")
+    torch.cuda.synchronize()
+    assert np.array_equal(codes.cpu().numpy(), want_c)
+    assert np.array_equal(fbits(f.cpu().numpy()), fbits(want_f))
+
+
+@pytest.mark.parametrize("vi,dim", [(0, 128), (1, 128), (3, 128), (0, 512), (1, 4096)])
+def test_beam_search_rabitq_bitexact(L, vi, dim):
+    """RaBitQ traversal at padded dims 128, 512 and 4096 (64- and 512-byte
+    codes, the config-4 and config-3 widths)."""
+    w, idx, plan, rq, anchors, qr = rabitq_artifacts(n=6000 if dim == 128 else 2500, dim=dim)
     dprep, hprep = _rq_prepared(L, qr, anchors)
     params = dict(BEAM_VARIANTS[vi], scorer=A.SCORER_RABITQ, pq_mode=A.PQ_LUT_GLOBAL)
     want = O.beam_search(idx.graph(), idx.attrs(), rq, hprep, plan.graph_routes, threads=8, **params)
@@ -531,8 +555,9 @@ def test_posting_scan_pq_u8_codebook_bitexact(L, k, pq_dim):
     assert np.array_equal(fbits(got[1]), fbits(want[1]))
 
 
-def test_posting_scan_rabitq_bitexact(L):
-    w, idx, plan, rq, anchors, qr = rabitq_artifacts()
+@pytest.mark.parametrize("dim", [128, 4096])
+def test_posting_scan_rabitq_bitexact(L, dim):
+    w, idx, plan, rq, anchors, qr = rabitq_artifacts(n=6000 if dim == 128 else 2500, dim=dim)
     dprep, hprep = _rq_prepared(L, qr, anchors)
     routes = plan.graph_routes  # scan each graph route's label posting
     lab = routes["primary_label"]
