@@ -132,6 +132,33 @@ __global__ void __launch_bounds__(256) rq_encode_kernel(const float* __restrict_
     }
 }
 
+// Entry rows of graph routes from the centroid distances: one warp per
+// route takes the anchor of smallest distance (lowest index on ties) and
+// starts the route at that anchor's entry row.
+__global__ void __launch_bounds__(256) rq_entries_kernel(const float* __restrict__ gdist, uint32_t num_anchors,
+                                                         const uint32_t* __restrict__ query_row, uint32_t n_routes,
+                                                         const uint32_t* __restrict__ anchor_entry,
+                                                         uint32_t* __restrict__ start_out)
+{
+    const uint32_t r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= n_routes) return;
+    const float* g = gdist + static_cast<size_t>(query_row[r]) * num_anchors;
+    float bd = FLT_MAX;
+    uint32_t bi = kU32Max;
+    for (uint32_t a = lane; a < num_anchors; a += 32) {
+        const float d = g[a];
+        if (bi == kU32Max || d < bd) { bd = d; bi = a; }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float od = __shfl_xor_sync(kFull, bd, off);
+        const uint32_t oi = __shfl_xor_sync(kFull, bi, off);
+        if (oi != kU32Max && (bi == kU32Max || od < bd || (od == bd && oi < bi))) { bd = od; bi = oi; }
+    }
+    if (lane == 0) start_out[r] = bi == kU32Max ? 0u : anchor_entry[bi];
+}
+
 // One warp per pair: lanes split the code words; the integer partials are
 // exact, then the combine runs on lane 0.
 __global__ void rq_score_pairs_kernel(gofann_codes codes, gofann_prepared prep,
@@ -217,6 +244,20 @@ int gofann_rabitq_encode(const float* residual, const float* rotated_centroids, 
     rq_encode_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, as_stream(stream)>>>(
         residual, rotated_centroids, anchor_ids, n, padded_dim, reinterpret_cast<uint32_t*>(codes_out), factors_out);
     GOFANN_CHECK_LAUNCH("rq_encode_kernel");
+    return GOFANN_OK;
+}
+
+int gofann_rabitq_route_entries(const float* gdist, uint32_t num_anchors, const uint32_t* query_row, uint32_t n_routes,
+                                const uint32_t* anchor_entry, uint32_t* start_local_out, void* stream)
+{
+    if (!gdist || !query_row || !anchor_entry || !start_local_out)
+        return fail(GOFANN_ERR_INVALID, "rabitq_route_entries: null pointer");
+    if (num_anchors == 0) return fail(GOFANN_ERR_INVALID, "rabitq_route_entries: no anchors");
+    if (n_routes == 0) return GOFANN_OK;
+    const uint64_t threads = static_cast<uint64_t>(n_routes) * 32;
+    rq_entries_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, as_stream(stream)>>>(
+        gdist, num_anchors, query_row, n_routes, anchor_entry, start_local_out);
+    GOFANN_CHECK_LAUNCH("rq_entries_kernel");
     return GOFANN_OK;
 }
 

@@ -219,6 +219,7 @@ def lib() -> C.CDLL:
         "gofann_rabitq_centroid_dist": [sp, U32, sp, U32, U32, sp, sp],
         "gofann_rabitq_rotate": [sp, U32, U32, sp, U32, C.c_int, sp, sp, C.c_size_t, sp, sp],
         "gofann_rabitq_encode": [sp, sp, sp, U32, U32, sp, sp, sp],
+        "gofann_rabitq_route_entries": [sp, U32, sp, U32, sp, sp, sp],
         "gofann_rabitq_centroid_dist_tc": [sp, U32, sp, U32, U32, C.c_int, sp, sp, C.c_size_t, sp, sp],
         "gofann_rabitq_score": [C.POINTER(Codes), C.POINTER(Prepared), sp, sp, U32, sp, sp, sp],
         "gofann_beam_search": [C.POINTER(Graph), C.POINTER(Attrs), C.POINTER(Codes), C.POINTER(Prepared),
@@ -264,7 +265,8 @@ def check(status: int, where: str) -> None:
 EXPORTED = ("gofann_abi_version", "gofann_last_error", "gofann_device_sm_count", "gofann_pq_build_lut",
             "gofann_pq_adc", "gofann_pq_encode", "gofann_rabitq_quantize", "gofann_rabitq_centroid_dist",
             "gofann_rabitq_score", "gofann_rabitq_gemm_scratch_bytes", "gofann_rabitq_rotate",
-            "gofann_rabitq_centroid_dist_tc", "gofann_rabitq_encode", "gofann_beam_search_scratch_bytes", "gofann_beam_search",
+            "gofann_rabitq_centroid_dist_tc", "gofann_rabitq_encode", "gofann_rabitq_route_entries",
+            "gofann_beam_search_scratch_bytes", "gofann_beam_search",
             "gofann_beam_search_noalloc",
             "gofann_posting_scan", "gofann_rerank", "gofann_route_merge", "gofann_shard_merge",
             "gofann_row_record_stride", "gofann_build_row_records", "gofann_offset_ids")

@@ -320,6 +320,16 @@ GOFANN_API int gofann_rabitq_encode(const float* residual, const float* rotated_
                                     const uint32_t* anchor_ids, uint32_t n, uint32_t padded_dim,
                                     uint8_t* codes_out, float* factors_out, void* stream);
 
+/* Entry rows of graph routes (no counterpart in the reference, whose routes
+ * start at a fixed row per graph): start_local_out[r] =
+ * anchor_entry[argmin_a gdist[query_row[r]][a]] (lowest anchor on ties),
+ * i.e. each route starts at the entry row of its query's nearest anchor.
+ * gdist device [rows][num_anchors] (gofann_rabitq_centroid_dist_tc),
+ * anchor_entry device [num_anchors] (a row of each anchor's cluster). */
+GOFANN_API int gofann_rabitq_route_entries(const float* gdist, uint32_t num_anchors, const uint32_t* query_row,
+                                           uint32_t n_routes, const uint32_t* anchor_entry,
+                                           uint32_t* start_local_out, void* stream);
+
 /* 1-bit int8 estimator for pairs (backend_rabitq.cu:3100-3200):
  * est = (f_add + gdist) + f_rescale * (float(ip_int) * scale + k1xsumq). */
 GOFANN_API int gofann_rabitq_score(const gofann_codes* codes, const gofann_prepared* prep,

@@ -458,6 +458,20 @@ def test_rabitq_encode_bitexact(L, pd):
     assert np.array_equal(fbits(f.cpu().numpy()), fbits(want_f))
 
 
+def test_rabitq_route_entries(L):
+    """Each route starts at the entry row of its query's nearest anchor
+    (lowest anchor on equal distances)."""
+    rng = np.random.default_rng(4)
+    rows, na, nr = 50, 300, 777
+    g = rng.integers(0, 40, size=(rows, na)).astype(np.float32)  # many ties
+    qr = rng.integers(0, rows, size=nr).astype(np.uint32)
+    entry = rng.permutation(100000)[:na].astype(np.uint32)
+    out = torch.empty(nr, dtype=torch.int32, device="cuda")
+    A.check(L.gofann_rabitq_route_entries(dptr(g), na, dptr(qr), nr, dptr(entry), A.ptr(out), stream()), "entries")
+    torch.cuda.synchronize()
+    assert np.array_equal(host(out, np.uint32), entry[np.argmin(g[qr], axis=1)])
+
+
 @pytest.mark.parametrize("vi,dim", [(0, 128), (1, 128), (3, 128), (0, 512), (1, 4096)])
 def test_beam_search_rabitq_bitexact(L, vi, dim):
     """RaBitQ traversal at padded dims 128, 512 and 4096 (64- and 512-byte
