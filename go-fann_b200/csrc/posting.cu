@@ -1,16 +1,36 @@
-// posting.cu — brute-force scans of low-frequency label postings (and any
-// explicit candidate slice), fused DNF filter, top-shortlist by (dist, id).
+// posting.cu — brute-force scans of label postings and attribute-order
+// slices, fused DNF filter, top-shortlist by (dist, id).
 //
 // The reference scans one route per single-thread block, inserting into a
 // (dist, id) max-heap one candidate at a time (lowfreq_pq_scan_kernel,
 // src/search/pq/backend_pq.cu:2046-2185; RaBitQ twin backend_rabitq.cu:
-// 5396-5751).  With unique candidate ids that heap ends holding exactly the
-// k smallest (dist, id) pairs of the passing candidates, whatever the
-// insertion order, and score-first elision only skips candidates that cannot
-// enter.  So here one 256-thread block per route scores a chunk of
-// candidates in parallel into shared memory and a bitonic sort keeps the k
-// best; the PQ LUT (or RaBitQ bit planes) is staged in shared memory once
-// per route.  PQ distances keep the reference's sequential subspace order.
+// 5396-5751).  That heap ends holding exactly the k smallest (dist, id)
+// pairs of the passing candidates, whatever the insertion order, and its
+// score-first elision only skips candidates that cannot enter.  Here one
+// 256-thread block scores a route's candidates in parallel and keeps the k
+// smallest pairs with a threshold filter: a candidate enters a shared-memory
+// buffer only when it is below the k-th pair of the candidates merged so far
+// (so it could still be in the result), and a full buffer is merged into the
+// running top-k by a bitonic sort.  After the first merge only about
+// k ln(n / k) of n candidates pass, so sorting costs little next to scoring.
+//
+// Scorers:
+//  * PQ tables: the query's LUT row (given, or built per route from the
+//    codebook as computePQTable does inside the reference's scan) staged in
+//    shared memory; the sum is sequential over subspaces
+//    (backend_pq.cu:2101-2104), one candidate per thread;
+//  * PQ_U8 (u8 queries, integer codebook): every table entry and partial sum
+//    is an integer below 2^24, so the sequential float sum equals the
+//    integer sum of byte differences against a packed codebook.  The blocks
+//    are persistent: each packs the codebook into shared memory once and
+//    then scans routes blockIdx.x, blockIdx.x + gridDim.x, ... -- no
+//    per-route table or codebook read;
+//  * RaBitQ: padded_dim = 128 G (G = 1..32) gives each candidate G lanes;
+//    a lane reads 16 bytes of the code (one coalesced 16 G-byte row per
+//    candidate) against its 4 words of the query's bit planes, held in
+//    registers for the whole route, and the lanes' partial inner products
+//    are summed by a warp reduction.  Other padded dims score one candidate
+//    per thread against the planes in shared memory.
 #include "pq_device.cuh"
 #include "rq_device.cuh"
 
@@ -18,15 +38,18 @@ namespace gofann {
 namespace {
 
 constexpr int kScanThreads = 256;
-constexpr int kSortSize = 4096;          // pairs per sort round
-constexpr int kKeep = 512;               // slots reserved for the running top-k (>= 400)
-constexpr int kChunk = kSortSize - kKeep;
+constexpr int kScanWarps = kScanThreads / kWarp;
+constexpr int kSortSize = 2048;      // running top-k + buffer, sorted together
+constexpr int kBatches = 4;          // 32-candidate batches per warp between buffer checks
+constexpr int kRoundCands = kScanWarps * kWarp * kBatches;
 
-__device__ __forceinline__ void bitonic_sort_pairs(float* d, uint32_t* id, int n, int tid, int nthreads)
+enum ScanKind { kScanPqTable = 0, kScanPqU8 = 1, kScanRabitq = 2 };
+
+__device__ __forceinline__ void bitonic_sort_pairs(float* d, uint32_t* id, int n, int tid)
 {
     for (int size = 2; size <= n; size <<= 1) {
         for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int i = tid; i < n / 2; i += nthreads) {
+            for (int i = tid; i < n / 2; i += kScanThreads) {
                 const int lo = 2 * i - (i & (stride - 1));
                 const int hi = lo + stride;
                 const bool up = (lo & size) == 0;
@@ -45,30 +68,148 @@ __device__ __forceinline__ uint32_t next_pow2(uint32_t x)
     return x <= 1 ? 1u : 1u << (32 - __clz(x - 1));
 }
 
-// One block per route (the hardware balances routes of very different
-// lengths); the sort spans only as many slots as the route has candidates.
-template <int kScorer>
-__global__ void __launch_bounds__(kScanThreads) posting_scan_kernel(
-    gofann_codes codes, gofann_prepared prep, AttrView attrs, gofann_routes routes,
-    const uint32_t* __restrict__ posting_ids, const uint64_t* __restrict__ route_begin,
-    const uint32_t* __restrict__ route_count, int k, uint32_t* __restrict__ out_ids, float* __restrict__ out_d)
+// Running top-k of one route: sorted pairs at [0, keep), the buffer after
+// them.  Empty slots hold (FLT_MAX, UINT32_MAX), the fill of the
+// reference's shortlist heap, which is also the first threshold: a
+// candidate enters only below it, as it enters that heap.
+struct TopK {
+    float* sd;
+    uint32_t* sid;
+    int keep, k;
+};
+struct TopKState {
+    int n_buf;
+    float thr_d;
+    uint32_t thr_id;
+};
+
+__device__ __forceinline__ void topk_reset(const TopK& t, TopKState& st, int tid)
+{
+    for (int i = tid; i < t.keep; i += kScanThreads) { t.sd[i] = FLT_MAX; t.sid[i] = kU32Max; }
+    if (tid == 0) { st.n_buf = 0; st.thr_d = FLT_MAX; st.thr_id = kU32Max; }
+    __syncthreads();
+}
+
+// Buffers (d, s) when it is below the threshold pair (the k-th smallest pair
+// merged so far, or the sentinel before k candidates were merged).
+__device__ __forceinline__ void topk_offer(const TopK& t, TopKState& st, float thr_d, uint32_t thr_id, float d,
+                                           uint32_t s)
+{
+    if (pair_less(d, s, thr_d, thr_id)) {
+        const int p = atomicAdd(&st.n_buf, 1);
+        t.sd[t.keep + p] = d;
+        t.sid[t.keep + p] = s;
+    }
+}
+
+// Sorts the top-k and `n_buf` buffered pairs (block-uniform n_buf).
+__device__ __forceinline__ void topk_merge(const TopK& t, TopKState& st, int n_buf, int tid)
+{
+    const int n = t.keep + n_buf;
+    const int np2 = static_cast<int>(next_pow2(static_cast<uint32_t>(n)));
+    for (int i = n + tid; i < np2; i += kScanThreads) { t.sd[i] = FLT_MAX; t.sid[i] = kU32Max; }
+    __syncthreads();
+    bitonic_sort_pairs(t.sd, t.sid, np2, tid);
+    if (tid == 0) { st.n_buf = 0; st.thr_d = t.sd[t.k - 1]; st.thr_id = t.sid[t.k - 1]; }
+    __syncthreads();
+}
+
+// Posting id at position i of the route, or UINT32_MAX when it fails the
+// route's predicate.
+__device__ __forceinline__ uint32_t scan_candidate(const gofann_routes& routes, const AttrView& attrs,
+                                                   uint32_t route, bool pred_on,
+                                                   const uint32_t* __restrict__ posting_ids, uint64_t begin,
+                                                   uint32_t i, uint32_t count)
+{
+    uint32_t s = kU32Max;
+    if (i < count) {
+        s = __ldg(posting_ids + begin + i);
+        if (s != kU32Max && pred_on && !pred_matches(routes, attrs, route, s)) s = kU32Max;
+    }
+    return s;
+}
+
+// 16-byte streaming load (read once per route: L2 evict-first).
+__device__ __forceinline__ uint4 ld_stream_u32x4(const void* p, uint64_t pol)
+{
+    return ldg_u32x4(reinterpret_cast<const uint4*>(p), pol);
+}
+
+template <int kG>
+__device__ __forceinline__ int32_t group_sum(int32_t v)
+{
+    if constexpr (kG == 32) {
+        return __reduce_add_sync(kFull, v);
+    } else {
+#pragma unroll
+        for (int o = kG / 2; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+        return v;
+    }
+}
+
+struct ScanArgs {
+    gofann_codes codes;
+    gofann_prepared prep;
+    AttrView attrs;
+    gofann_routes routes;
+    const uint32_t* posting_ids;
+    const uint64_t* route_begin;
+    const uint32_t* route_count;
+    int k;
+    uint32_t* out_ids;
+    float* out_d;
+    int32_t* status;
+};
+
+// kKind: ScanKind; kG: lanes per RaBitQ candidate (0 = one thread each).
+template <int kKind, int kG>
+__global__ void __launch_bounds__(kScanThreads) posting_scan_kernel(ScanArgs a)
 {
     extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ TopKState st;
+    __shared__ int s_bad;
     float* sd = reinterpret_cast<float*>(smem_raw);
     uint32_t* sid = reinterpret_cast<uint32_t*>(smem_raw + kSortSize * sizeof(float));
-    float* table = reinterpret_cast<float*>(smem_raw + kSortSize * (sizeof(float) + sizeof(uint32_t)));
-    const int tid = threadIdx.x;
-    const int pq_dim = static_cast<int>(codes.pq_dim);
-    {
-        const uint32_t route = blockIdx.x;
-        const uint32_t row = routes.query_row[route];
-        const bool pred_on = pred_enabled(routes, route);
+    uint32_t* wlist = sid + kSortSize;                                   // [kScanWarps][32]
+    unsigned char* area = reinterpret_cast<unsigned char*>(wlist + kScanWarps * kWarp);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int pq_dim = static_cast<int>(a.codes.pq_dim);
+    const uint64_t stream_pol = l2_stream_policy();
+    int keep = 32;
+    while (keep < a.k) keep <<= 1;
+    const TopK t{sd, sid, keep, a.k};
+    const int cap = kSortSize - keep;
+
+    // PQ_U8: pack the integer codebook once per (persistent) block
+    uint32_t* cbw = reinterpret_cast<uint32_t*>(area);
+    uint32_t* qw = cbw + pq_dim * GOFANN_PQ_CENTROIDS * (kKind == kScanPqU8 ? static_cast<int>(a.prep.dim) / pq_dim / 4
+                                                                             : 0);
+    if constexpr (kKind == kScanPqU8) {
+        if (tid == 0) s_bad = 0;
+        __syncthreads();
+        const bool ok = pack_u8_codebook(a.prep.pq_centroids, static_cast<int>(a.prep.dim), pq_dim, cbw, tid,
+                                         kScanThreads);
+        if (!ok) s_bad = 1;
+        __syncthreads();
+        if (s_bad && tid == 0 && a.status) atomicExch(a.status, GOFANN_ERR_INVALID);
+    }
+
+    for (uint32_t route = blockIdx.x; route < a.routes.n_routes; route += gridDim.x) {
+        const uint32_t row = a.routes.query_row[route];
+        const bool pred_on = pred_enabled(a.routes, route);
+        const uint64_t begin = a.route_begin[route];
+        uint32_t count = a.route_count[route];
+        if constexpr (kKind == kScanPqU8) {
+            if (s_bad) count = 0;  // invalid codebook: empty results, status set
+        }
+        // ---- per-route query state
+        float* table = reinterpret_cast<float*>(area);
         RqQueryView rq{};
-        if constexpr (kScorer == GOFANN_SCORER_PQ) {
-            const int dim = static_cast<int>(prep.dim);
-            if (prep.pq_lut) {
-                const float4* g = reinterpret_cast<const float4*>(prep.pq_lut + static_cast<size_t>(row) * pq_dim *
-                                                                                    GOFANN_PQ_CENTROIDS);
+        if constexpr (kKind == kScanPqTable) {
+            const int dim = static_cast<int>(a.prep.dim);
+            if (a.prep.pq_lut) {
+                const float4* g = reinterpret_cast<const float4*>(a.prep.pq_lut + static_cast<size_t>(row) * pq_dim *
+                                                                                      GOFANN_PQ_CENTROIDS);
                 float4* t4 = reinterpret_cast<float4*>(table);
                 for (int i = tid; i < pq_dim * GOFANN_PQ_CENTROIDS / 4; i += kScanThreads) t4[i] = __ldg(g + i);
             } else {
@@ -76,69 +217,159 @@ __global__ void __launch_bounds__(kScanThreads) posting_scan_kernel(
                 // the reference also runs inside its scan): query row to shared
                 // memory, then thread c evaluates column c of every subspace
                 float* q = table + pq_dim * GOFANN_PQ_CENTROIDS;
-                if (prep.pq_query_dtype == GOFANN_DTYPE_U8) {
-                    const uint8_t* qr = static_cast<const uint8_t*>(prep.pq_query) + static_cast<size_t>(row) * dim;
+                if (a.prep.pq_query_dtype == GOFANN_DTYPE_U8) {
+                    const uint8_t* qr = static_cast<const uint8_t*>(a.prep.pq_query) + static_cast<size_t>(row) * dim;
                     for (int i = tid; i < dim; i += kScanThreads) q[i] = static_cast<float>(qr[i]);
                 } else {
-                    const float* qr = static_cast<const float*>(prep.pq_query) + static_cast<size_t>(row) * dim;
+                    const float* qr = static_cast<const float*>(a.prep.pq_query) + static_cast<size_t>(row) * dim;
                     for (int i = tid; i < dim; i += kScanThreads) q[i] = qr[i];
                 }
                 __syncthreads();
                 const int w = dim / pq_dim;
-                const float* crow = prep.pq_centroids + static_cast<size_t>(tid) * dim;  // kScanThreads == 256
-                const uint64_t keep = l2_keep_policy();  // the codebook is shared by every route
+                const float* crow = a.prep.pq_centroids + static_cast<size_t>(tid) * dim;  // kScanThreads == 256
+                const uint64_t keep_pol = l2_keep_policy();  // the codebook is shared by every route
                 for (int m = 0; m < pq_dim; ++m)
-                    table[m * GOFANN_PQ_CENTROIDS + tid] = pq_entry<0>(q + m * w, crow + m * w, w, keep);
+                    table[m * GOFANN_PQ_CENTROIDS + tid] = pq_entry<0>(q + m * w, crow + m * w, w, keep_pol);
             }
+        } else if constexpr (kKind == kScanPqU8) {
+            const int nw = static_cast<int>(a.prep.dim) / 4;
+            const uint32_t* qr = reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(a.prep.pq_query) +
+                                                                   static_cast<size_t>(row) * a.prep.dim);
+            for (int i = tid; i < nw; i += kScanThreads) qw[i] = __ldg(qr + i);
         } else {
-            rq_build_planes(prep.rq_q8 + static_cast<size_t>(row) * codes.padded_dim,
-                            static_cast<int>(codes.padded_dim), reinterpret_cast<uint32_t*>(table), tid,
+            rq_build_planes(a.prep.rq_q8 + static_cast<size_t>(row) * a.codes.padded_dim,
+                            static_cast<int>(a.codes.padded_dim), reinterpret_cast<uint32_t*>(area), tid,
                             kScanThreads);
-            rq.planes = reinterpret_cast<const uint32_t*>(table);
-            rq.scale = prep.rq_scale[row];
-            rq.k1 = prep.rq_k1xsumq[row];
-            rq.gdist = prep.rq_centroid_dist + static_cast<size_t>(row) * codes.num_anchors;
+            rq.planes = reinterpret_cast<const uint32_t*>(area);
+            rq.scale = a.prep.rq_scale[row];
+            rq.k1 = a.prep.rq_k1xsumq[row];
+            rq.gdist = a.prep.rq_centroid_dist + static_cast<size_t>(row) * a.codes.num_anchors;
         }
-        const uint64_t begin = route_begin[route];
-        const uint32_t count = route_count[route];
-        // one chunk: candidates at [0, count), the sort spans the next power of
-        // two; several: the running top-k at [0, kKeep), chunks after it
-        const bool single = count <= static_cast<uint32_t>(kChunk);
-        const int keep_slots = single ? 0 : kKeep;
-        const int chunk = single ? static_cast<int>(count) : kChunk;
-        const int n_sort = single ? static_cast<int>(next_pow2(count)) : kSortSize;
-        for (int i = tid; i < keep_slots; i += kScanThreads) { sd[i] = FLT_MAX; sid[i] = kU32Max; }
-        __syncthreads();
-        for (uint32_t c0 = 0; c0 < count; c0 += static_cast<uint32_t>(chunk)) {
-            for (int j = tid; j < n_sort - keep_slots; j += kScanThreads) {
-                const uint32_t i = c0 + j;
-                float dist = FLT_MAX;
-                uint32_t s = kU32Max;
-                if (j < chunk && i < count) {
-                    s = posting_ids[begin + i];
-                    if (s != kU32Max && pred_on && !pred_matches(routes, attrs, route, s)) s = kU32Max;
-                    if (s != kU32Max) {
-                        if constexpr (kScorer == GOFANN_SCORER_PQ) {
-                            dist = pq_adc_sequential(table, codes.pq_codes + static_cast<size_t>(s) * pq_dim,
-                                                     pq_dim);
-                        } else {
-                            dist = rq_estimate(codes, rq, s);
+        topk_reset(t, st, tid);  // ends with a barrier: the query state is visible
+
+        // RaBitQ group path: this lane's 4 plane words of every plane
+        [[maybe_unused]] uint32_t pl[8][4];
+        [[maybe_unused]] const int slot = kG > 0 ? lane % (kG > 0 ? kG : 1) : 0;
+        if constexpr (kKind == kScanRabitq && kG > 0) {
+            const int words = static_cast<int>(a.codes.padded_dim / 32);
+#pragma unroll
+            for (int b = 0; b < 8; ++b) {
+                const uint4 v = *reinterpret_cast<const uint4*>(rq.planes + b * words + 4 * slot);
+                pl[b][0] = v.x; pl[b][1] = v.y; pl[b][2] = v.z; pl[b][3] = v.w;
+            }
+        }
+
+        for (uint32_t r0 = 0; r0 < count; r0 += kRoundCands) {
+            const float thr_d = st.thr_d;
+            const uint32_t thr_id = st.thr_id;
+#pragma unroll 1
+            for (int bt = 0; bt < kBatches; ++bt) {
+                const uint32_t pos0 = r0 + static_cast<uint32_t>((bt * kScanWarps + warp) * kWarp);
+                if (pos0 >= count) break;  // warp-uniform
+                const uint32_t s = scan_candidate(a.routes, a.attrs, route, pred_on, a.posting_ids, begin,
+                                                  pos0 + lane, count);
+                if constexpr (kKind == kScanRabitq && kG > 0) {
+                    constexpr int kCpw = 32 / kG;                    // candidates per warp pass
+                    constexpr int kU = kG >= 4 ? 4 : kG;             // passes unrolled
+                    const unsigned live = __ballot_sync(kFull, s != kU32Max);
+                    uint32_t* wl = wlist + warp * kWarp;
+                    if (s != kU32Max) wl[__popc(live & ((1u << lane) - 1u))] = s;
+                    __syncwarp();
+                    const int n_live = __popc(live);
+                    const int g = lane / kG;
+                    const size_t code_bytes = a.codes.padded_dim / 8;
+                    for (int j0 = 0; j0 < n_live; j0 += kCpw * kU) {
+                        uint4 x[kU];
+                        uint32_t sc[kU];
+                        float fa[kU], fr[kU];
+                        uint32_t an[kU];
+#pragma unroll
+                        for (int u = 0; u < kU; ++u) {
+                            const int j = j0 + u * kCpw + g;
+                            sc[u] = j < n_live ? wl[j] : kU32Max;
+                            x[u] = make_uint4(0u, 0u, 0u, 0u);
+                            fa[u] = fr[u] = 0.0f;
+                            an[u] = 0u;
+                            if (sc[u] != kU32Max) {
+                                x[u] = ld_stream_u32x4(a.codes.rq_codes + static_cast<size_t>(sc[u]) * code_bytes +
+                                                           16 * slot,
+                                                       stream_pol);
+                                if (slot == 0) {
+                                    fa[u] = __ldg(a.codes.rq_factors + static_cast<size_t>(sc[u]) * 3);
+                                    fr[u] = __ldg(a.codes.rq_factors + static_cast<size_t>(sc[u]) * 3 + 1);
+                                    an[u] = __ldg(a.codes.rq_anchor_ids + sc[u]);
+                                }
+                            }
+                        }
+#pragma unroll
+                        for (int u = 0; u < kU; ++u) {
+                            int32_t ip = rq_word_ip_planes(x[u].x, pl[0][0], pl[1][0], pl[2][0], pl[3][0], pl[4][0],
+                                                           pl[5][0], pl[6][0], pl[7][0]);
+                            ip += rq_word_ip_planes(x[u].y, pl[0][1], pl[1][1], pl[2][1], pl[3][1], pl[4][1],
+                                                    pl[5][1], pl[6][1], pl[7][1]);
+                            ip += rq_word_ip_planes(x[u].z, pl[0][2], pl[1][2], pl[2][2], pl[3][2], pl[4][2],
+                                                    pl[5][2], pl[6][2], pl[7][2]);
+                            ip += rq_word_ip_planes(x[u].w, pl[0][3], pl[1][3], pl[2][3], pl[3][3], pl[4][3],
+                                                    pl[5][3], pl[6][3], pl[7][3]);
+                            ip = group_sum<kG>(ip);
+                            if (slot == 0 && sc[u] != kU32Max) {
+                                const float d = rq_combine(ip, rq.scale, rq.k1, fa[u], fr[u], __ldg(rq.gdist + an[u]));
+                                topk_offer(t, st, thr_d, thr_id, d, sc[u]);
+                            }
                         }
                     }
+                    __syncwarp();  // wl is rewritten by the next batch
+                } else {
+                    if (s != kU32Max) {
+                        float d;
+                        if constexpr (kKind == kScanPqTable) {
+                            d = pq_adc_sequential(table, a.codes.pq_codes + static_cast<size_t>(s) * pq_dim, pq_dim);
+                        } else if constexpr (kKind == kScanPqU8) {
+                            d = pq_adc_u8_chunked(qw, cbw, a.codes.pq_codes + static_cast<size_t>(s) * pq_dim, pq_dim,
+                                                  stream_pol);
+                        } else {
+                            d = rq_estimate(a.codes, rq, s);
+                        }
+                        topk_offer(t, st, thr_d, thr_id, d, s);
+                    }
                 }
-                sd[keep_slots + j] = s == kU32Max ? FLT_MAX : dist;
-                sid[keep_slots + j] = s;
             }
             __syncthreads();
-            bitonic_sort_pairs(sd, sid, n_sort, tid, kScanThreads);
+            const int n_buf = st.n_buf;
+            __syncthreads();  // every thread has read n_buf before a merge resets it
+            if (n_buf > cap - kRoundCands) topk_merge(t, st, n_buf, tid);
         }
-        for (int i = tid; i < k; i += kScanThreads) {
-            const bool have = i < n_sort && count > 0;
-            const uint32_t id = have ? sid[i] : kU32Max;
-            out_ids[static_cast<size_t>(route) * k + i] = id;
-            out_d[static_cast<size_t>(route) * k + i] = id == kU32Max ? FLT_MAX : sd[i];
+        {
+            const int n_buf = st.n_buf;  // stable: the last round ended with barriers
+            if (n_buf > 0) topk_merge(t, st, n_buf, tid);
         }
+        for (int i = tid; i < a.k; i += kScanThreads) {
+            const uint32_t id = sid[i];
+            a.out_ids[static_cast<size_t>(route) * a.k + i] = id;
+            a.out_d[static_cast<size_t>(route) * a.k + i] = id == kU32Max ? FLT_MAX : sd[i];
+        }
+        __syncthreads();  // the next route overwrites the shared state
     }
+}
+
+template <int kKind, int kG>
+int launch_scan(const ScanArgs& a, size_t smem, bool persistent, cudaStream_t s, const char* what)
+{
+    const auto kern = posting_scan_kernel<kKind, kG>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_status(e, "posting_scan: shared memory attribute");
+    unsigned blocks = a.routes.n_routes;
+    if (persistent) {
+        int per_sm = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kScanThreads, smem);
+        if (e != cudaSuccess) return cuda_status(e, "posting_scan: occupancy");
+        const int sms = sm_count() > 0 ? sm_count() : 148;
+        const unsigned full = static_cast<unsigned>((per_sm > 0 ? per_sm : 1) * sms);
+        if (full < blocks) blocks = full;
+    }
+    kern<<<blocks, kScanThreads, smem, s>>>(a);
+    GOFANN_CHECK_LAUNCH(what);
+    return GOFANN_OK;
 }
 
 }  // namespace
@@ -151,7 +382,8 @@ extern "C" {
 int gofann_posting_scan(const gofann_codes* codes, const gofann_prepared* prep, const gofann_attrs* attrs,
                         const gofann_routes* routes, int scorer, const uint32_t* posting_ids,
                         const uint64_t* route_begin, const uint32_t* route_count, int32_t shortlist_k,
-                        int32_t score_first, uint32_t* out_ids, float* out_dists, void* stream)
+                        int32_t score_first, int32_t pq_mode, uint32_t* out_ids, float* out_dists,
+                        int32_t* status, void* stream)
 {
     (void)score_first;  // identical results either way (see file comment)
     if (!codes || !prep || !routes || !posting_ids || !route_begin || !route_count || !out_ids || !out_dists)
@@ -162,44 +394,74 @@ int gofann_posting_scan(const gofann_codes* codes, const gofann_prepared* prep, 
     if (routes->pred_offsets && (!attrs || !attrs->label_indptr || !routes->clauses || !routes->pred_handles))
         return fail(GOFANN_ERR_INVALID, "posting_scan: predicate arrays missing");
     if (routes->n_routes == 0) return GOFANN_OK;
-    AttrView av{};
+    ScanArgs a{};
+    a.codes = *codes;
+    a.prep = *prep;
+    a.routes = *routes;
     if (attrs) {
-        av.indptr = attrs->label_indptr;
-        av.indices = attrs->label_indices;
-        av.ranges = attrs->range_values;
-        av.n_samples = attrs->n_samples;
-        av.range_count = attrs->range_count;
+        a.attrs.indptr = attrs->label_indptr;
+        a.attrs.indices = attrs->label_indices;
+        a.attrs.ranges = attrs->range_values;
+        a.attrs.n_samples = attrs->n_samples;
+        a.attrs.range_count = attrs->range_count;
     }
-    size_t table_bytes = 0;
+    a.posting_ids = posting_ids;
+    a.route_begin = route_begin;
+    a.route_count = route_count;
+    a.k = shortlist_k;
+    a.out_ids = out_ids;
+    a.out_d = out_dists;
+    a.status = status;
+    const size_t base = static_cast<size_t>(kSortSize) * 8 + static_cast<size_t>(kScanWarps) * kWarp * 4;
+    cudaStream_t s = as_stream(stream);
     if (scorer == GOFANN_SCORER_PQ) {
         if (!codes->pq_codes) return fail(GOFANN_ERR_INVALID, "posting_scan: PQ codes missing");
         if (codes->pq_dim == 0 || codes->pq_dim > static_cast<uint32_t>(kMaxPqDim))
             return fail(GOFANN_ERR_UNSUPPORTED, "posting_scan: pq_dim %u unsupported", codes->pq_dim);
-        table_bytes = static_cast<size_t>(codes->pq_dim) * GOFANN_PQ_CENTROIDS * sizeof(float);
+        if (pq_mode == GOFANN_PQ_U8) {
+            if (!prep->pq_query || !prep->pq_centroids || prep->pq_query_dtype != GOFANN_DTYPE_U8)
+                return fail(GOFANN_ERR_INVALID, "posting_scan: PQ_U8 needs u8 pq_query and pq_centroids");
+            if (prep->dim != 4 * codes->pq_dim || codes->pq_dim % 16 != 0 || prep->dim > 256)
+                return fail(GOFANN_ERR_UNSUPPORTED,
+                            "posting_scan: PQ_U8 needs 4-wide subvectors, pq_dim a multiple of 16 and dim <= 256 "
+                            "(dim %u, pq_dim %u)", prep->dim, codes->pq_dim);
+            if ((reinterpret_cast<uintptr_t>(codes->pq_codes) & 15) != 0 ||
+                (reinterpret_cast<uintptr_t>(prep->pq_query) & 3) != 0)
+                return fail(GOFANN_ERR_INVALID, "posting_scan: PQ_U8 needs 16-byte aligned codes, 4-byte aligned "
+                                                "queries");
+            const size_t smem = base + static_cast<size_t>(codes->pq_dim) * GOFANN_PQ_CENTROIDS * 4 + prep->dim;
+            return launch_scan<kScanPqU8, 0>(a, smem, true, s, "posting_scan_kernel(u8)");
+        }
+        size_t table_bytes = static_cast<size_t>(codes->pq_dim) * GOFANN_PQ_CENTROIDS * sizeof(float);
         if (!prep->pq_lut) {
             if (!prep->pq_query || !prep->pq_centroids || prep->dim == 0 || prep->dim % codes->pq_dim != 0 ||
                 prep->dim > 4096)
                 return fail(GOFANN_ERR_INVALID, "posting_scan: needs pq_lut, or pq_query + pq_centroids + dim");
             table_bytes += static_cast<size_t>(prep->dim) * sizeof(float);
         }
-    } else if (scorer == GOFANN_SCORER_RABITQ) {
-        if (!codes->rq_codes || !prep->rq_q8) return fail(GOFANN_ERR_INVALID, "posting_scan: RaBitQ arrays missing");
-        if (codes->padded_dim == 0 || codes->padded_dim % 64 != 0 || codes->padded_dim > 4096)
-            return fail(GOFANN_ERR_UNSUPPORTED, "posting_scan: padded_dim %u unsupported", codes->padded_dim);
-        table_bytes = static_cast<size_t>(codes->padded_dim);
-    } else {
-        return fail(GOFANN_ERR_INVALID, "posting_scan: unknown scorer %d", scorer);
+        return launch_scan<kScanPqTable, 0>(a, base + table_bytes, false, s, "posting_scan_kernel(pq)");
     }
-    const size_t smem = static_cast<size_t>(kSortSize) * 8 + table_bytes;
-    cudaStream_t s = as_stream(stream);
-    const auto kern = scorer == GOFANN_SCORER_PQ ? posting_scan_kernel<GOFANN_SCORER_PQ>
-                                                 : posting_scan_kernel<GOFANN_SCORER_RABITQ>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return cuda_status(e, "posting_scan: shared memory attribute");
-    kern<<<routes->n_routes, kScanThreads, smem, s>>>(*codes, *prep, av, *routes, posting_ids, route_begin,
-                                                      route_count, shortlist_k, out_ids, out_dists);
-    GOFANN_CHECK_LAUNCH("posting_scan_kernel");
-    return GOFANN_OK;
+    if (scorer == GOFANN_SCORER_RABITQ) {
+        if (!codes->rq_codes || !prep->rq_q8) return fail(GOFANN_ERR_INVALID, "posting_scan: RaBitQ arrays missing");
+        const uint32_t pd = codes->padded_dim;
+        if (pd == 0 || pd % 64 != 0 || pd > 4096)
+            return fail(GOFANN_ERR_UNSUPPORTED, "posting_scan: padded_dim %u unsupported", pd);
+        const size_t smem = base + pd;  // 8 planes of pd bits
+        const bool aligned = (reinterpret_cast<uintptr_t>(codes->rq_codes) & 15) == 0;
+        if (aligned && pd % 128 == 0) {
+            switch (pd / 128) {
+            case 1: return launch_scan<kScanRabitq, 1>(a, smem, false, s, "posting_scan_kernel(rq1)");
+            case 2: return launch_scan<kScanRabitq, 2>(a, smem, false, s, "posting_scan_kernel(rq2)");
+            case 4: return launch_scan<kScanRabitq, 4>(a, smem, false, s, "posting_scan_kernel(rq4)");
+            case 8: return launch_scan<kScanRabitq, 8>(a, smem, false, s, "posting_scan_kernel(rq8)");
+            case 16: return launch_scan<kScanRabitq, 16>(a, smem, false, s, "posting_scan_kernel(rq16)");
+            case 32: return launch_scan<kScanRabitq, 32>(a, smem, false, s, "posting_scan_kernel(rq32)");
+            default: break;
+            }
+        }
+        return launch_scan<kScanRabitq, 0>(a, smem, false, s, "posting_scan_kernel(rq)");
+    }
+    return fail(GOFANN_ERR_INVALID, "posting_scan: unknown scorer %d", scorer);
 }
 
 }  // extern "C"

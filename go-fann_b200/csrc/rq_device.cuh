@@ -1,11 +1,13 @@
 // rq_device.cuh — device-side 1-bit RaBitQ estimator.
 //
-// The integer inner product sum_{d: bit(d)} q8[d] is computed from 8 bit
-// planes of u = q8 + 127 (0..254):  ip = sum_b 2^b popc(code & plane_b)
-// - 127 popc(code).  Integer sums are exact, so this equals the reference's
-// dp4a nibble-mask form (backend_rabitq.cu:3070-3098) bit for bit, with one
-// popc per plane per 32 dimensions instead of 8 dp4a + 8 table loads.
-// Code bit layout: dimension d is bit 31-(d%32) of little-endian word d/32.
+// The integer inner product sum_{d: bit(d)} q8[d] is computed from the 8 bit
+// planes of the two's-complement query bytes, q8[d] = sum_{b<7} 2^b bit_b(d)
+// - 128 bit_7(d):  ip = sum_{b<7} 2^b popc(code & plane_b) - 128
+// popc(code & plane_7).  Integer sums are exact, so this equals the
+// reference's dp4a nibble-mask form (backend_rabitq.cu:3070-3098) bit for
+// bit, with one popc per plane per 32 dimensions instead of 8 dp4a + 8 table
+// loads.  Code bit layout: dimension d is bit 31-(d%32) of little-endian
+// word d/32.
 #pragma once
 
 #include "common.cuh"
@@ -23,7 +25,7 @@ __device__ __forceinline__ void rq_build_planes(const int8_t* __restrict__ q8, i
     for (int w = tid; w < words; w += nthreads) {
         uint32_t p[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         for (int k = 0; k < 32; ++k) {
-            const uint32_t u = static_cast<uint32_t>(static_cast<int>(q8[w * 32 + k]) + 127);
+            const uint32_t u = static_cast<uint8_t>(q8[w * 32 + k]);
 #pragma unroll
             for (int b = 0; b < 8; ++b) p[b] |= ((u >> b) & 1u) << (31 - k);
         }
@@ -32,12 +34,26 @@ __device__ __forceinline__ void rq_build_planes(const int8_t* __restrict__ q8, i
     }
 }
 
+// Inner product of one code word with the planes p[0..7] of its 32 dimensions.
+__device__ __forceinline__ int32_t rq_word_ip_planes(uint32_t code_w, uint32_t p0, uint32_t p1, uint32_t p2,
+                                                     uint32_t p3, uint32_t p4, uint32_t p5, uint32_t p6,
+                                                     uint32_t p7)
+{
+    int32_t acc = __popc(code_w & p0);
+    acc += __popc(code_w & p1) << 1;
+    acc += __popc(code_w & p2) << 2;
+    acc += __popc(code_w & p3) << 3;
+    acc += __popc(code_w & p4) << 4;
+    acc += __popc(code_w & p5) << 5;
+    acc += __popc(code_w & p6) << 6;
+    return acc - (__popc(code_w & p7) << 7);
+}
+
 __device__ __forceinline__ int32_t rq_word_ip(uint32_t code_w, const uint32_t* planes, int words, int w)
 {
-    int32_t acc = 0;
-#pragma unroll
-    for (int b = 0; b < 8; ++b) acc += __popc(code_w & planes[b * words + w]) << b;
-    return acc - 127 * __popc(code_w);
+    return rq_word_ip_planes(code_w, planes[w], planes[words + w], planes[2 * words + w], planes[3 * words + w],
+                             planes[4 * words + w], planes[5 * words + w], planes[6 * words + w],
+                             planes[7 * words + w]);
 }
 
 // Whole-code inner product by one thread (codes 16-byte aligned when

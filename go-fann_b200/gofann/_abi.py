@@ -228,7 +228,7 @@ def lib() -> C.CDLL:
         "gofann_beam_search_noalloc": [C.POINTER(Graph), C.POINTER(Attrs), C.POINTER(Codes), C.POINTER(Prepared),
                                        C.POINTER(Routes), C.POINTER(SearchParams), C.POINTER(SearchOut), sp],
         "gofann_posting_scan": [C.POINTER(Codes), C.POINTER(Prepared), C.POINTER(Attrs), C.POINTER(Routes),
-                                C.c_int, sp, sp, sp, I32, I32, sp, sp, sp],
+                                C.c_int, sp, sp, sp, I32, I32, I32, sp, sp, sp, sp],
         "gofann_rerank": [sp, C.c_int, U32, U32, sp, C.POINTER(Attrs), C.POINTER(Routes), sp, U32, I32, sp, sp,
                           sp],
         "gofann_route_merge": [sp, sp, U32, sp, sp, U32, I32, sp, sp, sp],

@@ -206,7 +206,8 @@ class Pipeline:
         A.check(self.L.gofann_posting_scan(C.byref(self.di.codes_s), C.byref(self.prep_s), C.byref(self.di.attrs_s),
                                            C.byref(self.dp.post_s), A.SCORER_PQ, A.ptr(self.di.posting_ids),
                                            A.ptr(self.dp.post_begin), A.ptr(self.dp.post_count),
-                                           self.cfg.lowfreq_shortlist, 1, A.ptr(self.p_ids), A.ptr(self.p_d), s),
+                                           self.cfg.lowfreq_shortlist, 1, self.cfg.pq_mode, A.ptr(self.p_ids),
+                                           A.ptr(self.p_d), A.ptr(self.status), s),
                 "gofann_posting_scan")
 
     def rerank(self, queries: torch.Tensor, stream=None):

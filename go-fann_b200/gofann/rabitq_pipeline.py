@@ -117,8 +117,9 @@ class RabitqPipeline:
             return
         A.check(self.L.gofann_posting_scan(C.byref(self.cs), C.byref(self.ps), C.byref(self.at), C.byref(self.prs),
                                            A.SCORER_RABITQ, A.ptr(self.idx.posting_ids), A.ptr(self.p_begin),
-                                           A.ptr(self.p_count), self.shortlist, 1, A.ptr(self.p_ids), A.ptr(self.p_d),
-                                           stream_handle(stream)), "gofann_posting_scan")
+                                           A.ptr(self.p_count), self.shortlist, 1, A.PQ_LUT_GLOBAL, A.ptr(self.p_ids),
+                                           A.ptr(self.p_d), A.ptr(self.status), stream_handle(stream)),
+                "gofann_posting_scan")
 
     def rerank(self, queries: torch.Tensor, stream=None):
         s = stream_handle(stream)

@@ -370,12 +370,20 @@ GOFANN_API int gofann_beam_search_noalloc(const gofann_graph* graph, const gofan
 /* Brute-force scan of each route's posting slice [begin, begin+count) of
  * posting_ids, DNF filter (before scoring, or after a can-enter test when
  * score_first), top-shortlist_k by (dist, id) (backend_pq.cu:2046-2134). PQ
- * distances are sequential sums over subspaces (backend_pq.cu:2101-2104). */
+ * distances are sequential sums over subspaces (backend_pq.cu:2101-2104),
+ * read from prep->pq_lut or from a table built per route from pq_query and
+ * pq_centroids.  pq_mode GOFANN_PQ_U8 (u8 pq_query, 4-wide subvectors,
+ * pq_dim a multiple of 16, dim <= 256) scores against the integer codebook
+ * instead -- the same bits with no per-route table; a codebook value that
+ * is not an integer in 0..255 sets *status (when non-NULL) to
+ * GOFANN_ERR_INVALID and leaves every shortlist empty.  Any other pq_mode
+ * uses the tables. */
 GOFANN_API int gofann_posting_scan(const gofann_codes* codes, const gofann_prepared* prep,
                         const gofann_attrs* attrs, const gofann_routes* routes, int scorer,
                         const uint32_t* posting_ids, const uint64_t* route_begin,
                         const uint32_t* route_count, int32_t shortlist_k, int32_t score_first,
-                        uint32_t* out_ids, float* out_dists, void* stream);
+                        int32_t pq_mode, uint32_t* out_ids, float* out_dists, int32_t* status,
+                        void* stream);
 
 /* ---------------------------------------------------------- exact rerank */
 /* Exact L2 of each candidate against its query row, residual label check

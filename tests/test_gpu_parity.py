@@ -515,15 +515,19 @@ def test_beam_search_edge_cases(L):
 
 
 # ----------------------------------------------------------- postings
-def run_gpu_posting(L, codes, prep, attrs, routes, scorer, pids, begin, count, k):
+def run_gpu_posting(L, codes, prep, attrs, routes, scorer, pids, begin, count, k, pq_mode=A.PQ_LUT_GLOBAL,
+                    expect_status=0):
     dc, da, dr = dev_dict(codes), dev_dict(attrs), dev_dict(routes)
     cs, pp, at, rs = A.fill_codes(dc), A.fill_prepared(prep), A.fill_attrs(da), A.fill_routes(dr)
     n = rs.n_routes
     ids = torch.empty((n, k), dtype=torch.int32, device="cuda")
     d = torch.empty((n, k), dtype=torch.float32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
     A.check(L.gofann_posting_scan(C.byref(cs), C.byref(pp), C.byref(at), C.byref(rs), scorer, dptr((pids)),
-                                  dptr((begin)), dptr((count)), k, 1, A.ptr(ids), A.ptr(d), stream()), "posting")
+                                  dptr((begin)), dptr((count)), k, 1, pq_mode, A.ptr(ids), A.ptr(d), A.ptr(status),
+                                  stream()), "posting")
     torch.cuda.synchronize()
+    assert int(status.item()) == expect_status
     return host(ids, np.uint32), d.cpu().numpy()
 
 
@@ -550,9 +554,10 @@ def test_posting_scan_pq_bitexact(L, k, fused):
 @pytest.mark.parametrize("k,pq_dim", [(10, 48), (100, 48), (400, 48), (100, 24)])
 def test_posting_scan_pq_u8_codebook_bitexact(L, k, pq_dim):
     """The index's integer codebook with u8 queries and no prebuilt table (the
-    traversal's GOFANN_PQ_U8 inputs): the scan builds its table itself and
-    matches the oracle's float table + sequential float ADC bit for bit, for
-    4- and 8-byte subvectors, multi-chunk postings and an empty posting."""
+    traversal's GOFANN_PQ_U8 inputs).  4-byte subvectors run the PQ_U8 scorer
+    (persistent blocks, packed integer codebook), 8-byte ones the table the
+    scan builds itself; both match the oracle's float table + sequential
+    float ADC bit for bit, over multi-round postings and an empty posting."""
     from gofann.planner import concat_routes, subset_routes
     w, idx, plan = cfg2_small_u8cb(pq_dim)
     lut = O.pq_build_lut(w.queries.astype(np.float32), idx.pq_centroids, idx.pq_codes.shape[1])
@@ -563,10 +568,26 @@ def test_posting_scan_pq_u8_codebook_bitexact(L, k, pq_dim):
     count = np.concatenate([plan.posting_count, idx.posting_count[big], [0]]).astype(np.uint32)
     want = O.posting_scan(idx.codes(), {"pq_lut": lut}, idx.attrs(), routes, A.SCORER_PQ, idx.posting_ids, begin,
                           count, k)
+    mode = A.PQ_U8 if pq_dim == 48 else A.PQ_DIRECT
     got = run_gpu_posting(L, idx.codes(), pq_prep(w, idx, A.PQ_U8), idx.attrs(), routes, A.SCORER_PQ,
-                          idx.posting_ids, begin, count, k)
+                          idx.posting_ids, begin, count, k, pq_mode=mode)
     assert np.array_equal(got[0], want[0])
     assert np.array_equal(fbits(got[1]), fbits(want[1]))
+
+
+def test_posting_scan_pq_u8_rejects_fractional_codebook(L):
+    """A codebook value that is not an integer: the PQ_U8 scan sets the status
+    word and returns empty shortlists (no scoring on a wrong codebook)."""
+    w, idx, plan = cfg2_small_u8cb(48)
+    prep = pq_prep(w, idx, A.PQ_U8)
+    cent = prep["pq_centroids"].clone()
+    cent[3, 5] += 0.5
+    prep = dict(prep, pq_centroids=cent)
+    routes = plan.posting_routes
+    ids, d = run_gpu_posting(L, idx.codes(), prep, idx.attrs(), routes, A.SCORER_PQ, idx.posting_ids,
+                             plan.posting_begin, plan.posting_count, 10, pq_mode=A.PQ_U8,
+                             expect_status=A.ERR_INVALID)
+    assert np.all(ids == A.U32MAX) and np.all(d == np.float32(np.finfo(np.float32).max))
 
 
 @pytest.mark.parametrize("dim", [128, 4096])
@@ -579,6 +600,33 @@ def test_posting_scan_rabitq_bitexact(L, dim):
     want = O.posting_scan(rq, hprep, idx.attrs(), routes, A.SCORER_RABITQ, idx.posting_ids, begin, count, 100)
     got = run_gpu_posting(L, rq, dprep, idx.attrs(), routes, A.SCORER_RABITQ,
                           idx.posting_ids, begin, count, 100)
+    assert np.array_equal(got[0], want[0])
+    assert np.array_equal(fbits(got[1]), fbits(want[1]))
+
+
+@pytest.mark.parametrize("dim,k", [(128, 100), (160, 10), (480, 400), (992, 100)])
+def test_posting_scan_rabitq_long_slices(L, dim, k):
+    """Slices of a random order of the whole base (the attribute-order range
+    scans): thousands of candidates per route, so the running top-k merges
+    several times; lanes per candidate 1, none (padded_dim 192 is not a
+    multiple of 128), 4 and 8; UINT32_MAX padding and repeated ids inside the
+    slices; the planner's DNF predicates on half of the routes."""
+    w, idx, plan, rq, anchors, qr = rabitq_artifacts(n=6000, dim=dim, n_queries=48)
+    dprep, hprep = _rq_prepared(L, qr, anchors)
+    rng = np.random.default_rng(dim)
+    order = rng.permutation(w.n).astype(np.uint32)
+    order[rng.random(w.n) < 0.01] = A.U32MAX
+    order[100:110] = order[200:210]
+    routes = {kk: v.copy() for kk, v in plan.graph_routes.items()}
+    n = routes["query_row"].shape[0]
+    routes["pred_enabled"] = (np.arange(n) % 2).astype(np.uint8)
+    lo = rng.integers(0, w.n // 2, size=n)
+    cnt = rng.integers(1, w.n - lo).astype(np.uint32)
+    cnt[0], lo[0] = w.n, 0   # the whole order
+    cnt[1] = 0               # an empty slice
+    begin = lo.astype(np.uint64)
+    want = O.posting_scan(rq, hprep, idx.attrs(), routes, A.SCORER_RABITQ, order, begin, cnt, k)
+    got = run_gpu_posting(L, rq, dprep, idx.attrs(), routes, A.SCORER_RABITQ, order, begin, cnt, k)
     assert np.array_equal(got[0], want[0])
     assert np.array_equal(fbits(got[1]), fbits(want[1]))
 
