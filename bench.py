@@ -54,6 +54,9 @@ def parse():
                     help="PQ scoring: 0 table in global memory, 1 table in shared memory, 2 direct from the "
                          "codebook, 3 integer codebook (u8; the index builder rounds the codebook)")
     ap.add_argument("--resident-warps", type=int, default=0, help="cap on concurrent routes (0 = automatic)")
+    ap.add_argument("--shortlist", type=int, default=0,
+                    help="config 2: candidates each route reranks (traversal result width and posting shortlist); "
+                         "0 = 100 on one GPU, fewer per shard on several")
     ap.add_argument("--cpu-sample", type=int, default=0, help="queries in the CPU baseline sample (0 = auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
@@ -164,6 +167,53 @@ def beam_bytes(counters: np.ndarray, n_routes: int, degree: int, pq_dim: int, av
 
 
 # ------------------------------------------------------------ GPU arm
+def stage_times(pipe, queries, xchg, shard_base, steps, world, device):
+    """Mean device time of each stage of a config-2 step (CUDA events on the
+    launching stream around every stage, an untimed pass of `steps` steps;
+    every rank runs the same steps and collectives), max and min over ranks."""
+    import torch
+    import torch.distributed as dist
+    from gofann.engine import stream_handle
+    names = ["lut", "beam", "posting", "rerank", "route_merge"] + (["shard_exchange"] if world > 1 else [])
+    stream = torch.cuda.current_stream()
+    acc = np.zeros(len(names))
+    for _ in range(steps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+        ev[0].record(stream)
+        pipe.build_lut(queries)
+        ev[1].record(stream)
+        pipe.beam_search()
+        ev[2].record(stream)
+        pipe.posting_scan()
+        ev[3].record(stream)
+        pipe.rerank(queries)
+        ev[4].record(stream)
+        pipe.merge()
+        ev[5].record(stream)
+        if world > 1:
+            xchg.exchange(pipe.out_ids, pipe.out_d, shard_base, stream_handle())
+            ev[6].record(stream)
+        torch.cuda.synchronize()
+        acc += [ev[i].elapsed_time(ev[i + 1]) for i in range(len(names))]
+    t = torch.tensor(acc / steps, dtype=torch.float32, device=device)
+    allt = t.unsqueeze(0)
+    if world > 1:
+        allt = torch.zeros((world, len(names)), dtype=torch.float32, device=device)
+        dist.all_gather_into_tensor(allt, t)
+    a = allt.cpu().numpy()
+    return {"max": {n: round(float(v), 3) for n, v in zip(names, a.max(0))},
+            "min": {n: round(float(v), 3) for n, v in zip(names, a.min(0))}}
+
+
+def shard_shortlist(world: int) -> int:
+    """Candidates each route reranks on one shard.  The merged top-10 takes
+    about 10 / world results from each of `world` shards of an id-range
+    split, so a shard's shortlist can shrink with the shard count; the
+    queue-size sweep still has to reach the recall target on the merged
+    result."""
+    return 100 if world <= 1 else max(30, 100 // world * 2)
+
+
 def run_gofann(args):
     import torch
     import torch.distributed as dist
@@ -189,8 +239,11 @@ def run_gofann(args):
     nq = len(q.labels)
     k = 10
 
+    shortlist = args.shortlist or shard_shortlist(world)
+
     def make_pipe(qs):
-        cfg = SearchConfig(queue_size=qs, result_width=100, pq_mode=args.pq_mode, resident_warps=args.resident_warps)
+        cfg = SearchConfig(queue_size=qs, result_width=shortlist, lowfreq_shortlist=shortlist, pq_mode=args.pq_mode,
+                           resident_warps=args.resident_warps)
         return Pipeline(dindex, dplan, cfg)
 
     xchg = ShardExchange(world, nq, k, device) if world > 1 else None
@@ -259,10 +312,15 @@ def run_gofann(args):
     ms = start.elapsed_time(end) / args.steps
     beam_ms = float(np.mean([a.elapsed_time(b) for a, b in beam_ev]))
     t = torch.tensor([ms, beam_ms], device=device)
+    rank_ms = [ms]
     if world > 1:
+        g = torch.zeros(world, device=device)
+        dist.all_gather_into_tensor(g, torch.tensor([ms], device=device))
+        rank_ms = [round(float(x), 3) for x in g.cpu()]
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, beam_ms = float(t[0]), float(t[1])
     value = nq / (ms / 1e3)
+    stages = stage_times(pipe, q.vectors, xchg, shard_base, args.steps, world, device)
 
     # ---- end to end through host buffers (pinned), copies inside the timed region
     hq = q.vectors.cpu().pin_memory()
@@ -306,7 +364,7 @@ def run_gofann(args):
     cnt = pipe.g_counters[:dplan.n_graph].cpu().numpy().view(np.uint32).astype(np.int64)
     avg_labels = float(idx.label_indices.numel()) / max(1, idx.n)
     table_bytes = dindex.pq_dim * 256 * 4 if args.pq_mode in A.TABLE_MODES else idx.dim
-    bytes_launch = beam_bytes(cnt, dplan.n_graph, idx.degree, dindex.pq_dim, avg_labels, 100, table_bytes)
+    bytes_launch = beam_bytes(cnt, dplan.n_graph, idx.degree, dindex.pq_dim, avg_labels, shortlist, table_bytes)
     peaks = measured_peaks()
     achieved = bytes_launch / (beam_ms / 1e3) / 1e9
     # DRAM bytes per launch: the ncu capture of a small case of the same
@@ -324,14 +382,19 @@ def run_gofann(args):
             "vs_baseline": None, "dtype": "u8", "data": "synthetic",
             "config": {"workload": "config2: 10M x 192 u8, 200k-tag Zipf(1.1), AND of 1-2 tags, PQ 48x256, "
                                    "degree 64, exact u8 rerank", "n_base": args.n, "n_queries": nq,
-                       "queue_size": chosen, "recall_at_10": round(final_recall, 4), "recall_sweep": recalls,
+                       "queue_size": chosen, "shortlist": shortlist, "recall_at_10": round(final_recall, 4),
+                       "recall_sweep": recalls,
                        "graph_routes": dplan.n_graph, "posting_routes": dplan.n_post,
                        "graph_rows": idx.stats.get("graph_rows"), "label_graphs": idx.stats.get("groups"),
                        "pq_mode": PQ_MODE_NAMES.get(args.pq_mode, str(args.pq_mode)),
                        "l2_flush": "inputs larger than L2 (index ~25 GB resident, rows read at random)",
                        "planning": "route planning runs before the timed region, as the reference's query "
                                    "preparation does (validate_and_prepare_queries runs before qps_start)",
-                       "parallelism": f"shard{world}" if world > 1 else "single"},
+                       "parallelism": f"shard{world}" if world > 1 else "single",
+                       "stage_ms": stages["max"], "stage_ms_min_rank": stages["min"],
+                       "stage_timing": "CUDA events around each stage in an untimed pass of the same steps; "
+                                       "max and min over ranks",
+                       "rank_step_ms": rank_ms},
             "e2e": {"value": round(nq / (e_ms / 1e3), 1), "unit": "queries/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(nq * k * 8)},
             "gpu_launches": int(pipe.launches_per_run * args.steps + (2 * args.steps if world > 1 else 0)),

@@ -83,6 +83,23 @@ class SearchParams(C.Structure):
                 ("pq_mode", I32), ("resident_warps", I32)]
 
 
+class Index(C.Structure):
+    _fields_ = [("graph", Graph), ("attrs", Attrs), ("codes", Codes), ("pq_centroids", P), ("base", P),
+                ("base_dtype", I32), ("dim", U32), ("posting_ids", P), ("rq_rotation", P), ("rq_anchors", P),
+                ("rq_anchor_entry", P)]
+
+
+class Batch(C.Structure):
+    _fields_ = [("queries", P), ("n_queries", U32), ("reserved", U32), ("graph_routes", Routes),
+                ("posting_routes", Routes), ("posting_begin", P), ("posting_count", P),
+                ("query_route_offsets", P), ("query_routes", P)]
+
+
+class BatchParams(C.Structure):
+    _fields_ = [("search", SearchParams), ("posting_shortlist", I32), ("topk", I32), ("rq_entries", I32),
+                ("reserved", I32)]
+
+
 class SearchOut(C.Structure):
     _fields_ = [("ids", P), ("dists", P), ("steps", P), ("counters", P), ("status", P), ("trace", P),
                 ("trace_width", U32), ("reserved", U32)]
@@ -227,6 +244,11 @@ def lib() -> C.CDLL:
                                sp],
         "gofann_beam_search_noalloc": [C.POINTER(Graph), C.POINTER(Attrs), C.POINTER(Codes), C.POINTER(Prepared),
                                        C.POINTER(Routes), C.POINTER(SearchParams), C.POINTER(SearchOut), sp],
+        "gofann_search_batch_scratch_bytes": [C.POINTER(Index), C.POINTER(Batch), C.POINTER(BatchParams)],
+        "gofann_search_batch": [C.POINTER(Index), C.POINTER(Batch), C.POINTER(BatchParams), sp, C.c_size_t, sp, sp,
+                                sp, sp],
+        "gofann_predicate_pass_masks": [C.POINTER(Graph), C.POINTER(Attrs), C.POINTER(Routes), sp, sp, U32, sp, sp,
+                                        sp],
         "gofann_posting_scan": [C.POINTER(Codes), C.POINTER(Prepared), C.POINTER(Attrs), C.POINTER(Routes),
                                 C.c_int, sp, sp, sp, I32, I32, I32, sp, sp, sp, sp],
         "gofann_rerank": [sp, C.c_int, U32, U32, sp, C.POINTER(Attrs), C.POINTER(Routes), sp, U32, I32, sp, sp,
@@ -246,6 +268,7 @@ def lib() -> C.CDLL:
     L.gofann_rabitq_gemm_scratch_bytes.restype = C.c_size_t
     L.gofann_row_record_stride.argtypes = [U32]
     L.gofann_row_record_stride.restype = C.c_size_t
+    L.gofann_search_batch_scratch_bytes.restype = C.c_size_t
     _LIB = L
     return L
 
@@ -268,7 +291,8 @@ EXPORTED = ("gofann_abi_version", "gofann_last_error", "gofann_device_sm_count",
             "gofann_rabitq_centroid_dist_tc", "gofann_rabitq_encode", "gofann_rabitq_route_entries",
             "gofann_beam_search_scratch_bytes", "gofann_beam_search",
             "gofann_beam_search_noalloc",
-            "gofann_posting_scan", "gofann_rerank", "gofann_route_merge", "gofann_shard_merge",
+            "gofann_posting_scan", "gofann_predicate_pass_masks", "gofann_search_batch_scratch_bytes",
+            "gofann_search_batch", "gofann_rerank", "gofann_route_merge", "gofann_shard_merge",
             "gofann_row_record_stride", "gofann_build_row_records", "gofann_offset_ids")
 
 

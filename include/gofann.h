@@ -24,6 +24,11 @@
  *   gofann_beam_search        native_warp_independent_search_kernel_impl (device-resident)
  *                                                     src/search/pq/backend_pq.cu:3988-5199,
  *                             native_rabitq_search_kernel src/search/rabitq/backend_rabitq.cu:3496-4299
+ *   gofann_search_batch       execute_graph_batch + lowfreq scan + rerank + merge
+ *                                                     src/search/pq/backend_pq.cu:9740-10185, 10769,
+ *                                                     2479-2592, 13205-13226
+ *   gofann_predicate_pass_masks  prepare_candidate_pass_masks
+ *                                                     src/predicates/gpu_predicate_parallel.cuh:21-42
  *   gofann_posting_scan       lowfreq_pq_scan_kernel  src/search/pq/backend_pq.cu:2046-2185,
  *                             lowfreq_rabitq_scan_kernel src/search/rabitq/backend_rabitq.cu:5396-5751
  *   gofann_rerank             resident_pq_batch_exact_rerank_kernel src/search/pq/backend_pq.cu:5201-5310,
@@ -43,7 +48,7 @@
 extern "C" {
 #endif
 
-#define GOFANN_ABI_VERSION 2
+#define GOFANN_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define GOFANN_API __attribute__((visibility("default")))
@@ -384,6 +389,83 @@ GOFANN_API int gofann_posting_scan(const gofann_codes* codes, const gofann_prepa
                         const uint32_t* route_count, int32_t shortlist_k, int32_t score_first,
                         int32_t pq_mode, uint32_t* out_ids, float* out_dists, int32_t* status,
                         void* stream);
+
+/* ------------------------------------------------------- whole batches */
+/* Index-resident inputs of a batch (device pointers).  The PQ fields serve
+ * GOFANN_SCORER_PQ, the rq_ fields GOFANN_SCORER_RABITQ (codes.rq_* hold
+ * the 1-bit codes, factors and anchor ids). */
+typedef struct gofann_index {
+    gofann_graph graph;
+    gofann_attrs attrs;
+    gofann_codes codes;
+    const float* pq_centroids;     /* [256][dim]: pivots + mean (backend_pq.cu:1812-1815) */
+    const void* base;              /* rerank store [n_samples][dim] of base_dtype */
+    int32_t base_dtype;            /* GOFANN_DTYPE_* */
+    uint32_t dim;
+    const uint32_t* posting_ids;   /* label postings and attribute-order slices */
+    const float* rq_rotation;      /* [dim][padded_dim] */
+    const float* rq_anchors;       /* [num_anchors][padded_dim], rotated */
+    const uint32_t* rq_anchor_entry; /* [num_anchors] graph entry row of each anchor, or NULL */
+} gofann_index;
+
+/* One batch of routed queries (device pointers).  Route query_row values
+ * index the query rows; results of route r land in slot r of [graph routes ;
+ * posting routes], which query_route_offsets / query_routes group by query
+ * (route_to_original_query). */
+typedef struct gofann_batch {
+    const void* queries;            /* [n_queries][dim]: u8 for a u8 base, f32 otherwise */
+    uint32_t n_queries;
+    uint32_t reserved;
+    gofann_routes graph_routes;     /* traversal routes (n_routes may be 0) */
+    gofann_routes posting_routes;   /* posting-scan routes (n_routes may be 0) */
+    const uint64_t* posting_begin;  /* [posting n_routes] offsets into index posting_ids */
+    const uint32_t* posting_count;
+    const uint32_t* query_route_offsets; /* [n_queries+1] */
+    const uint32_t* query_routes;
+} gofann_batch;
+
+typedef struct gofann_batch_params {
+    gofann_search_params search;    /* traversal; search.result_width = traversal shortlist */
+    int32_t posting_shortlist;      /* 1..400 */
+    int32_t topk;                   /* results per query, 1..10 */
+    int32_t rq_entries;             /* RaBitQ: 1 = start each graph route at the entry row of its
+                                       query's nearest anchor (needs rq_anchor_entry) */
+    int32_t reserved;
+} gofann_batch_params;
+
+/* Device scratch gofann_search_batch needs for this batch shape. */
+GOFANN_API size_t gofann_search_batch_scratch_bytes(const gofann_index* index, const gofann_batch* batch,
+                                                    const gofann_batch_params* params);
+
+/* A whole batch on one stream with no allocation and no host
+ * synchronisation: query preparation (PQ: the lookup tables in the table
+ * modes; RaBitQ: rotation and centroid distances on the tensor cores,
+ * int8 quantisation, optional route entry points), the traversal of the
+ * graph routes, the posting scans, the exact rerank of both shortlist sets
+ * and the route -> query merge -- execute_graph_batch,
+ * run_lowfreq_pq_search_with_context, the high-frequency rerank and
+ * merge_route_results_to_original (backend_pq.cu:9740-10185, 10769,
+ * 2479-2592, 13205-13226; backend_rabitq.cu:13762-13776).  out_ids /
+ * out_dists: device [n_queries][topk]; status: device [1] error word or
+ * NULL.  Results equal the per-stage calls' bit for bit. */
+GOFANN_API int gofann_search_batch(const gofann_index* index, const gofann_batch* batch,
+                                   const gofann_batch_params* params, void* scratch, size_t scratch_bytes,
+                                   uint32_t* out_ids, float* out_dists, int32_t* status, void* stream);
+
+/* ------------------------------------------------- predicate bitmaps */
+/* Pass bits of candidate rows (prepare_candidate_pass_masks,
+ * src/predicates/gpu_predicate_parallel.cuh:21-42): bit i % 32 of
+ * out_masks[i / 32] is 1 when candidate i -- local row cand_rows[i] of the
+ * graph group of route cand_route[i], i.e. the sample
+ * row_to_sample[label_offset[group_id[route]] + row] -- matches the route's
+ * DNF predicate (gpu_predicate::matches), or when the route has no enabled
+ * predicate.  out_masks: device [ceil(n_candidates / 32)].  A route, group
+ * or row out of range gives a 0 bit and sets *status (when non-NULL) to
+ * GOFANN_ERR_INVALID. */
+GOFANN_API int gofann_predicate_pass_masks(const gofann_graph* graph, const gofann_attrs* attrs,
+                                           const gofann_routes* routes, const uint32_t* cand_route,
+                                           const uint32_t* cand_rows, uint32_t n_candidates,
+                                           uint32_t* out_masks, int32_t* status, void* stream);
 
 /* ---------------------------------------------------------- exact rerank */
 /* Exact L2 of each candidate against its query row, residual label check

@@ -77,6 +77,7 @@ def olib() -> C.CDLL:
         L.oracle_rabitq_encode_f32.argtypes = [sp, sp, U32, U32, sp, sp, sp]
         L.oracle_pickup_index.restype = C.c_int
         L.oracle_pred_matches.argtypes = [C.POINTER(A.Routes), C.POINTER(A.Attrs), U32, U32]
+        L.oracle_pred_enabled.argtypes = [C.POINTER(A.Routes), U32]
         L.oracle_labels_match.argtypes = [C.POINTER(A.Routes), C.POINTER(A.Attrs), U32, U32]
         for fn in ("oracle_beam_search", "oracle_posting_scan", "oracle_rerank", "oracle_route_merge",
                    "oracle_shard_merge", "oracle_filtered_topk"):
@@ -326,6 +327,26 @@ def pred_matches(routes: dict, attrs: dict, pair_route, pair_sample):
     L = olib()
     return np.array([L.oracle_pred_matches(C.byref(rs), C.byref(at), int(r), int(s))
                      for r, s in zip(pair_route, pair_sample)], np.uint8)
+
+
+def predicate_pass_masks(graph: dict, attrs: dict, routes: dict, cand_route, cand_rows) -> np.ndarray:
+    """Pass bitmap of candidate rows (prepare_candidate_pass_masks,
+    src/predicates/gpu_predicate_parallel.cuh:21-42): bit i % 32 of word i / 32
+    = candidate i (local row cand_rows[i] of route cand_route[i]'s graph
+    group) matches the route's DNF predicate, or the route has none enabled.
+    Loops in Python over oracle_pred_matches: small cases only."""
+    rs, at = A.fill_routes(routes), A.fill_attrs(attrs)
+    L = olib()
+    cand_route = np.asarray(cand_route, np.uint32)
+    cand_rows = np.asarray(cand_rows, np.uint32)
+    n = cand_route.shape[0]
+    bits = np.zeros(((n + 31) // 32) * 32, np.uint8)
+    off, r2s, grp = graph["label_offset"], graph["row_to_sample"], routes["group_id"]
+    for i, (r, row) in enumerate(zip(cand_route.tolist(), cand_rows.tolist())):
+        s = int(r2s[int(off[grp[r]]) + row])
+        bits[i] = L.oracle_pred_matches(C.byref(rs), C.byref(at), r, s) if L.oracle_pred_enabled(C.byref(rs), r) \
+            else 1
+    return np.packbits(bits.reshape(-1, 32)[:, ::-1], axis=1, bitorder="big").view(">u4").astype(np.uint32).ravel()
 
 
 def rabitq_encode_f32(residual, rotated_centroids, anchor_ids):

@@ -92,3 +92,79 @@ def host(t: torch.Tensor, dtype) -> np.ndarray:
 
 def fbits(x) -> np.ndarray:
     return np.ascontiguousarray(x, np.float32).view(np.uint32)
+
+
+def with_predicates(w, idx, routes: dict, seed=0, range_count=2):
+    """Range attributes, row filter masks and two predicate forms for the
+    routes of a small workload:
+      * dnf: 1-3 OR-ed clauses per route -- the route's residual labels, a
+        label of a random sample, float range atoms in modes 1-3 over two
+        dimensions (gpu_predicate_index.cuh:100-136, range_filter.cuh:28-77)
+        -- and a few routes with the predicate disabled;
+      * legacy: no DNF; per-route filter bits against per-row masks
+        (backend_pq.cu:4394-4397), per-route range modes 0-3 with bounds
+        (range_filter.cuh:47-98), a quarter of the routes marked compiled.
+    Returns (attrs, graph, dnf_routes, legacy_routes)."""
+    from gofann import _abi as A
+    rng = np.random.default_rng(seed)
+    attrs = dict(idx.attrs())
+    vals = rng.uniform(0.0, 1000.0, size=(w.n, range_count)).astype(np.float32)
+    vals[::97, 0] = 500.0  # exact bound hits
+    attrs["range_values"] = vals
+    graph = dict(idx.graph())
+    rows = graph["adjacency"].shape[0]
+    mask = np.zeros(rows, np.uint64)
+    for _ in range(8):
+        mask |= np.uint64(1) << rng.integers(0, 64, size=rows).astype(np.uint64)
+    graph["row_filter_mask"] = mask
+    n = routes["query_row"].shape[0]
+    ip, ind = attrs["label_indptr"], attrs["label_indices"]
+
+    def atom(dim):
+        mode = int(rng.integers(1, 4))
+        lo, hi = np.sort(rng.uniform(0, 1000, size=2)).astype(np.float32)
+        if rng.random() < 0.2:
+            lo = np.float32(500.0)
+        return (dim, mode, lo, hi)
+
+    offs, clauses, handles, ranges = [0], [], [], []
+    rip, rind = routes["qlabel_indptr"], routes["qlabel_indices"]
+    for r in range(n):
+        prim = routes["primary_label"][r]
+        for c in range(int(rng.integers(1, 4))):
+            lb, rb = len(handles), len(ranges)
+            if c == 0:
+                handles += [int(x) for x in rind[rip[r]:rip[r + 1]] if x != prim]
+            else:
+                s = int(rng.integers(0, w.n))
+                row = ind[ip[s]:ip[s + 1]]
+                if row.size and rng.random() < 0.7:
+                    handles.append(int(row[rng.integers(0, row.size)]))
+            for _ in range(int(rng.integers(0 if c == 0 else 1, 3))):
+                ranges.append(atom(int(rng.integers(0, range_count))))
+            clauses.append((lb, len(handles), rb, len(ranges)))
+        offs.append(len(clauses))
+    cl = np.zeros(len(clauses), A.CLAUSE_DTYPE)
+    for i, (a, b, c, d) in enumerate(clauses):
+        cl[i] = (a, b, c, d)
+    ra = np.zeros(max(1, len(ranges)), A.RANGE_ATOM_DTYPE)
+    for i, x in enumerate(ranges):
+        ra[i] = x
+    dnf = dict(routes)
+    dnf.update(pred_offsets=np.asarray(offs, np.uint32), clauses=cl,
+               pred_handles=np.asarray(handles if handles else [0], np.uint32), pred_ranges=ra,
+               pred_enabled=(rng.random(n) < 0.9).astype(np.uint8))
+    legacy = {k: v for k, v in routes.items()
+              if k not in ("pred_offsets", "clauses", "pred_handles", "pred_ranges", "pred_enabled")}
+    fb = np.zeros(n, np.uint64)
+    for _ in range(4):
+        fb |= np.uint64(1) << rng.integers(0, 64, size=n).astype(np.uint64)
+    fb[::11] = 0
+    fb[1::13] = np.uint64(0xFFFFFFFFFFFFFFFF)
+    legacy["filter_bits"] = fb
+    legacy["range_modes"] = rng.integers(0, 4, size=(n, range_count)).astype(np.uint8)
+    lo = rng.uniform(0, 400, size=(n, range_count)).astype(np.float32)
+    legacy["range_lower"] = lo
+    legacy["range_upper"] = (lo + rng.uniform(300, 900, size=(n, range_count))).astype(np.float32)
+    legacy["route_compiled"] = (rng.random(n) < 0.25).astype(np.uint8)
+    return attrs, graph, dnf, legacy

@@ -19,7 +19,7 @@ def test_library_exports_every_header_symbol():
     for name in declared:
         assert hasattr(lib, name), name
     assert set(declared) == set(A.EXPORTED)
-    assert lib.gofann_abi_version() == 2
+    assert lib.gofann_abi_version() == 3
 
 
 def test_nm_dynamic_symbols():
@@ -40,6 +40,10 @@ def test_struct_layouts_match_c():
 int main(void) {
   S(gofann_clause) S(gofann_range_atom) S(gofann_graph) S(gofann_attrs) S(gofann_codes)
   S(gofann_prepared) S(gofann_routes) S(gofann_search_params) S(gofann_search_out)
+  S(gofann_index) S(gofann_batch) S(gofann_batch_params)
+  O(gofann_index, pq_centroids) O(gofann_index, base_dtype) O(gofann_index, rq_anchor_entry)
+  O(gofann_batch, graph_routes) O(gofann_batch, posting_routes) O(gofann_batch, query_routes)
+  O(gofann_batch_params, posting_shortlist) O(gofann_batch_params, rq_entries)
   O(gofann_codes, rq_codes) O(gofann_codes, padded_dim) O(gofann_routes, query_row)
   O(gofann_routes, route_compiled) O(gofann_search_params, alpha) O(gofann_search_params, pq_mode) O(gofann_search_params, resident_warps) O(gofann_prepared, dim) O(gofann_prepared, pq_query)
   O(gofann_graph, total_rows) O(gofann_graph, records) O(gofann_graph, record_stride) O(gofann_attrs, n_samples) O(gofann_prepared, n_rows)
@@ -54,7 +58,8 @@ int main(void) {
     got = dict(ln.split() for ln in lines if ln)
     py = {"gofann_clause": A.Clause, "gofann_range_atom": A.RangeAtom, "gofann_graph": A.Graph,
           "gofann_attrs": A.Attrs, "gofann_codes": A.Codes, "gofann_prepared": A.Prepared,
-          "gofann_routes": A.Routes, "gofann_search_params": A.SearchParams, "gofann_search_out": A.SearchOut}
+          "gofann_routes": A.Routes, "gofann_search_params": A.SearchParams, "gofann_search_out": A.SearchOut,
+          "gofann_index": A.Index, "gofann_batch": A.Batch, "gofann_batch_params": A.BatchParams}
     for cname, st in py.items():
         assert int(got[cname]) == C.sizeof(st), cname
     for key, val in got.items():
