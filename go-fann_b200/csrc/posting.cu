@@ -147,6 +147,10 @@ __device__ __forceinline__ int32_t group_sum(int32_t v)
     }
 }
 
+struct ScanArgs;
+template <int kKind>
+__device__ __forceinline__ void prefetch_candidate(const ScanArgs& a, uint32_t s);
+
 struct ScanArgs {
     gofann_codes codes;
     gofann_prepared prep;
@@ -161,9 +165,33 @@ struct ScanArgs {
     int32_t* status;
 };
 
+// Fetches candidate s's code row (and RaBitQ factors and anchor id) into
+// L2 ahead of its scoring.
+template <int kKind>
+__device__ __forceinline__ void prefetch_candidate(const ScanArgs& a, uint32_t s)
+{
+    if (s == kU32Max) return;
+    if constexpr (kKind == kScanRabitq) {
+        const size_t cb = a.codes.padded_dim / 8;
+        const uint8_t* p = a.codes.rq_codes + static_cast<size_t>(s) * cb;
+        for (size_t o = 0; o < cb; o += 128) prefetch_l2(p + o);
+        prefetch_l2(a.codes.rq_factors + static_cast<size_t>(s) * 3);
+        prefetch_l2(a.codes.rq_anchor_ids + s);
+    } else {
+        const uint8_t* p = a.codes.pq_codes + static_cast<size_t>(s) * a.codes.pq_dim;
+        prefetch_l2(p);
+        prefetch_l2(p + a.codes.pq_dim - 1);
+    }
+}
+
+// Three blocks per SM for the register-plane RaBitQ scorer (its 32 plane
+// registers would otherwise leave two).
+template <int kKind, int kG>
+constexpr int scan_min_blocks() { return kKind == kScanRabitq && kG > 0 ? 3 : 1; }
+
 // kKind: ScanKind; kG: lanes per RaBitQ candidate (0 = one thread each).
 template <int kKind, int kG>
-__global__ void __launch_bounds__(kScanThreads) posting_scan_kernel(ScanArgs a)
+__global__ void __launch_bounds__(kScanThreads, scan_min_blocks<kKind, kG>()) posting_scan_kernel(ScanArgs a)
 {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __shared__ TopKState st;
@@ -171,7 +199,8 @@ __global__ void __launch_bounds__(kScanThreads) posting_scan_kernel(ScanArgs a)
     float* sd = reinterpret_cast<float*>(smem_raw);
     uint32_t* sid = reinterpret_cast<uint32_t*>(smem_raw + kSortSize * sizeof(float));
     uint32_t* wlist = sid + kSortSize;                                   // [kScanWarps][32]
-    unsigned char* area = reinterpret_cast<unsigned char*>(wlist + kScanWarps * kWarp);
+    int32_t* wipbuf = reinterpret_cast<int32_t*>(wlist + kScanWarps * kWarp);  // [kScanWarps][32]
+    unsigned char* area = reinterpret_cast<unsigned char*>(wipbuf + kScanWarps * kWarp);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int pq_dim = static_cast<int>(a.codes.pq_dim);
     const uint64_t stream_pol = l2_stream_policy();
@@ -259,6 +288,11 @@ __global__ void __launch_bounds__(kScanThreads) posting_scan_kernel(ScanArgs a)
             }
         }
 
+        // A warp scans positions warp*32 + 256 j (j = 0, 1, ...).  Without a
+        // predicate, the ids of its next batch are loaded while this batch is
+        // scored and their rows prefetched after it, one batch ahead.
+        uint32_t s_next = kU32Max;
+        bool have_next = false;
         for (uint32_t r0 = 0; r0 < count; r0 += kRoundCands) {
             const float thr_d = st.thr_d;
             const uint32_t thr_id = st.thr_id;
@@ -266,57 +300,64 @@ __global__ void __launch_bounds__(kScanThreads) posting_scan_kernel(ScanArgs a)
             for (int bt = 0; bt < kBatches; ++bt) {
                 const uint32_t pos0 = r0 + static_cast<uint32_t>((bt * kScanWarps + warp) * kWarp);
                 if (pos0 >= count) break;  // warp-uniform
-                const uint32_t s = scan_candidate(a.routes, a.attrs, route, pred_on, a.posting_ids, begin,
-                                                  pos0 + lane, count);
+                uint32_t s;
+                if (have_next) {
+                    s = s_next;
+                } else {
+                    s = scan_candidate(a.routes, a.attrs, route, pred_on, a.posting_ids, begin, pos0 + lane, count);
+                    prefetch_candidate<kKind>(a, s);
+                }
+                have_next = !pred_on;
+                if (have_next) {
+                    const uint32_t pn = pos0 + kScanWarps * kWarp + lane;
+                    s_next = pn < count ? __ldg(a.posting_ids + begin + pn) : kU32Max;
+                }
                 if constexpr (kKind == kScanRabitq && kG > 0) {
+                    // Each lane loads the factors and anchor of its own candidate;
+                    // the groups compute the inner products of the batch's live
+                    // candidates in order (lane 0 of a group stores them); then
+                    // every lane combines its own candidate's distance.
                     constexpr int kCpw = 32 / kG;                    // candidates per warp pass
                     constexpr int kU = kG >= 4 ? 4 : kG;             // passes unrolled
                     const unsigned live = __ballot_sync(kFull, s != kU32Max);
                     uint32_t* wl = wlist + warp * kWarp;
-                    if (s != kU32Max) wl[__popc(live & ((1u << lane) - 1u))] = s;
+                    int32_t* wip = wipbuf + warp * kWarp;
+                    const int my_pos = __popc(live & ((1u << lane) - 1u));
+                    float fa = 0.0f, fr = 0.0f;
+                    uint32_t an = 0u;
+                    if (s != kU32Max) {
+                        wl[my_pos] = s;
+                        fa = __ldg(a.codes.rq_factors + static_cast<size_t>(s) * 3);
+                        fr = __ldg(a.codes.rq_factors + static_cast<size_t>(s) * 3 + 1);
+                        an = __ldg(a.codes.rq_anchor_ids + s);
+                    }
                     __syncwarp();
                     const int n_live = __popc(live);
                     const int g = lane / kG;
                     const size_t code_bytes = a.codes.padded_dim / 8;
                     for (int j0 = 0; j0 < n_live; j0 += kCpw * kU) {
                         uint4 x[kU];
-                        uint32_t sc[kU];
-                        float fa[kU], fr[kU];
-                        uint32_t an[kU];
 #pragma unroll
                         for (int u = 0; u < kU; ++u) {
                             const int j = j0 + u * kCpw + g;
-                            sc[u] = j < n_live ? wl[j] : kU32Max;
                             x[u] = make_uint4(0u, 0u, 0u, 0u);
-                            fa[u] = fr[u] = 0.0f;
-                            an[u] = 0u;
-                            if (sc[u] != kU32Max) {
-                                x[u] = ld_stream_u32x4(a.codes.rq_codes + static_cast<size_t>(sc[u]) * code_bytes +
+                            if (j < n_live)
+                                x[u] = ld_stream_u32x4(a.codes.rq_codes + static_cast<size_t>(wl[j]) * code_bytes +
                                                            16 * slot,
                                                        stream_pol);
-                                if (slot == 0) {
-                                    fa[u] = __ldg(a.codes.rq_factors + static_cast<size_t>(sc[u]) * 3);
-                                    fr[u] = __ldg(a.codes.rq_factors + static_cast<size_t>(sc[u]) * 3 + 1);
-                                    an[u] = __ldg(a.codes.rq_anchor_ids + sc[u]);
-                                }
-                            }
                         }
 #pragma unroll
                         for (int u = 0; u < kU; ++u) {
-                            int32_t ip = rq_word_ip_planes(x[u].x, pl[0][0], pl[1][0], pl[2][0], pl[3][0], pl[4][0],
-                                                           pl[5][0], pl[6][0], pl[7][0]);
-                            ip += rq_word_ip_planes(x[u].y, pl[0][1], pl[1][1], pl[2][1], pl[3][1], pl[4][1],
-                                                    pl[5][1], pl[6][1], pl[7][1]);
-                            ip += rq_word_ip_planes(x[u].z, pl[0][2], pl[1][2], pl[2][2], pl[3][2], pl[4][2],
-                                                    pl[5][2], pl[6][2], pl[7][2]);
-                            ip += rq_word_ip_planes(x[u].w, pl[0][3], pl[1][3], pl[2][3], pl[3][3], pl[4][3],
-                                                    pl[5][3], pl[6][3], pl[7][3]);
-                            ip = group_sum<kG>(ip);
-                            if (slot == 0 && sc[u] != kU32Max) {
-                                const float d = rq_combine(ip, rq.scale, rq.k1, fa[u], fr[u], __ldg(rq.gdist + an[u]));
-                                topk_offer(t, st, thr_d, thr_id, d, sc[u]);
-                            }
+                            const uint32_t cw[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
+                            const int32_t ip = group_sum<kG>(rq_ip4_csa(cw, pl));
+                            const int j = j0 + u * kCpw + g;
+                            if (slot == 0 && j < n_live) wip[j] = ip;
                         }
+                    }
+                    __syncwarp();
+                    if (s != kU32Max) {
+                        const float d = rq_combine(wip[my_pos], rq.scale, rq.k1, fa, fr, __ldg(rq.gdist + an));
+                        topk_offer(t, st, thr_d, thr_id, d, s);
                     }
                     __syncwarp();  // wl is rewritten by the next batch
                 } else {
@@ -333,6 +374,7 @@ __global__ void __launch_bounds__(kScanThreads) posting_scan_kernel(ScanArgs a)
                         topk_offer(t, st, thr_d, thr_id, d, s);
                     }
                 }
+                if (have_next) prefetch_candidate<kKind>(a, s_next);
             }
             __syncthreads();
             const int n_buf = st.n_buf;
@@ -412,7 +454,7 @@ int gofann_posting_scan(const gofann_codes* codes, const gofann_prepared* prep, 
     a.out_ids = out_ids;
     a.out_d = out_dists;
     a.status = status;
-    const size_t base = static_cast<size_t>(kSortSize) * 8 + static_cast<size_t>(kScanWarps) * kWarp * 4;
+    const size_t base = static_cast<size_t>(kSortSize) * 8 + static_cast<size_t>(kScanWarps) * kWarp * 8;
     cudaStream_t s = as_stream(stream);
     if (scorer == GOFANN_SCORER_PQ) {
         if (!codes->pq_codes) return fail(GOFANN_ERR_INVALID, "posting_scan: PQ codes missing");

@@ -49,6 +49,65 @@ __device__ __forceinline__ int32_t rq_word_ip_planes(uint32_t code_w, uint32_t p
     return acc - (__popc(code_w & p7) << 7);
 }
 
+// Carry-save adders on 32 bit lanes: x + y + z = s + 2 c (full adder), x + y
+// = s + 2 c (half adder), every bit position independently.
+__device__ __forceinline__ void csa_full(uint32_t x, uint32_t y, uint32_t z, uint32_t& s, uint32_t& c)
+{
+    s = x ^ y ^ z;
+    c = (x & y) | (z & (x ^ y));
+}
+__device__ __forceinline__ void csa_half(uint32_t x, uint32_t y, uint32_t& s, uint32_t& c)
+{
+    s = x ^ y;
+    c = x & y;
+}
+
+// Inner product of 4 code words c[0..3] with their planes p[b][0..3]:
+// sum_{b<7} 2^b sum_j popc(c_j & p_bj) - 128 sum_j popc(c_j & p_7j).  The
+// 28 masked words of weights 1..64 are reduced column by column with
+// carry-save adders (a column's carries join the next column) to one word
+// per weight 1..256, and the 4 words of weight -128 to one word per weight
+// 128..512: 12 popc instead of 32 (popc issues at a quarter of the integer
+// logic rate).  Exact integer arithmetic: the same value as
+// rq_word_ip_planes summed over the 4 words.
+__device__ __forceinline__ int32_t rq_ip4_csa(const uint32_t (&c)[4], const uint32_t (&p)[8][4])
+{
+    uint32_t col[9];
+    uint32_t k0, k1, k2;  // carries into the current column
+    {   // weight 1: 4 words -> 1, carries 2
+        uint32_t s;
+        csa_full(c[0] & p[0][0], c[1] & p[0][1], c[2] & p[0][2], s, k0);
+        csa_half(s, c[3] & p[0][3], col[0], k1);
+    }
+    {   // weight 2: 4 words + 2 carries -> 1, carries 3
+        uint32_t s, s2, n0, n1, n2;
+        csa_full(k0, k1, c[0] & p[1][0], s, n0);
+        csa_full(c[1] & p[1][1], c[2] & p[1][2], c[3] & p[1][3], s2, n1);
+        csa_half(s, s2, col[1], n2);
+        k0 = n0; k1 = n1; k2 = n2;
+    }
+#pragma unroll
+    for (int b = 2; b < 7; ++b) {  // weights 4..64: 4 words + 3 carries -> 1, carries 3
+        uint32_t s, s2, n0, n1, n2;
+        csa_full(k0, k1, k2, s, n0);
+        csa_full(c[0] & p[b][0], c[1] & p[b][1], c[2] & p[b][2], s2, n1);
+        csa_full(s, s2, c[3] & p[b][3], col[b], n2);
+        k0 = n0; k1 = n1; k2 = n2;
+    }
+    csa_full(k0, k1, k2, col[7], col[8]);  // weights 128 and 256
+    uint32_t ng0, ng1, ng2;                // weight -128 words -> weights 128, 256, 512
+    {
+        uint32_t s, e0, e1;
+        csa_full(c[0] & p[7][0], c[1] & p[7][1], c[2] & p[7][2], s, e0);
+        csa_half(s, c[3] & p[7][3], ng0, e1);
+        csa_half(e0, e1, ng1, ng2);
+    }
+    int32_t acc = 0;
+#pragma unroll
+    for (int b = 0; b < 9; ++b) acc += __popc(col[b]) << b;
+    return acc - ((__popc(ng0) + (__popc(ng1) << 1) + (__popc(ng2) << 2)) << 7);
+}
+
 __device__ __forceinline__ int32_t rq_word_ip(uint32_t code_w, const uint32_t* planes, int words, int w)
 {
     return rq_word_ip_planes(code_w, planes[w], planes[words + w], planes[2 * words + w], planes[3 * words + w],
