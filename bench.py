@@ -54,6 +54,8 @@ def parse():
                     help="PQ scoring: 0 table in global memory, 1 table in shared memory, 2 direct from the "
                          "codebook, 3 integer codebook (u8; the index builder rounds the codebook)")
     ap.add_argument("--resident-warps", type=int, default=0, help="cap on concurrent routes (0 = automatic)")
+    ap.add_argument("--float-codebook", action="store_true",
+                    help="config 2: keep the trained float PQ codebook (needs --pq-mode 0, 1 or 2)")
     ap.add_argument("--shortlist", type=int, default=0,
                     help="config 2: candidates each route reranks (traversal result width and posting shortlist); "
                          "0 = 100 on one GPU, fewer per shard on several")
@@ -63,7 +65,7 @@ def parse():
     ap.add_argument("--range-scan-rows", type=int, default=30_000,
                     help="config 3: a range predicate of at most this many rows scans its slice, a wider one "
                          "traverses the graph")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3],
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3],
                     help="BASELINE configuration: 2 (10M x 192 u8, PQ; the default) or 3 (2.7M x 4096 f32, RaBitQ)")
     return ap.parse_args()
 
@@ -148,7 +150,7 @@ def build_workload(args, rank, world, device, t0):
     shard = data
     if world > 1:
         shard = S.shard_data(data, lo, hi, device)
-    idx = W.build_index(shard, seed=args.seed, t0=t0)
+    idx = W.build_index(shard, seed=args.seed, t0=t0, float_codebook=args.float_codebook)
     return data, idx, gt, eval_idx, lo
 
 
@@ -224,6 +226,8 @@ def run_gofann(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.float_codebook and args.pq_mode == A.PQ_U8:
+        raise SystemExit("--float-codebook needs a float PQ mode: --pq-mode 0 (table), 1 (shared table) or 2 (direct)")
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
@@ -387,6 +391,7 @@ def run_gofann(args):
                        "graph_routes": dplan.n_graph, "posting_routes": dplan.n_post,
                        "graph_rows": idx.stats.get("graph_rows"), "label_graphs": idx.stats.get("groups"),
                        "pq_mode": PQ_MODE_NAMES.get(args.pq_mode, str(args.pq_mode)),
+                       "codebook": "float (trained)" if args.float_codebook else "integer (trained, rounded)",
                        "l2_flush": "inputs larger than L2 (index ~25 GB resident, rows read at random)",
                        "planning": "route planning runs before the timed region, as the reference's query "
                                    "preparation does (validate_and_prepare_queries runs before qps_start)",
@@ -449,7 +454,6 @@ def cpu_search(hidx, plan, qv, sel, qs, threads):
     lut = O.pq_build_lut(qs_v.astype(np.float32), hidx["centroids"], hidx["codes"]["pq_codes"].shape[1])
     gr = subset_routes(plan.graph_routes, gsel)
     gr["query_row"] = pos[plan.graph_query[gsel]].astype(np.uint32)
-    gr["start_local"] = pipe.groutes["start_local"].cpu().numpy().view(np.uint32)[gsel]  # entries set on the device
     pr = subset_routes(plan.posting_routes, psel)
     pr["query_row"] = pos[plan.posting_query[psel]].astype(np.uint32)
     ids, bd, _, _ = O.beam_search(hidx["graph"], hidx["attrs"], hidx["codes"], {"pq_lut": lut}, gr, threads=threads,
@@ -642,6 +646,155 @@ def c3_bytes(pipe, idx, stage: str) -> float:
     return float(n_cand * (idx.dim * 4 + 4) + (pipe.ng + pipe.npo) * idx.dim * 4)
 
 
+def run_config1(args):
+    """100k x 128 f32 from a 64-centre mixture, one
+    label per vector from 100 (Zipf 1.0), 1k single-label queries, PQ 32x256
+    with float queries (per-query tables), per-label graphs of degree 32,
+    exact f32 rerank of 100.  The whole index fits in L2, so every timed step
+    is preceded by an L2 flush outside its events."""
+    import torch
+    from gofann import _abi as A, index_build, planner, synth
+    from gofann.engine import DeviceIndex, DevicePlan, Pipeline, SearchConfig
+    from oracle import oracle as O
+    from gofann import workload_gpu as W
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        raise SystemExit("config 1 runs on one GPU")
+    torch.cuda.set_device(0)
+    t0 = time.time()
+    n = args.n if args.n != 10_000_000 else 100_000
+    nq = args.queries if args.queries != 100_000 else 1_000
+    w = synth.config1(seed=args.seed, n=n, n_queries=nq)
+    idx = index_build.build_index(w, threshold=2000, degree=32, pq_dim=32, seed=args.seed, device="cuda")
+    plan = planner.plan_queries(idx, w.query_labels)
+    W._log(f"config 1 index: {idx.adjacency.shape[0]} graph rows, {len(idx.label_offset)} label graphs", t0)
+    # exact filtered ground truth (every query label; one label per vector)
+    from gofann.planner import _route_tables
+    labs = [np.asarray(x, np.uint32) for x in w.query_labels]
+    gt_routes = _route_tables(list(range(nq)), labs, [x[0] for x in labs], [0] * nq, [0] * nq)
+    gt_routes["pred_enabled"][:] = 0
+    gt, _ = O.filtered_topk(w.base, A.DTYPE_F32, w.queries, idx.attrs(), gt_routes, 10)
+    di, dp = DeviceIndex(idx, "cuda"), DevicePlan(plan, "cuda")
+    q = torch.from_numpy(w.queries).cuda()
+    mode = args.pq_mode if args.pq_mode != A.PQ_U8 else A.PQ_LUT_GLOBAL
+    sweep = [args.queue_size] if args.queue_size else QUEUE_SWEEP
+    recalls, chosen = {}, None
+    for qs in sweep:
+        pipe = Pipeline(di, dp, SearchConfig(queue_size=qs, result_width=100, pq_mode=mode))
+        ids, _ = pipe.run(q)
+        torch.cuda.synchronize()
+        recalls[qs] = round(W.recall_at_k(ids.cpu().numpy().view(np.uint32), gt, 10), 4)
+        W._log(f"queue {qs}: recall@10 {recalls[qs]}", t0)
+        if recalls[qs] >= args.recall:
+            chosen = qs
+            break
+    if chosen is None:
+        chosen = max(recalls, key=lambda x: recalls[x])
+        pipe = Pipeline(di, dp, SearchConfig(queue_size=chosen, result_width=100, pq_mode=mode))
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 126 MB L2
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    for _ in range(args.warmup):
+        pipe.run(q)
+    sampler = ClockSampler(0)
+    sampler.start()
+    steps, beam = [], []
+    for _ in range(args.steps):
+        flush.fill_(1)
+        e = [ev() for _ in range(4)]
+        e[0].record(stream)
+        pipe.build_lut(q)
+        e[1].record(stream)
+        pipe.beam_search()
+        e[2].record(stream)
+        pipe.posting_scan()
+        pipe.rerank(q)
+        pipe.merge()
+        e[3].record(stream)
+        steps.append((e[0], e[3]))
+        beam.append((e[1], e[2]))
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = float(np.mean([a.elapsed_time(b) for a, b in steps]))
+    beam_ms = float(np.mean([a.elapsed_time(b) for a, b in beam]))
+    # end to end: pinned queries + route tables in, top-10 out, per step
+    hq = q.cpu().pin_memory()
+    dev_tables = [v for v in dp.graph.values()] + [v for v in dp.post.values()] + \
+        [dp.post_begin, dp.post_count, dp.qoff, dp.qroutes]
+    host_tables = [v.cpu().pin_memory() for v in dev_tables]
+    hid = torch.empty((nq, 10), dtype=torch.int32).pin_memory()
+    hd = torch.empty((nq, 10), dtype=torch.float32).pin_memory()
+    dq = torch.empty_like(q)
+    e_ms = []
+    for _ in range(max(3, args.steps // 2)):
+        flush.fill_(2)
+        e0, e1 = ev(), ev()
+        torch.cuda.synchronize()
+        wall0 = time.perf_counter()
+        e0.record(stream)
+        dq.copy_(hq, non_blocking=True)
+        for tgt, src in zip(dev_tables, host_tables):
+            tgt.copy_(src, non_blocking=True)
+        ids, d = pipe.run(dq)
+        hid.copy_(ids, non_blocking=True)
+        hd.copy_(d, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms.append(max(e0.elapsed_time(e1), (time.perf_counter() - wall0) * 1e3))
+    h2d = hq.numel() * 4 + sum(v.numel() * v.element_size() for v in host_tables)
+    final = hid.numpy().view(np.uint32)
+    cnt = pipe.g_counters[:dp.n_graph].cpu().numpy().view(np.uint32).astype(np.int64)
+    avg_labels = float(idx.label_indices.shape[0]) / max(1, idx.label_indptr.shape[0] - 1)
+    table_bytes = 32 * 256 * 4 if mode in A.TABLE_MODES else w.dim * 4
+    bytes_launch = beam_bytes(cnt, dp.n_graph, idx.degree, 32, avg_labels, 100, table_bytes)
+    peaks = measured_peaks()
+    achieved = bytes_launch / (beam_ms / 1e3) / 1e9
+    line = {
+        "metric": "filtered QPS @ recall@10=0.95 (config 1)", "value": round(nq / (ms / 1e3), 1),
+        "unit": "queries/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"config1: {n} x 128 f32, 1 of 100 labels (Zipf 1.0), single-label queries, "
+                               f"PQ 32x256 float queries, degree 32, exact f32 rerank of 100", "n_base": n,
+                   "n_queries": nq, "queue_size": chosen, "recall_at_10": round(W.recall_at_k(final, gt, 10), 4),
+                   "recall_sweep": recalls, "graph_routes": dp.n_graph, "posting_routes": dp.n_post,
+                   "pq_mode": PQ_MODE_NAMES.get(mode, str(mode)),
+                   "l2_flush": "256 MB write before every timed step (outside its events)",
+                   "beam_ms": round(beam_ms, 4), "parallelism": "single"},
+        "e2e": {"value": round(nq / (float(np.mean(e_ms)) / 1e3), 1), "unit": "queries/s",
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(nq * 10 * 8)},
+        "gpu_launches": int(pipe.launches_per_run * args.steps),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None, "kernel": "beam_search_kernel",
+                     "kernel_ms": round(beam_ms, 4), "algorithmic_bytes_per_launch": int(bytes_launch),
+                     "peak_source": peaks["source"]},
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline:
+        lut = O.pq_build_lut(w.queries, idx.pq_centroids, 32)
+        threads = O.cpu_count()
+        cfgp = dict(queue_size=chosen, result_width=100, predicate_bias=1, alpha=0.15,
+                    early_stop_mode=A.EARLY_STOP_ADAPTIVE, finish_limit=100)
+        tt = time.perf_counter()
+        bi, _, _, _ = O.beam_search(idx.graph(), idx.attrs(), idx.codes(), {"pq_lut": lut}, plan.graph_routes,
+                                    threads=threads, **cfgp)
+        ri, rd = O.rerank(w.base, A.DTYPE_F32, w.queries, idx.attrs(), plan.graph_routes, bi, 10)
+        pi, _ = O.posting_scan(idx.codes(), {"pq_lut": lut}, idx.attrs(), plan.posting_routes, A.SCORER_PQ,
+                               idx.posting_ids, plan.posting_begin, plan.posting_count, 100)
+        rpi, rpd = O.rerank(w.base, A.DTYPE_F32, w.queries, idx.attrs(), plan.posting_routes, pi, 10)
+        qoff, order = plan.merge_tables()
+        ci, cd = O.route_merge(np.concatenate([ri, rpi]), np.concatenate([rd, rpd]), qoff, order, 10)
+        el = time.perf_counter() - tt
+        gd = hd.numpy()
+        valid = ci != U32MAX
+        line["cpu_baseline"] = {"value": round(nq / el, 1), "unit": "queries/s", "cores": threads, "kind": "port",
+                                "sample": f"all {nq} config-1 queries, queue {chosen}; LUT build in C, traversal "
+                                          f"on {threads} threads, posting scans, f32 rerank, merge; {el:.1f} s"}
+        line["parity"] = {"checked_queries": nq, "id_mismatches": int(np.any(final != ci, axis=1).sum()),
+                          "dist_rel_max": float(np.max(np.abs(gd[valid] - cd[valid]) /
+                                                       np.maximum(np.abs(cd[valid]), 1e-30))) if valid.any() else 0.0,
+                          "tolerance": "ids equal up to f32 rerank ties, distances within 1e-5 relative"}
+    print(json.dumps(line), flush=True)
+
+
 def run_config3(args):
     import torch
     from gofann import workload_rabitq as WR
@@ -790,7 +943,12 @@ def run_config3(args):
 
 def main():
     args = parse()
-    if args.config == 3:
+    if args.config == 1:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "config 1 reference arm not built; run --config 2"}))
+            return
+        run_config1(args)
+    elif args.config == 3:
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "config 3 reference arm not built; run --config 2"}))
             return

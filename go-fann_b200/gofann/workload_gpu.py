@@ -240,10 +240,13 @@ def merge_candidates(ids: torch.Tensor, dist: torch.Tensor, k: int) -> torch.Ten
 
 
 def build_index(data: dict, threshold=2000, degree=64, n_random=40, pq_dim=48, seed=0, t0=None,
-                torch_encode=False, passes=1, window=2048) -> GpuIndex:
+                torch_encode=False, passes=1, window=2048, float_codebook=False) -> GpuIndex:
     """passes > 1: each pass orders the label's members by coarse cluster and
     a different random projection; the window k-NN lists of all passes are
-    merged (nearest distinct ids), which widens every row's candidate pool."""
+    merged (nearest distinct ids), which widens every row's candidate pool.
+    float_codebook: keep the trained float centroids (the reference's
+    artefacts are float pivots + mean), which the table and direct PQ modes
+    score; by default they are rounded to integers for GOFANN_PQ_U8."""
     t0 = t0 or time.time()
     dev = data["base"].device
     base = data["base"]
@@ -253,7 +256,9 @@ def build_index(data: dict, threshold=2000, degree=64, n_random=40, pq_dim=48, s
     try:
         # codebook values rounded to integers in 0..255: with u8 queries every
         # table entry and ADC sum is then an exact integer (GOFANN_PQ_U8)
-        cent = train_pq_gpu(base, pq_dim, seed).round_().clamp_(0, 255)
+        cent = train_pq_gpu(base, pq_dim, seed)
+        if not float_codebook:
+            cent = cent.round_().clamp_(0, 255)
         codes = torch.empty((n, pq_dim), dtype=torch.uint8, device=dev)
         if torch_encode:
             w = dim // pq_dim
