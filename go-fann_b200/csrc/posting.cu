@@ -394,6 +394,57 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<kKind, kG>()) po
     }
 }
 
+// Merge of segment shortlists (merge_shortlists, src/search/common/
+// posting_segment_merge.cuh:13-61): route r's segments are rows
+// seg_indptr[r] .. seg_indptr[r+1] of the [segments][k] shortlists; the
+// reference inserts every entry into one k-slot shortlist heap, which keeps
+// the k smallest (dist, id) pairs of the union -- what the threshold filter
+// and the bitonic merges of TopK keep.
+__global__ void __launch_bounds__(kScanThreads) segment_merge_kernel(const uint32_t* __restrict__ seg_indptr,
+                                                                     uint32_t n_routes,
+                                                                     const uint32_t* __restrict__ seg_ids,
+                                                                     const float* __restrict__ seg_d, int k,
+                                                                     uint32_t* __restrict__ out_ids,
+                                                                     float* __restrict__ out_d)
+{
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ TopKState st;
+    float* sd = reinterpret_cast<float*>(smem_raw);
+    uint32_t* sid = reinterpret_cast<uint32_t*>(smem_raw + kSortSize * sizeof(float));
+    const int tid = threadIdx.x;
+    int keep = 32;
+    while (keep < k) keep <<= 1;
+    const TopK t{sd, sid, keep, k};
+    const int cap = kSortSize - keep;
+    for (uint32_t route = blockIdx.x; route < n_routes; route += gridDim.x) {
+        const uint64_t b = static_cast<uint64_t>(seg_indptr[route]) * k;
+        const uint64_t e = static_cast<uint64_t>(seg_indptr[route + 1]) * k;
+        topk_reset(t, st, tid);
+        for (uint64_t r0 = b; r0 < e; r0 += kRoundCands) {
+            const float thr_d = st.thr_d;
+            const uint32_t thr_id = st.thr_id;
+            for (int j = tid; j < kRoundCands; j += kScanThreads) {
+                const uint64_t i = r0 + j;
+                if (i < e) topk_offer(t, st, thr_d, thr_id, __ldg(seg_d + i), __ldg(seg_ids + i));
+            }
+            __syncthreads();
+            const int n_buf = st.n_buf;
+            __syncthreads();
+            if (n_buf > cap - kRoundCands) topk_merge(t, st, n_buf, tid);
+        }
+        {
+            const int n_buf = st.n_buf;
+            if (n_buf > 0) topk_merge(t, st, n_buf, tid);
+        }
+        for (int i = tid; i < k; i += kScanThreads) {
+            const uint32_t id = sid[i];
+            out_ids[static_cast<size_t>(route) * k + i] = id;
+            out_d[static_cast<size_t>(route) * k + i] = id == kU32Max ? FLT_MAX : sd[i];
+        }
+        __syncthreads();
+    }
+}
+
 template <int kKind, int kG>
 int launch_scan(const ScanArgs& a, size_t smem, bool persistent, cudaStream_t s, const char* what)
 {
@@ -504,6 +555,25 @@ int gofann_posting_scan(const gofann_codes* codes, const gofann_prepared* prep, 
         return launch_scan<kScanRabitq, 0>(a, smem, false, s, "posting_scan_kernel(rq)");
     }
     return fail(GOFANN_ERR_INVALID, "posting_scan: unknown scorer %d", scorer);
+}
+
+int gofann_segment_merge(const uint32_t* seg_indptr, uint32_t n_routes, const uint32_t* seg_ids,
+                         const float* seg_dists, int32_t shortlist_k, uint32_t* out_ids, float* out_dists,
+                         void* stream)
+{
+    if (!seg_indptr || !seg_ids || !seg_dists || !out_ids || !out_dists)
+        return fail(GOFANN_ERR_INVALID, "segment_merge: null argument");
+    if (shortlist_k < 1 || shortlist_k > GOFANN_MAX_SHORTLIST)
+        return fail(GOFANN_ERR_INVALID, "segment_merge: shortlist %d outside 1..%d", shortlist_k,
+                    GOFANN_MAX_SHORTLIST);
+    if (n_routes == 0) return GOFANN_OK;
+    const size_t smem = static_cast<size_t>(kSortSize) * 8;
+    const int sms = sm_count() > 0 ? sm_count() : 148;
+    const unsigned blocks = n_routes < static_cast<uint32_t>(sms) * 8 ? n_routes : static_cast<unsigned>(sms) * 8;
+    segment_merge_kernel<<<blocks, kScanThreads, smem, as_stream(stream)>>>(seg_indptr, n_routes, seg_ids, seg_dists,
+                                                                           shortlist_k, out_ids, out_dists);
+    GOFANN_CHECK_LAUNCH("segment_merge_kernel");
+    return GOFANN_OK;
 }
 
 }  // extern "C"

@@ -247,6 +247,7 @@ def lib() -> C.CDLL:
         "gofann_search_batch_scratch_bytes": [C.POINTER(Index), C.POINTER(Batch), C.POINTER(BatchParams)],
         "gofann_search_batch": [C.POINTER(Index), C.POINTER(Batch), C.POINTER(BatchParams), sp, C.c_size_t, sp, sp,
                                 sp, sp],
+        "gofann_segment_merge": [sp, U32, sp, sp, I32, sp, sp, sp],
         "gofann_predicate_pass_masks": [C.POINTER(Graph), C.POINTER(Attrs), C.POINTER(Routes), sp, sp, U32, sp, sp,
                                         sp],
         "gofann_posting_scan": [C.POINTER(Codes), C.POINTER(Prepared), C.POINTER(Attrs), C.POINTER(Routes),
@@ -291,7 +292,7 @@ EXPORTED = ("gofann_abi_version", "gofann_last_error", "gofann_device_sm_count",
             "gofann_rabitq_centroid_dist_tc", "gofann_rabitq_encode", "gofann_rabitq_route_entries",
             "gofann_beam_search_scratch_bytes", "gofann_beam_search",
             "gofann_beam_search_noalloc",
-            "gofann_posting_scan", "gofann_predicate_pass_masks", "gofann_search_batch_scratch_bytes",
+            "gofann_posting_scan", "gofann_segment_merge", "gofann_predicate_pass_masks", "gofann_search_batch_scratch_bytes",
             "gofann_search_batch", "gofann_rerank", "gofann_route_merge", "gofann_shard_merge",
             "gofann_row_record_stride", "gofann_build_row_records", "gofann_offset_ids")
 

@@ -24,6 +24,8 @@
  *   gofann_beam_search        native_warp_independent_search_kernel_impl (device-resident)
  *                                                     src/search/pq/backend_pq.cu:3988-5199,
  *                             native_rabitq_search_kernel src/search/rabitq/backend_rabitq.cu:3496-4299
+ *   gofann_segment_merge      posting_segments::merge_shortlists
+ *                                                     src/search/common/posting_segment_merge.cuh:13-61
  *   gofann_search_batch       execute_graph_batch + lowfreq scan + rerank + merge
  *                                                     src/search/pq/backend_pq.cu:9740-10185, 10769,
  *                                                     2479-2592, 13205-13226
@@ -451,6 +453,17 @@ GOFANN_API size_t gofann_search_batch_scratch_bytes(const gofann_index* index, c
 GOFANN_API int gofann_search_batch(const gofann_index* index, const gofann_batch* batch,
                                    const gofann_batch_params* params, void* scratch, size_t scratch_bytes,
                                    uint32_t* out_ids, float* out_dists, int32_t* status, void* stream);
+
+/* Merge of segment shortlists (merge_shortlists,
+ * src/search/common/posting_segment_merge.cuh:13-61): a long posting or range
+ * slice is scanned as several segments (one gofann_posting_scan route each,
+ * shortlists [segments][shortlist_k]); route r owns segments seg_indptr[r] ..
+ * seg_indptr[r+1] - 1 and gets the shortlist_k smallest (dist, id) pairs of
+ * their union -- the shortlist one scan of the whole slice gives.  out_*:
+ * device [n_routes][shortlist_k], UINT32_MAX / FLT_MAX fill. */
+GOFANN_API int gofann_segment_merge(const uint32_t* seg_indptr, uint32_t n_routes, const uint32_t* seg_ids,
+                                    const float* seg_dists, int32_t shortlist_k, uint32_t* out_ids,
+                                    float* out_dists, void* stream);
 
 /* ------------------------------------------------- predicate bitmaps */
 /* Pass bits of candidate rows (prepare_candidate_pass_masks,
