@@ -18,13 +18,14 @@ import numpy as np
 import torch
 
 from . import _abi as A
+from . import range_postings as RP
 from .engine import _t, stream_handle
 from .workload_rabitq import RqIndex, RqPlan
 
 
 class RabitqPipeline:
     def __init__(self, idx: RqIndex, plan: RqPlan, queue_size: int, shortlist: int = 200, topk: int = 10,
-                 alpha: float = 0.15, entries: bool = True):
+                 alpha: float = 0.15, entries: bool = True, segment_rows: int = 0):
         self.L = A.lib()
         d = idx.base.device
         self.idx, self.plan = idx, plan
@@ -43,6 +44,20 @@ class RabitqPipeline:
         self.proutes = {k: _t(v, d) for k, v in plan.posting_routes.items()}
         self.grs, self.prs = A.fill_routes(self.groutes), A.fill_routes(self.proutes)
         self.p_begin, self.p_count = _t(plan.posting_begin, d), _t(plan.posting_count, d)
+        # segmented scans (posting_segments::make_plan): slices longer than
+        # segment_rows are scanned as near-equal segments, one block each, and
+        # their shortlists merged per route
+        self.seg = None
+        if segment_rows and npo:
+            sp = RP.make_plan(np.arange(npo), plan.posting_begin, plan.posting_count, segment_rows)
+            sel = sp.query_positions.astype(np.int64)
+            seg_routes = {k: _t(np.ascontiguousarray(v[sel]), d) for k, v in plan.posting_routes.items()}
+            nseg = int(sel.shape[0])
+            self.seg = {"routes": seg_routes, "rs": A.fill_routes(seg_routes), "n": nseg,
+                        "begin": _t(sp.offsets, d), "count": _t(sp.sizes.astype(np.uint32), d),
+                        "indptr": _t(sp.query_indptr, d),
+                        "ids": torch.empty((nseg, shortlist), dtype=torch.int32, device=d),
+                        "d": torch.empty((nseg, shortlist), dtype=torch.float32, device=d)}
         r2q = np.concatenate([plan.graph_query, plan.posting_query]).astype(np.int64)
         order = np.argsort(r2q, kind="stable").astype(np.uint32)
         qoff = np.zeros(nq + 1, np.uint32)
@@ -80,7 +95,7 @@ class RabitqPipeline:
                                     alpha=alpha)
         self.out_s = A.SearchOut(ids=A.ptr(self.g_ids), dists=A.ptr(self.g_d), steps=A.ptr(self.g_steps),
                                  counters=A.ptr(self.g_counters), status=A.ptr(self.status))
-        self.launches_per_run = 2 * (1 if ng else 0) + 2 * (1 if npo else 0) + 1
+        self.launches_per_run = 2 * (1 if ng else 0) + 2 * (1 if npo else 0) + 1 + (1 if self.seg else 0)
 
     def prepare(self, queries: torch.Tensor, stream=None):
         """Rotation, int8 quantisation and centroid distances (the reference
@@ -114,6 +129,17 @@ class RabitqPipeline:
 
     def posting_scan(self, stream=None):
         if not self.npo:
+            return
+        if self.seg:
+            g = self.seg
+            A.check(self.L.gofann_posting_scan(C.byref(self.cs), C.byref(self.ps), C.byref(self.at), C.byref(g["rs"]),
+                                               A.SCORER_RABITQ, A.ptr(self.idx.posting_ids), A.ptr(g["begin"]),
+                                               A.ptr(g["count"]), self.shortlist, 1, A.PQ_LUT_GLOBAL, A.ptr(g["ids"]),
+                                               A.ptr(g["d"]), A.ptr(self.status), stream_handle(stream)),
+                    "gofann_posting_scan(segments)")
+            A.check(self.L.gofann_segment_merge(A.ptr(g["indptr"]), self.npo, A.ptr(g["ids"]), A.ptr(g["d"]),
+                                                self.shortlist, A.ptr(self.p_ids), A.ptr(self.p_d),
+                                                stream_handle(stream)), "gofann_segment_merge")
             return
         A.check(self.L.gofann_posting_scan(C.byref(self.cs), C.byref(self.ps), C.byref(self.at), C.byref(self.prs),
                                            A.SCORER_RABITQ, A.ptr(self.idx.posting_ids), A.ptr(self.p_begin),

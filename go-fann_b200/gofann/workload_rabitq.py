@@ -38,6 +38,8 @@ offline):
 from __future__ import annotations
 
 import ctypes as C
+import os
+import tempfile
 import time
 from dataclasses import dataclass, field
 
@@ -45,6 +47,7 @@ import numpy as np
 import torch
 
 from . import _abi as A
+from . import range_postings as RP
 
 SELECTIVITIES = (0.001, 0.01, 0.1, 0.5)
 RANGE_MAX = 1e9
@@ -89,7 +92,7 @@ class RqIndex:
     posting_begin: np.ndarray    # [vocab] u64 (membership)
     posting_count: np.ndarray    # [vocab] u32
     order_base: int              # offset of the attribute order in posting_ids
-    sorted_attr: np.ndarray      # [n] f32 attribute values in that order (host)
+    range_index: object          # the FARPIDX1 range postings (range_postings.Index)
     stats: dict = field(default_factory=dict)
 
 
@@ -285,15 +288,21 @@ def build_index(data: dict, degree=32, n_random=8, seed=0, t0=None, chunk=1 << 1
         _log(f"global graph {n} rows, degree {degree}", t0)
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
+    # ordered range postings: written as a FARPIDX1 file and loaded back the
+    # way the reference maps its ordered_postings.bin
     attr = data["attr"]
-    order_attr = torch.argsort(attr.squeeze(1))
+    rdir = tempfile.mkdtemp(prefix="gofann_rp_")
+    rpath = os.path.join(rdir, "ordered_postings.bin")
+    RP.write(rpath, attr.cpu().numpy())
+    rindex = RP.load(rpath)
+    order_attr = torch.from_numpy(rindex.dimensions[0].sample_ids.astype(np.int64)).to(dev)
     posting_ids = torch.cat([data["postings"], order_attr.to(torch.int32)])
+    _log(f"range postings {rpath}: {rindex.dimensions[0].unique_values.shape[0]} distinct values", t0)
     return RqIndex(n=n, dim=dim, padded_dim=p, base=base, attr=attr, set_indptr=data["set_indptr"],
                    set_indices=data["set_indices"], rotation=rot, anchors=ranchors, codes=codes, factors=factors,
                    anchor_ids=aid32, adjacency=adj, seed=seed_row, anchor_entry=anchor_entry, posting_ids=posting_ids,
                    posting_begin=data["begin"].astype(np.uint64), posting_count=data["card"].astype(np.uint32),
-                   order_base=int(data["postings"].numel()),
-                   sorted_attr=attr.squeeze(1)[order_attr].cpu().numpy(),
+                   order_base=int(data["postings"].numel()), range_index=rindex,
                    stats=dict(graph_rows=n, anchors=int(anchors.shape[0])))
 
 
@@ -328,14 +337,15 @@ def plan_queries(idx: RqIndex, q: RqQueries, range_scan_rows=30_000) -> RqPlan:
     """Membership -> posting scan; range -> slice scan of the attribute order
     when it holds at most range_scan_rows rows, else graph traversal with the
     range as a DNF atom."""
-    lo = np.searchsorted(idx.sorted_attr, q.lower, side="left")
-    hi = np.searchsorted(idx.sorted_attr, q.upper, side="left")
+    nq = q.kind.shape[0]
+    modes = np.where(q.kind == 1, 3, 0).astype(np.uint8).reshape(nq, 1)
+    sl = RP.choose_smallest_slice(idx.range_index, modes, q.lower.reshape(nq, 1), q.upper.reshape(nq, 1))
     g_q, p_q, p_b, p_c = [], [], [], []
-    for i in range(q.kind.shape[0]):
+    for i in range(nq):
         if q.kind[i] == 0:
             p_q.append(i); p_b.append(int(idx.posting_begin[q.value[i]])); p_c.append(int(idx.posting_count[q.value[i]]))
-        elif hi[i] - lo[i] <= range_scan_rows:
-            p_q.append(i); p_b.append(idx.order_base + int(lo[i])); p_c.append(int(hi[i] - lo[i]))
+        elif sl.count[i] <= range_scan_rows:  # RP.eligible_for_scan
+            p_q.append(i); p_b.append(idx.order_base + int(sl.begin[i])); p_c.append(int(sl.count[i]))
         else:
             g_q.append(i)
     g_q = np.asarray(g_q, np.int64)
