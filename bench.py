@@ -68,6 +68,9 @@ def parse():
     ap.add_argument("--range-scan-rows", type=int, default=30_000,
                     help="config 3: a range predicate of at most this many rows scans its slice, a wider one "
                          "traverses the graph")
+    ap.add_argument("--mode", default="pq", choices=["pq", "exact"],
+                    help="config 2: PQ navigation + exact rerank (pq), or the Full-GPU exact-distance mode (exact: "
+                         "traversal and posting scans on the exact distances of the HBM-resident base vectors)")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3],
                     help="BASELINE configuration: 2 (10M x 192 u8, PQ; the default) or 3 (2.7M x 4096 f32, RaBitQ)")
     return ap.parse_args()
@@ -420,6 +423,231 @@ def run_gofann(args):
                        "beam_ids": pipe.g_ids[:dplan.n_graph].cpu().numpy().view(np.uint32),
                        "beam_d": pipe.g_d[:dplan.n_graph].cpu().numpy()}
             line["cpu_baseline"], line["parity"] = cpu_baseline(args, data, idx, plan, chosen, t0, gpu_res)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------ Full-GPU exact mode
+def exact_bytes(counters: np.ndarray, n_routes: int, degree: int, dim: int, topk: int) -> float:
+    """Algorithmic HBM bytes of one exact-traversal launch: per expansion the
+    adjacency row and the node's row -> sample entry; per distance
+    evaluation the candidate's row -> sample entry and its full base row; per
+    route its query row and top-k output."""
+    e, v = counters[:, 0].sum(), counters[:, 1].sum()
+    return float(e * (degree * 4 + 4) + v * (4 + dim) + n_routes * (dim + topk * 8))
+
+
+def cpu_exact_search(hidx, plan, qv, sel, qs, threads):
+    """The reference's Full-GPU path restated on host cores for the queries
+    `sel`: exact traversal of the graph routes, exact posting scans and the
+    route -> query merge (oracle/)."""
+    from gofann.planner import subset_routes
+    from oracle import oracle as O
+    from gofann import _abi as A
+    pos = np.full(qv.shape[0], -1, np.int64)
+    pos[sel] = np.arange(len(sel))
+    gsel = np.nonzero(pos[plan.graph_query] >= 0)[0]
+    psel = np.nonzero(pos[plan.posting_query] >= 0)[0]
+    qs_v = np.ascontiguousarray(qv[sel])
+    gr = subset_routes(plan.graph_routes, gsel)
+    gr["query_row"] = pos[plan.graph_query[gsel]].astype(np.uint32)
+    pr = subset_routes(plan.posting_routes, psel)
+    pr["query_row"] = pos[plan.posting_query[psel]].astype(np.uint32)
+    bi, bd, _ = O.exact_search(hidx["graph"], hidx["attrs"], hidx["base"], A.DTYPE_U8, qs_v, gr, threads=threads,
+                               queue_size=qs, result_width=10, early_stop_mode=A.EARLY_STOP_ADAPTIVE)
+    pi, pd = O.exact_posting_scan(hidx["base"], A.DTYPE_U8, qs_v, hidx["attrs"], pr, hidx["posting_ids"],
+                                  plan.posting_begin[psel], plan.posting_count[psel], 10)
+    r2q = np.concatenate([gr["query_row"], pr["query_row"]]).astype(np.int64)
+    order = np.argsort(r2q, kind="stable").astype(np.uint32)
+    qoff = np.zeros(len(sel) + 1, np.uint32)
+    qoff[1:] = np.cumsum(np.bincount(r2q, minlength=len(sel)))
+    fi, fd = O.route_merge(np.concatenate([bi, pi]), np.concatenate([bd, pd]), qoff, order, 10)
+    return {"gsel": gsel, "final_ids": fi, "final_d": fd}
+
+
+def run_exact_mode(args):
+    """Config 2 in the Full-GPU exact-distance mode (run_full_gpu_search,
+    src/search/full_gpu/backend_full_gpu.cu:5387): the same index, graphs,
+    routes and queries as the PQ mode, scored by exact u8 distances."""
+    import torch
+    import torch.distributed as dist
+    from gofann import _abi as A, planner, workload_gpu as W
+    from gofann.engine import DeviceIndex, DevicePlan, ExactPipeline, SearchConfig, stream_handle
+    from gofann.sharding import ShardExchange
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=600))
+    t0 = time.time()
+    data, idx, gt, eval_idx, shard_base = build_workload(args, rank, world, device, t0)
+    q = data["queries"]
+    plan = planner.plan_queries(idx, q.labels)
+    dplan = DevicePlan(plan, device)
+    dindex = DeviceIndex(idx, device, row_records=False)
+    nq, k = len(q.labels), 10
+    xchg = ShardExchange(world, nq, k, device) if world > 1 else None
+
+    def make_pipe(qs):
+        return ExactPipeline(dindex, dplan, SearchConfig(queue_size=qs, resident_warps=args.resident_warps))
+
+    def step(pipe, queries):
+        ids, d = pipe.run(queries)
+        if world == 1:
+            return ids, d
+        return xchg.exchange(ids, d, shard_base, stream_handle())
+
+    sweep = [args.queue_size] if args.queue_size else QUEUE_SWEEP
+    chosen, recalls = None, {}
+    for qs in sweep:
+        pipe = make_pipe(qs)
+        ids, _ = step(pipe, q.vectors)
+        torch.cuda.synchronize()
+        r = None
+        if rank == 0:
+            pred = ids[torch.from_numpy(eval_idx).to(device)].cpu().numpy().view(np.uint32)
+            r = W.recall_at_k(pred, gt, k)
+        rr = torch.tensor([r if r is not None else 0.0], device=device)
+        if world > 1:
+            dist.broadcast(rr, 0)
+        recalls[qs] = round(float(rr.item()), 4)
+        W._log(f"exact mode, queue {qs}: recall@10 {recalls[qs]}", t0)
+        if recalls[qs] >= args.recall:
+            chosen = qs
+            break
+    if chosen is None:
+        chosen = max(recalls, key=lambda x: recalls[x])
+    pipe = make_pipe(chosen)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        step(pipe, q.vectors)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    beam_ev, post_ev = [], []
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start.record(stream)
+    for _ in range(args.steps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record(stream)
+        pipe.beam_search(q.vectors)
+        ev[1].record(stream)
+        pipe.posting_scan(q.vectors)
+        ev[2].record(stream)
+        pipe.merge()
+        if world > 1:
+            xchg.exchange(pipe.out_ids, pipe.out_d, shard_base, stream_handle())
+        beam_ev.append(ev)
+    end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = start.elapsed_time(end) / args.steps
+    beam_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in beam_ev]))
+    post_ms = float(np.mean([e[1].elapsed_time(e[2]) for e in beam_ev]))
+    t = torch.tensor([ms, beam_ms, post_ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, beam_ms, post_ms = (float(x) for x in t)
+    value = nq / (ms / 1e3)
+
+    # end to end: pinned query H2D, route tables H2D, top-10 D2H inside the timed region
+    hq = q.vectors.cpu().pin_memory()
+    hid = torch.empty((nq, k), dtype=torch.int32).pin_memory()
+    hd = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+    dev_tables = [v for v in dplan.graph.values()] + [v for v in dplan.post.values()] + \
+        [dplan.post_begin, dplan.post_count, dplan.qoff, dplan.qroutes]
+    host_tables = [v.cpu().pin_memory() for v in dev_tables]
+    h2d = hq.numel() + sum(v.numel() * v.element_size() for v in host_tables)
+    dq = torch.empty_like(q.vectors)
+    for _ in range(2):
+        dq.copy_(hq, non_blocking=True)
+        ids, d = step(pipe, dq)
+        hid.copy_(ids, non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_steps = max(3, args.steps // 2)
+    wall0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(e_steps):
+        dq.copy_(hq, non_blocking=True)
+        for tgt, src in zip(dev_tables, host_tables):
+            tgt.copy_(src, non_blocking=True)
+        ids, d = step(pipe, dq)
+        hid.copy_(ids, non_blocking=True)
+        hd.copy_(d, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = max(e0.elapsed_time(e1), (time.perf_counter() - wall0) * 1e3) / e_steps
+    te = torch.tensor([e_ms], device=device)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e_ms = float(te[0])
+
+    cnt = pipe.g_counters[:dplan.n_graph].cpu().numpy().view(np.uint32).astype(np.int64)
+    bytes_launch = exact_bytes(cnt, dplan.n_graph, idx.degree, idx.dim, k)
+    peaks = measured_peaks()
+    achieved = bytes_launch / (beam_ms / 1e3) / 1e9
+    if rank == 0:
+        final_pred = hid[torch.from_numpy(eval_idx)].numpy().view(np.uint32)
+        final_recall = W.recall_at_k(final_pred, gt, k)
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": {"workload": "config2 in the Full-GPU exact-distance mode: 10M x 192 u8, 200k-tag Zipf(1.1), "
+                                   "AND of 1-2 tags, degree 64, exact u8 distances in the traversal and posting "
+                                   "scans (no PQ, no rerank)", "mode": "exact", "n_base": args.n, "n_queries": nq,
+                       "queue_size": chosen, "recall_at_10": round(final_recall, 4), "recall_sweep": recalls,
+                       "graph_routes": dplan.n_graph, "posting_routes": dplan.n_post,
+                       "l2_flush": "inputs larger than L2 (base 1.9 GB + graphs 18.5 GB, rows read at random)",
+                       "planning": "route planning runs before the timed region",
+                       "parallelism": f"shard{world}" if world > 1 else "single",
+                       "stage_ms": {"exact_traversal": round(beam_ms, 3), "exact_posting": round(post_ms, 3)}},
+            "e2e": {"value": round(nq / (e_ms / 1e3), 1), "unit": "queries/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(nq * k * 8)},
+            "gpu_launches": int(pipe.launches_per_run * args.steps + (2 * args.steps if world > 1 else 0)),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                         "kernel": "exact_search_kernel", "kernel_ms": round(beam_ms, 3),
+                         "algorithmic_bytes_per_launch": int(bytes_launch), "peak_source": peaks["source"]},
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            from oracle import oracle as O
+            threads = O.cpu_count()
+            hidx = host_index(idx)
+            qv = q.vectors.cpu().numpy()
+            rng = np.random.default_rng(1)
+            sel = np.sort(rng.choice(nq, size=min(nq, args.cpu_sample or 2000), replace=False))
+            tt = time.perf_counter()
+            res = cpu_exact_search(hidx, plan, qv, sel, chosen, threads)
+            el = time.perf_counter() - tt
+            gi = pipe.out_ids.cpu().numpy().view(np.uint32)[sel]
+            gd = pipe.out_d.cpu().numpy()[sel]
+            line["cpu_baseline"] = {"value": round(len(sel) / el, 1), "unit": "queries/s", "cores": threads,
+                                    "kind": "port",
+                                    "sample": f"{len(sel)} of {nq} config-2 queries, queue {chosen}, exact traversal "
+                                              f"+ exact posting scans + merge, {el:.1f} s on {threads} threads"}
+            mism = int(np.any(gi != res["final_ids"], axis=1).sum())
+            dmism = int(np.any(gd.view(np.uint32) != res["final_d"].view(np.uint32), axis=1).sum())
+            line["parity"] = {"checked_queries": int(len(sel)), "id_mismatches": mism, "dist_bit_mismatches": dmism,
+                              "status": "green" if mism + dmism == 0 else "red",
+                              "oracle": "CPU restatement of the reference's Full-GPU path (oracle/)"}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -960,6 +1188,8 @@ def main():
         run_config3(args)
     elif args.impl == "reference":
         run_reference(args)
+    elif args.mode == "exact":
+        run_exact_mode(args)
     else:
         run_gofann(args)
 

@@ -31,6 +31,7 @@
 //    registers for the whole route, and the lanes' partial inner products
 //    are summed by a warp reduction.  Other padded dims score one candidate
 //    per thread against the planes in shared memory.
+#include "exact_device.cuh"
 #include "pq_device.cuh"
 #include "rq_device.cuh"
 
@@ -43,7 +44,13 @@ constexpr int kSortSize = 2048;      // running top-k + buffer, sorted together
 constexpr int kBatches = 4;          // 32-candidate batches per warp between buffer checks
 constexpr int kRoundCands = kScanWarps * kWarp * kBatches;
 
-enum ScanKind { kScanPqTable = 0, kScanPqU8 = 1, kScanRabitq = 2 };
+// kScanExact*: exact L2 of the full base rows (the Full-GPU backend's
+// low-frequency scan, full_gpu_lowfreq_kernel, backend_full_gpu.cu:
+// 2124-2260), one candidate per thread.
+enum ScanKind { kScanPqTable = 0, kScanPqU8 = 1, kScanRabitq = 2, kScanExactU8 = 3, kScanExactF32 = 4,
+                kScanExactF16 = 5 };
+template <int kKind>
+constexpr bool is_exact() { return kKind == kScanExactU8 || kKind == kScanExactF32 || kKind == kScanExactF16; }
 
 __device__ __forceinline__ void bitonic_sort_pairs(float* d, uint32_t* id, int n, int tid)
 {
@@ -163,6 +170,10 @@ struct ScanArgs {
     uint32_t* out_ids;
     float* out_d;
     int32_t* status;
+    const void* base;       // exact kinds: [n_samples][dim] rows
+    const void* queries;    // exact kinds: [rows][dim]
+    uint32_t dim;
+    uint32_t row_bytes;
 };
 
 // Fetches candidate s's code row (and RaBitQ factors and anchor id) into
@@ -171,7 +182,10 @@ template <int kKind>
 __device__ __forceinline__ void prefetch_candidate(const ScanArgs& a, uint32_t s)
 {
     if (s == kU32Max) return;
-    if constexpr (kKind == kScanRabitq) {
+    if constexpr (is_exact<kKind>()) {
+        const unsigned char* p = static_cast<const unsigned char*>(a.base) + static_cast<size_t>(s) * a.row_bytes;
+        for (uint32_t o = 0; o < a.row_bytes; o += 128) prefetch_l2(p + o);
+    } else if constexpr (kKind == kScanRabitq) {
         const size_t cb = a.codes.padded_dim / 8;
         const uint8_t* p = a.codes.rq_codes + static_cast<size_t>(s) * cb;
         for (size_t o = 0; o < cb; o += 128) prefetch_l2(p + o);
@@ -265,6 +279,11 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<kKind, kG>()) po
             const uint32_t* qr = reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(a.prep.pq_query) +
                                                                    static_cast<size_t>(row) * a.prep.dim);
             for (int i = tid; i < nw; i += kScanThreads) qw[i] = __ldg(qr + i);
+        } else if constexpr (is_exact<kKind>()) {
+            const uint4* src = reinterpret_cast<const uint4*>(static_cast<const unsigned char*>(a.queries) +
+                                                              static_cast<size_t>(row) * a.row_bytes);
+            for (uint32_t i = tid; i < a.row_bytes / 16; i += kScanThreads)
+                reinterpret_cast<uint4*>(area)[i] = __ldg(src + i);
         } else {
             rq_build_planes(a.prep.rq_q8 + static_cast<size_t>(row) * a.codes.padded_dim,
                             static_cast<int>(a.codes.padded_dim), reinterpret_cast<uint32_t*>(area), tid,
@@ -368,6 +387,14 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<kKind, kG>()) po
                         } else if constexpr (kKind == kScanPqU8) {
                             d = pq_adc_u8_chunked(qw, cbw, a.codes.pq_codes + static_cast<size_t>(s) * pq_dim, pq_dim,
                                                   stream_pol);
+                        } else if constexpr (kKind == kScanExactU8) {
+                            d = static_cast<float>(l2_u8_thread(
+                                static_cast<const uint8_t*>(a.base) + static_cast<size_t>(s) * a.row_bytes,
+                                reinterpret_cast<const uint4*>(area), static_cast<int>(a.row_bytes / 16), stream_pol));
+                        } else if constexpr (kKind == kScanExactF32 || kKind == kScanExactF16) {
+                            d = l2_float_thread<kKind == kScanExactF32 ? GOFANN_DTYPE_F32 : GOFANN_DTYPE_F16>(
+                                static_cast<const unsigned char*>(a.base) + static_cast<size_t>(s) * a.row_bytes, area,
+                                static_cast<int>(a.dim));
                         } else {
                             d = rq_estimate(a.codes, rq, s);
                         }
@@ -555,6 +582,56 @@ int gofann_posting_scan(const gofann_codes* codes, const gofann_prepared* prep, 
         return launch_scan<kScanRabitq, 0>(a, smem, false, s, "posting_scan_kernel(rq)");
     }
     return fail(GOFANN_ERR_INVALID, "posting_scan: unknown scorer %d", scorer);
+}
+
+int gofann_exact_posting_scan(const void* base, int dtype, uint32_t n_samples, uint32_t dim, const void* queries,
+                              const gofann_attrs* attrs, const gofann_routes* routes, const uint32_t* posting_ids,
+                              const uint64_t* route_begin, const uint32_t* route_count, int32_t k,
+                              uint32_t* out_ids, float* out_dists, void* stream)
+{
+    if (!base || !queries || !routes || !posting_ids || !route_begin || !route_count || !out_ids || !out_dists)
+        return fail(GOFANN_ERR_INVALID, "exact_posting_scan: null argument");
+    if (k < 1 || k > GOFANN_MAX_SHORTLIST)
+        return fail(GOFANN_ERR_INVALID, "exact_posting_scan: k %d outside 1..%d", k, GOFANN_MAX_SHORTLIST);
+    if (!routes->query_row) return fail(GOFANN_ERR_INVALID, "exact_posting_scan: routes.query_row missing");
+    if (routes->pred_offsets && (!attrs || !attrs->label_indptr || !routes->clauses || !routes->pred_handles))
+        return fail(GOFANN_ERR_INVALID, "exact_posting_scan: predicate arrays missing");
+    if (dtype != GOFANN_DTYPE_U8 && dtype != GOFANN_DTYPE_F32 && dtype != GOFANN_DTYPE_F16)
+        return fail(GOFANN_ERR_INVALID, "exact_posting_scan: unknown dtype %d", dtype);
+    const uint32_t elem = dtype == GOFANN_DTYPE_U8 ? 1u : (dtype == GOFANN_DTYPE_F16 ? 2u : 4u);
+    if (dim == 0 || (dim * elem) % 16 != 0 || dim * elem > 16384)
+        return fail(GOFANN_ERR_UNSUPPORTED, "exact_posting_scan: rows of %u x %u bytes (need a multiple of 16, "
+                                            "<= 16 KB)", dim, elem);
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (reinterpret_cast<uintptr_t>(queries) & 15) != 0)
+        return fail(GOFANN_ERR_INVALID, "exact_posting_scan: base and queries must be 16-byte aligned");
+    if (routes->n_routes == 0) return GOFANN_OK;
+    ScanArgs a{};
+    a.routes = *routes;
+    if (attrs) {
+        a.attrs.indptr = attrs->label_indptr;
+        a.attrs.indices = attrs->label_indices;
+        a.attrs.ranges = attrs->range_values;
+        a.attrs.n_samples = attrs->n_samples;
+        a.attrs.range_count = attrs->range_count;
+    } else {
+        a.attrs.n_samples = n_samples;
+    }
+    a.posting_ids = posting_ids;
+    a.route_begin = route_begin;
+    a.route_count = route_count;
+    a.k = k;
+    a.out_ids = out_ids;
+    a.out_d = out_dists;
+    a.base = base;
+    a.queries = queries;
+    a.dim = dim;
+    a.row_bytes = dim * elem;
+    const size_t smem = static_cast<size_t>(kSortSize) * 8 + static_cast<size_t>(kScanWarps) * kWarp * 8 + a.row_bytes;
+    cudaStream_t s = as_stream(stream);
+    if (dtype == GOFANN_DTYPE_U8) return launch_scan<kScanExactU8, 0>(a, smem, false, s, "posting_scan_kernel(exact u8)");
+    if (dtype == GOFANN_DTYPE_F16)
+        return launch_scan<kScanExactF16, 0>(a, smem, false, s, "posting_scan_kernel(exact f16)");
+    return launch_scan<kScanExactF32, 0>(a, smem, false, s, "posting_scan_kernel(exact f32)");
 }
 
 int gofann_segment_merge(const uint32_t* seg_indptr, uint32_t n_routes, const uint32_t* seg_ids,

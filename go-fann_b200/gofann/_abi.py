@@ -258,6 +258,10 @@ def lib() -> C.CDLL:
         "gofann_shard_merge": [sp, sp, U32, U32, I32, sp, sp, sp],
         "gofann_offset_ids": [sp, C.c_size_t, U32, sp],
         "gofann_build_row_records": [C.POINTER(Graph), C.POINTER(Attrs), C.POINTER(Codes), sp, sp, sp],
+        "gofann_exact_search": [C.POINTER(Graph), sp, C.POINTER(Attrs), sp, C.c_int, U32, sp, C.POINTER(Routes),
+                                C.POINTER(SearchParams), C.POINTER(SearchOut), sp, C.c_size_t, sp],
+        "gofann_exact_posting_scan": [sp, C.c_int, U32, U32, sp, C.POINTER(Attrs), C.POINTER(Routes), sp, sp, sp,
+                                      I32, sp, sp, sp],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -267,6 +271,8 @@ def lib() -> C.CDLL:
     L.gofann_beam_search_scratch_bytes.restype = C.c_size_t
     L.gofann_rabitq_gemm_scratch_bytes.argtypes = [U32, U32, U32, C.c_int]
     L.gofann_rabitq_gemm_scratch_bytes.restype = C.c_size_t
+    L.gofann_exact_search_scratch_bytes.argtypes = [U32]
+    L.gofann_exact_search_scratch_bytes.restype = C.c_size_t
     L.gofann_row_record_stride.argtypes = [U32]
     L.gofann_row_record_stride.restype = C.c_size_t
     L.gofann_search_batch_scratch_bytes.restype = C.c_size_t
@@ -294,7 +300,8 @@ EXPORTED = ("gofann_abi_version", "gofann_last_error", "gofann_device_sm_count",
             "gofann_beam_search_noalloc",
             "gofann_posting_scan", "gofann_segment_merge", "gofann_predicate_pass_masks", "gofann_search_batch_scratch_bytes",
             "gofann_search_batch", "gofann_rerank", "gofann_route_merge", "gofann_shard_merge",
-            "gofann_row_record_stride", "gofann_build_row_records", "gofann_offset_ids")
+            "gofann_row_record_stride", "gofann_build_row_records", "gofann_offset_ids",
+            "gofann_exact_search_scratch_bytes", "gofann_exact_search", "gofann_exact_posting_scan")
 
 
 def header_symbols(header: str | os.PathLike | None = None) -> list[str]:

@@ -242,5 +242,68 @@ class Pipeline:
         return self.out_ids, self.out_d
 
 
+class ExactPipeline:
+    """The Full-GPU exact-distance mode for one batch shape
+    (run_full_gpu_search, src/search/full_gpu/backend_full_gpu.cu:5387):
+    graph routes are traversed with exact distances of the HBM-resident base
+    vectors (gofann_exact_search), posting routes are scanned exactly
+    (gofann_exact_posting_scan), both emit their top-k directly, and the
+    routes are merged per query.  No codes, no tables, no rerank."""
+
+    def __init__(self, dindex: DeviceIndex, dplan: DevicePlan, cfg: SearchConfig):
+        self.L = A.lib()
+        self.di, self.dp, self.cfg = dindex, dplan, cfg
+        d = dindex.device
+        nq, ng, npo, k = dplan.n_queries, dplan.n_graph, dplan.n_post, cfg.topk
+        self.r_ids = torch.empty((ng + npo + 1, k), dtype=torch.int32, device=d)
+        self.r_d = torch.empty((ng + npo + 1, k), dtype=torch.float32, device=d)
+        self.g_steps = torch.empty(max(ng, 1), dtype=torch.int32, device=d)
+        self.g_counters = torch.zeros((max(ng, 1), 4), dtype=torch.int32, device=d)
+        self.out_ids = torch.empty((nq, k), dtype=torch.int32, device=d)
+        self.out_d = torch.empty((nq, k), dtype=torch.float32, device=d)
+        self.status = torch.zeros(1, dtype=torch.int32, device=d)
+        self.scratch_bytes = int(self.L.gofann_exact_search_scratch_bytes(max(ng, 1)))
+        self.scratch = torch.empty(self.scratch_bytes, dtype=torch.uint8, device=d)
+        self.params = A.fill_params(queue_size=cfg.queue_size, result_width=k, finish_limit=cfg.finish_limit,
+                                    early_stop_mode=cfg.early_stop_mode, max_steps=cfg.max_steps,
+                                    resident_warps=cfg.resident_warps)
+        self.out_s = A.SearchOut(ids=A.ptr(self.r_ids), dists=A.ptr(self.r_d), steps=A.ptr(self.g_steps),
+                                 counters=A.ptr(self.g_counters), status=A.ptr(self.status))
+        self.launches_per_run = (1 if ng else 0) + (1 if npo else 0) + 1
+
+    def beam_search(self, queries: torch.Tensor, stream=None):
+        if not self.dp.n_graph:
+            return
+        A.check(self.L.gofann_exact_search(C.byref(self.di.graph_s), None, C.byref(self.di.attrs_s),
+                                           A.ptr(self.di.base), DTYPES[self.di.dtype], self.di.dim, A.ptr(queries),
+                                           C.byref(self.dp.graph_s), C.byref(self.params), C.byref(self.out_s),
+                                           A.ptr(self.scratch), self.scratch_bytes, stream_handle(stream)),
+                "gofann_exact_search")
+
+    def posting_scan(self, queries: torch.Tensor, stream=None):
+        if not self.dp.n_post:
+            return
+        ng = self.dp.n_graph
+        A.check(self.L.gofann_exact_posting_scan(A.ptr(self.di.base), DTYPES[self.di.dtype], self.di.n, self.di.dim,
+                                                 A.ptr(queries), C.byref(self.di.attrs_s), C.byref(self.dp.post_s),
+                                                 A.ptr(self.di.posting_ids), A.ptr(self.dp.post_begin),
+                                                 A.ptr(self.dp.post_count), self.cfg.topk, A.ptr(self.r_ids[ng:]),
+                                                 A.ptr(self.r_d[ng:]), stream_handle(stream)),
+                "gofann_exact_posting_scan")
+
+    def merge(self, stream=None):
+        k = self.cfg.topk
+        A.check(self.L.gofann_route_merge(A.ptr(self.r_ids), A.ptr(self.r_d), k, A.ptr(self.dp.qoff),
+                                          A.ptr(self.dp.qroutes), self.dp.n_queries, k, A.ptr(self.out_ids),
+                                          A.ptr(self.out_d), stream_handle(stream)), "gofann_route_merge")
+
+    def run(self, queries: torch.Tensor, stream=None):
+        """Whole batch on device; returns (ids, dists) device tensors [Q][k]."""
+        self.beam_search(queries, stream)
+        self.posting_scan(queries, stream)
+        self.merge(stream)
+        return self.out_ids, self.out_d
+
+
 def to_numpy_ids(t: torch.Tensor) -> np.ndarray:
     return t.cpu().numpy().view(np.uint32)

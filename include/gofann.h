@@ -373,6 +373,44 @@ GOFANN_API int gofann_beam_search_noalloc(const gofann_graph* graph, const gofan
                                           const gofann_routes* routes, const gofann_search_params* params,
                                           const gofann_search_out* out, void* stream);
 
+/* ------------------------------------------------ Full-GPU exact mode */
+/* Bytes of device scratch gofann_exact_search needs for n_routes routes. */
+GOFANN_API size_t gofann_exact_search_scratch_bytes(uint32_t n_routes);
+
+/* Full-GPU exact-distance traversal (run_full_gpu_highfreq_route,
+ * src/search/full_gpu/backend_full_gpu.cu:1682-2043): the graph routes are
+ * searched with the exact L2 distance of the full base vectors (base device
+ * [n_samples][dim] of dtype u8 / f32 / f16, queries device [n_rows][dim] of
+ * the same dtype, both 16-byte aligned with rows a multiple of 16 bytes) --
+ * no codes and no rerank.  Per route the result is the top-k (k =
+ * params->result_width, 1..10) of the expanded nodes that pass the route's
+ * filter (filter_bits against graph->row_filter_mask, the residual labels
+ * qlabel_* except primary_label, and the range_modes atoms), as sample ids
+ * ascending by (distance, id); the search stops by the reference's
+ * finish-hit rule (params->early_stop_mode, finish_limit, max_steps).
+ * label_size: device [group_count] rows per graph group, or NULL to derive
+ * it from consecutive label_offset entries (the last group ends at
+ * total_rows).  out->counters, when set, receive per route [expanded
+ * nodes, distance evaluations, expanded nodes that passed the filter,
+ * frontier admissions]. */
+GOFANN_API int gofann_exact_search(const gofann_graph* graph, const uint32_t* label_size,
+                                   const gofann_attrs* attrs, const void* base, int dtype, uint32_t dim,
+                                   const void* queries, const gofann_routes* routes,
+                                   const gofann_search_params* params, const gofann_search_out* out,
+                                   void* scratch, size_t scratch_bytes, void* stream);
+
+/* Full-GPU exact posting scan (full_gpu_lowfreq_kernel,
+ * src/search/full_gpu/backend_full_gpu.cu:2124-2260): every member of each
+ * route's posting slice that passes the route's DNF predicate is scored by
+ * exact L2 (the same arithmetic as gofann_exact_search) and the k smallest
+ * (distance, id) pairs are kept (UINT32_MAX / FLT_MAX fill).  out_*: device
+ * [n_routes][k]. */
+GOFANN_API int gofann_exact_posting_scan(const void* base, int dtype, uint32_t n_samples, uint32_t dim,
+                                         const void* queries, const gofann_attrs* attrs,
+                                         const gofann_routes* routes, const uint32_t* posting_ids,
+                                         const uint64_t* route_begin, const uint32_t* route_count, int32_t k,
+                                         uint32_t* out_ids, float* out_dists, void* stream);
+
 /* ------------------------------------------------------- posting scans */
 /* Brute-force scan of each route's posting slice [begin, begin+count) of
  * posting_ids, DNF filter (before scoring, or after a can-enter test when

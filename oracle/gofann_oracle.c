@@ -1246,3 +1246,294 @@ void oracle_seq_hash(const uint32_t* values, int n, uint32_t* table, int32_t* ou
     for (int i = 0; i < HASH_CAP; ++i) table[i] = U32MAX;
     for (int i = 0; i < n; ++i) outcome[i] = oracle_hash_add(table, values[i]);
 }
+
+/* ------------------------------------------------- Full-GPU exact mode */
+/* l2_distance_device, backend_full_gpu.cu:1106-1190: u8 as the integer
+ * |x|^2 + |q|^2 - 2 x.q of dp4a (the sum of squared differences) converted
+ * to float; f32 lane partials over d = l, l+32, ... (`partial += diff *
+ * diff`, contracted to fma), then the shfl_down tree; f16 with an even dim
+ * over half2 pairs p = l, l+32, ...: partial + (dx*dx + dy*dy), the pair term
+ * contracted as fma(dx, dx, dy*dy).  Queries have the base's dtype. */
+float oracle_full_l2(const void* base, int dtype, uint32_t dim, uint32_t sample, const void* queries,
+                     uint32_t row)
+{
+    if (dtype == GOFANN_DTYPE_U8) {
+        const uint8_t* b = (const uint8_t*)base + (size_t)sample * dim;
+        const uint8_t* q = (const uint8_t*)queries + (size_t)row * dim;
+        uint32_t acc = 0;
+        for (uint32_t d = 0; d < dim; ++d) {
+            const int diff = (int)b[d] - (int)q[d];
+            acc += (uint32_t)(diff * diff);
+        }
+        return (float)acc;
+    }
+    float v[KW];
+    for (int l = 0; l < KW; ++l) v[l] = 0.0f;
+    if (dtype == GOFANN_DTYPE_F32) {
+        const float* b = (const float*)base + (size_t)sample * dim;
+        const float* q = (const float*)queries + (size_t)row * dim;
+        for (uint32_t d = 0; d < dim; ++d) {
+            const float diff = b[d] - q[d];
+            v[d % KW] = fmaf(diff, diff, v[d % KW]);
+        }
+    } else {
+        const uint16_t* b = (const uint16_t*)base + (size_t)sample * dim;
+        const uint16_t* q = (const uint16_t*)queries + (size_t)row * dim;
+        if ((dim & 1u) == 0) {
+            for (uint32_t p = 0; p < dim / 2; ++p) {
+                const float dx = f16_decode(b[2 * p]) - f16_decode(q[2 * p]);
+                const float dy = f16_decode(b[2 * p + 1]) - f16_decode(q[2 * p + 1]);
+                v[p % KW] = v[p % KW] + fmaf(dx, dx, dy * dy);
+            }
+        } else {
+            for (uint32_t d = 0; d < dim; ++d) {
+                const float diff = f16_decode(b[d]) - f16_decode(q[d]);
+                v[d % KW] = fmaf(diff, diff, v[d % KW]);
+            }
+        }
+    }
+    return oracle_warp_sum(v);
+}
+
+/* better_result / insert_best_result, backend_full_gpu.cu:1328-1375 */
+static int full_better(float ld, uint32_t li, float rd, uint32_t ri)
+{
+    return ld < rd || (ld == rd && li < ri);
+}
+static int full_insert_best(float dist, uint32_t id, int topk, float* bd, uint32_t* bi, int* size)
+{
+    int changed = 0;
+    for (int i = 0; i < *size; ++i) {
+        if (bi[i] == id) {
+            if (dist >= bd[i]) return 0;
+            for (int j = i; j + 1 < *size; ++j) { bd[j] = bd[j + 1]; bi[j] = bi[j + 1]; }
+            --*size;
+            changed = 1;
+            break;
+        }
+    }
+    if (*size == topk && !full_better(dist, id, bd[topk - 1], bi[topk - 1])) return changed;
+    int pos = *size;
+    if (*size < topk) ++*size; else pos = topk - 1;
+    while (pos > 0 && full_better(dist, id, bd[pos - 1], bi[pos - 1])) {
+        bd[pos] = bd[pos - 1];
+        bi[pos] = bi[pos - 1];
+        --pos;
+    }
+    bd[pos] = dist;
+    bi[pos] = id;
+    return 1;
+}
+
+/* candidate_passes_device, backend_full_gpu.cu:1015-1092, with the route's
+ * filter expressed by its descriptor: the filter bit against the row mask,
+ * the active range atoms, the residual labels. */
+static int full_passes(const gofann_graph* g, const gofann_attrs* a, const gofann_routes* r, uint32_t route,
+                       uint64_t qbit, uint32_t grow, uint32_t sample)
+{
+    const uint64_t mask = g->row_filter_mask ? g->row_filter_mask[grow] : ~0ull;
+    if (qbit == 0 || (mask & qbit) == 0) return 0;
+    const uint32_t active = count_active(r, route);
+    if (active != 0 && (!a->range_values || count_matching(r, a, route, sample) != active)) return 0;
+    return oracle_labels_match(r, a, route, sample);
+}
+
+/* pickup_next_unused_from_pool_block, backend_full_gpu.cu:1536-1596: the
+ * unused entry of smallest distance, the smallest index among equals. */
+static int full_pickup(fpair* f, int size, fpair* out)
+{
+    int best = -1;
+    for (int i = 1; i < size; ++i) {
+        if (f[i].second & POOL_USED) continue;
+        if (best < 0 || f[i].first < f[best].first) best = i;
+    }
+    if (best < 0) return 0;
+    *out = f[best];
+    f[best].second |= POOL_USED;
+    return 1;
+}
+
+typedef struct {
+    const gofann_graph* g; const uint32_t* label_size; const gofann_attrs* a; const void* base; int dtype;
+    uint32_t dim; const void* queries; const gofann_routes* r; const gofann_search_params* sp;
+    uint32_t* ids; float* d; int32_t* steps; uint32_t* trace; uint32_t trace_width;
+    uint32_t begin, end, stride;
+} full_job;
+
+/* One graph route of run_full_gpu_highfreq_route (backend_full_gpu.cu:
+ * 1682-2043). */
+static void full_search_one(const full_job* j, uint32_t route, uint32_t* hash, fpair* pool)
+{
+    const gofann_graph* g = j->g;
+    const gofann_attrs* a = j->a;
+    const gofann_routes* r = j->r;
+    const gofann_search_params* sp = j->sp;
+    const int QS = sp->queue_size, K = sp->result_width;
+    uint32_t* oid = j->ids + (size_t)route * K;
+    float* od = j->d + (size_t)route * K;
+    uint32_t* tr = j->trace ? j->trace + (size_t)route * j->trace_width : NULL;
+    float bd[GOFANN_MAX_TOPK];
+    uint32_t bi[GOFANN_MAX_TOPK];
+    int bsize = 0, steps = 0, expanded = 0, passed = 0, fh = 0;
+    for (int i = 0; i < K; ++i) { oid[i] = U32MAX; od[i] = FLT_MAX; }
+    if (tr) for (uint32_t i = 0; i < j->trace_width; ++i) tr[i] = U32MAX;
+    if (j->steps) j->steps[route] = 0;
+    const uint32_t grp = r->group_id[route];
+    if (grp >= g->group_count) return;
+    const uint32_t off = g->label_offset[grp];
+    uint32_t gsize = j->label_size ? j->label_size[grp]
+                                   : (grp + 1 < g->group_count ? g->label_offset[grp + 1] : g->total_rows) - off;
+    if (off > g->total_rows || gsize > g->total_rows - off) gsize = 0;
+    const uint32_t seed = r->start_local[route];
+    if (gsize == 0 || seed >= gsize) return;
+    const uint32_t qrow = r->query_row[route];
+    const uint64_t qbit = r->filter_bits ? r->filter_bits[route] : ~0ull;
+    const uint32_t seed_sample = g->row_to_sample[off + seed];
+    if (seed_sample >= a->n_samples) return;
+    for (int i = 0; i < HASH_CAP; ++i) hash[i] = U32MAX;
+    int hs = 1;
+    fpair e;
+    e.first = oracle_full_l2(j->base, j->dtype, j->dim, seed_sample, j->queries, qrow);
+    e.second = seed;
+    e.base = e.first;
+    oracle_smmh_insert(pool, &hs, e);
+    oracle_hash_add(hash, seed);
+    fpair now, next;
+    if (!full_pickup(pool, hs, &now)) return;
+    int first_step = 1;
+    const int cap = sp->max_steps > 0 ? sp->max_steps : (1 << 22);
+    const uint32_t deg = g->degree < GOFANN_MAX_DEGREE ? g->degree : GOFANN_MAX_DEGREE;
+    uint32_t cand_local[GOFANN_MAX_DEGREE];
+    float cand_d[GOFANN_MAX_DEGREE];
+    for (;;) {
+        if (steps >= cap) break;
+        const uint32_t now_local = now.second & ~POOL_USED;
+        const uint32_t now_row = off + now_local;
+        const uint32_t now_sample = g->row_to_sample[now_row];
+        int improved = 0;
+        if (tr && (uint32_t)expanded < j->trace_width) tr[expanded] = now_local;
+        ++expanded;
+        if (now_sample < a->n_samples && full_passes(g, a, r, route, qbit, now_row, now_sample)) {
+            ++passed;
+            improved = full_insert_best(now.first, now_sample, K, bd, bi, &bsize);
+        }
+        ++steps;
+        /* every edge tested against the table before any insertion */
+        for (uint32_t ed = 0; ed < deg; ++ed) {
+            cand_local[ed] = U32MAX;
+            const uint32_t local = g->adjacency[(size_t)now_row * g->degree + ed];
+            if (local == U32MAX || local >= gsize || oracle_hash_test(hash, local)) continue;
+            const uint32_t s = g->row_to_sample[off + local];
+            if (s >= a->n_samples) continue;
+            cand_local[ed] = local;
+            cand_d[ed] = oracle_full_l2(j->base, j->dtype, j->dim, s, j->queries, qrow);
+        }
+        for (uint32_t ed = 0; ed < deg; ++ed) {
+            if (cand_local[ed] == U32MAX) continue;
+            if (hs > 2 && hs >= QS + 1 && pool[2].first < cand_d[ed]) continue;
+            fpair kp;
+            kp.first = cand_d[ed];
+            kp.second = cand_local[ed];
+            kp.base = kp.first;
+            oracle_smmh_insert(pool, &hs, kp);
+            oracle_hash_add(hash, cand_local[ed]);
+            if (hs >= QS + 2) oracle_smmh_pop_max(pool, &hs);
+        }
+        if (!full_pickup(pool, hs, &next)) break;
+        if (!first_step) {
+            const uint32_t next_sample = g->row_to_sample[off + (next.second & ~POOL_USED)];
+            if (sp->early_stop_mode == GOFANN_EARLY_STOP_ADAPTIVE && improved) {
+                fh = 0;
+            } else if (bsize == K && !full_better(next.first, next_sample, bd[K - 1], bi[K - 1])) {
+                ++fh;
+                if (early_stop(sp->early_stop_mode, fh, sp->finish_limit, QS, expanded, passed, K)) break;
+            } else {
+                fh = 0;
+            }
+        }
+        now = next;
+        first_step = 0;
+    }
+    for (int i = 0; i < bsize; ++i) { oid[i] = bi[i]; od[i] = bd[i]; }
+    if (j->steps) j->steps[route] = steps;
+}
+
+static void* full_worker(void* arg)
+{
+    full_job* j = (full_job*)arg;
+    uint32_t* hash = (uint32_t*)malloc(HASH_CAP * sizeof(uint32_t));
+    fpair* pool = (fpair*)malloc((size_t)(j->sp->queue_size + 3) * sizeof(fpair));
+    for (uint32_t route = j->begin; route < j->end; route += j->stride) full_search_one(j, route, hash, pool);
+    free(hash);
+    free(pool);
+    return NULL;
+}
+
+int oracle_exact_search(const gofann_graph* g, const uint32_t* label_size, const gofann_attrs* a,
+                        const void* base, int dtype, uint32_t dim, const void* queries, const gofann_routes* r,
+                        const gofann_search_params* sp, uint32_t* ids, float* d, int32_t* steps,
+                        uint32_t* trace, uint32_t trace_width, int threads)
+{
+    if (sp->queue_size < 2 || sp->queue_size > GOFANN_MAX_QUEUE || sp->result_width < 1 ||
+        sp->result_width > GOFANN_MAX_TOPK)
+        return GOFANN_ERR_INVALID;
+    if (threads < 1) threads = 1;
+    pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)threads);
+    full_job* jobs = (full_job*)malloc(sizeof(full_job) * (size_t)threads);
+    for (int t = 0; t < threads; ++t) {
+        full_job jb = {g, label_size, a, base, dtype, dim, queries, r, sp, ids, d, steps, trace, trace_width,
+                       (uint32_t)t, r->n_routes, (uint32_t)threads};
+        jobs[t] = jb;
+        if (threads == 1) full_worker(&jobs[t]);
+        else pthread_create(&th[t], NULL, full_worker, &jobs[t]);
+    }
+    if (threads > 1)
+        for (int t = 0; t < threads; ++t) pthread_join(th[t], NULL);
+    free(th);
+    free(jobs);
+    return GOFANN_OK;
+}
+
+/* full_gpu_lowfreq_kernel, backend_full_gpu.cu:2124-2260: every posting
+ * member passing the route's filter (here its DNF predicate) is scored
+ * exactly and inserted into the sorted top-k. */
+int oracle_exact_posting_scan(const void* base, int dtype, uint32_t dim, const void* queries,
+                              const gofann_attrs* a, const gofann_routes* r, const uint32_t* posting_ids,
+                              const uint64_t* route_begin, const uint32_t* route_count, int k,
+                              uint32_t* out_ids, float* out_d)
+{
+    if (k < 1 || k > GOFANN_MAX_SHORTLIST) return GOFANN_ERR_INVALID;
+    float* bd = (float*)malloc(sizeof(float) * (size_t)k);
+    uint32_t* bi = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)k);
+    for (uint32_t route = 0; route < r->n_routes; ++route) {
+        int size = 0;
+        const uint32_t row = r->query_row[route];
+        const int pred_on = oracle_pred_enabled(r, route);
+        for (uint32_t i = 0; i < route_count[route]; ++i) {
+            const uint32_t s = posting_ids[route_begin[route] + i];
+            if (s == U32MAX || s >= a->n_samples) continue;
+            if (pred_on && !oracle_pred_matches(r, a, route, s)) continue;
+            full_insert_best(oracle_full_l2(base, dtype, dim, s, queries, row), s, k, bd, bi, &size);
+        }
+        for (int i = 0; i < k; ++i) {
+            out_ids[(size_t)route * k + i] = i < size ? bi[i] : U32MAX;
+            out_d[(size_t)route * k + i] = i < size ? bd[i] : FLT_MAX;
+        }
+    }
+    free(bd);
+    free(bi);
+    return GOFANN_OK;
+}
+
+/* The entry full_pickup() takes from a frontier of `size` entries (index 0
+ * unused; vals carry the used bit), or -1; nothing is modified. */
+int oracle_full_pickup_index(const float* keys, const uint32_t* vals, int size)
+{
+    fpair* f = (fpair*)calloc((size_t)(size > 1 ? size : 1), sizeof(fpair));
+    for (int i = 0; i < size; ++i) { f[i].first = keys[i]; f[i].second = vals[i]; f[i].base = keys[i]; }
+    fpair out;
+    int idx = -1;
+    if (full_pickup(f, size, &out)) idx = (int)(out.second & ~POOL_USED);
+    free(f);
+    return idx;
+}

@@ -66,6 +66,17 @@ int oracle_seq_smmh(const int* op, const float* key, const uint32_t* payload, in
                     float* out_first, uint32_t* out_second, uint32_t* popped);
 int oracle_seq_result_heap(const float* key, const uint32_t* payload, int n, int cap,
                            float* out_first, uint32_t* out_second);
+float oracle_full_l2(const void* base, int dtype, uint32_t dim, uint32_t sample, const void* queries,
+                     uint32_t row);
+int oracle_exact_search(const gofann_graph* g, const uint32_t* label_size, const gofann_attrs* a,
+                        const void* base, int dtype, uint32_t dim, const void* queries, const gofann_routes* r,
+                        const gofann_search_params* sp, uint32_t* ids, float* d, int32_t* steps,
+                        uint32_t* trace, uint32_t trace_width, int threads);
+int oracle_exact_posting_scan(const void* base, int dtype, uint32_t dim, const void* queries,
+                              const gofann_attrs* a, const gofann_routes* r, const uint32_t* posting_ids,
+                              const uint64_t* route_begin, const uint32_t* route_count, int k,
+                              uint32_t* out_ids, float* out_d);
+int oracle_full_pickup_index(const float* keys, const uint32_t* vals, int size);
 void oracle_seq_hash(const uint32_t* values, int n, uint32_t* table, int32_t* outcome);
 
 #ifdef __cplusplus

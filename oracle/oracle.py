@@ -79,7 +79,16 @@ def olib() -> C.CDLL:
         L.oracle_pred_matches.argtypes = [C.POINTER(A.Routes), C.POINTER(A.Attrs), U32, U32]
         L.oracle_pred_enabled.argtypes = [C.POINTER(A.Routes), U32]
         L.oracle_labels_match.argtypes = [C.POINTER(A.Routes), C.POINTER(A.Attrs), U32, U32]
-        for fn in ("oracle_beam_search", "oracle_posting_scan", "oracle_rerank", "oracle_route_merge",
+        L.oracle_full_pickup_index.argtypes = [sp, sp, C.c_int]
+        L.oracle_full_pickup_index.restype = C.c_int
+        L.oracle_full_l2.argtypes = [sp, C.c_int, U32, U32, sp, U32]
+        L.oracle_full_l2.restype = C.c_float
+        L.oracle_exact_search.argtypes = [C.POINTER(A.Graph), sp, C.POINTER(A.Attrs), sp, C.c_int, U32, sp,
+                                          C.POINTER(A.Routes), C.POINTER(A.SearchParams), sp, sp, sp, sp, U32,
+                                          C.c_int]
+        L.oracle_exact_posting_scan.argtypes = [sp, C.c_int, U32, sp, C.POINTER(A.Attrs), C.POINTER(A.Routes), sp,
+                                                sp, sp, C.c_int, sp, sp]
+        for fn in ("oracle_exact_search", "oracle_exact_posting_scan", "oracle_beam_search", "oracle_posting_scan", "oracle_rerank", "oracle_route_merge",
                    "oracle_shard_merge", "oracle_filtered_topk"):
             getattr(L, fn).restype = C.c_int
         _O = L
@@ -266,6 +275,55 @@ def filtered_topk(base, dtype: int, queries, attrs: dict, routes: dict, k: int):
     return ids, d
 
 
+def exact_search(graph: dict, attrs: dict, base, dtype: int, queries, routes: dict, label_size=None,
+                 threads: int = 1, trace_width: int = 0, **params):
+    """Full-GPU exact-distance traversal (run_full_gpu_highfreq_route,
+    backend_full_gpu.cu:1682-2043): per route the top-k sample ids and
+    distances, step counts and (optionally) the expansion trace."""
+    g, at, rs = A.fill_graph(graph), A.fill_attrs(attrs), A.fill_routes(routes)
+    sp = A.fill_params(**params)
+    base = np.ascontiguousarray(base)
+    queries = np.ascontiguousarray(queries)
+    ls = None if label_size is None else _c(label_size, np.uint32)
+    n, k = rs.n_routes, sp.result_width
+    ids = np.empty((n, k), np.uint32)
+    d = np.empty((n, k), np.float32)
+    steps = np.empty(n, np.int32)
+    trace = np.empty((n, trace_width), np.uint32) if trace_width else None
+    st = olib().oracle_exact_search(C.byref(g), P(ls), C.byref(at), P(base), dtype, base.shape[1], P(queries),
+                                    C.byref(rs), C.byref(sp), P(ids), P(d), P(steps), P(trace), trace_width, threads)
+    if st != 0:
+        raise RuntimeError(f"oracle_exact_search status {st}")
+    if trace_width:
+        return ids, d, steps, trace
+    return ids, d, steps
+
+
+def exact_posting_scan(base, dtype: int, queries, attrs: dict, routes: dict, posting_ids, route_begin, route_count,
+                       k: int):
+    """Full-GPU exact posting scan (full_gpu_lowfreq_kernel, backend_full_gpu.cu:2124-2260)."""
+    base = np.ascontiguousarray(base)
+    queries = np.ascontiguousarray(queries)
+    at, rs = A.fill_attrs(attrs), A.fill_routes(routes)
+    pid, rb, rc = _c(posting_ids, np.uint32), _c(route_begin, np.uint64), _c(route_count, np.uint32)
+    n = rs.n_routes
+    ids = np.empty((n, k), np.uint32)
+    d = np.empty((n, k), np.float32)
+    st = olib().oracle_exact_posting_scan(P(base), dtype, base.shape[1], P(queries), C.byref(at), C.byref(rs), P(pid),
+                                          P(rb), P(rc), k, P(ids), P(d))
+    if st != 0:
+        raise RuntimeError(f"oracle_exact_posting_scan status {st}")
+    return ids, d
+
+
+def full_l2(base, dtype: int, queries, pair_row, pair_sample):
+    base = np.ascontiguousarray(base)
+    queries = np.ascontiguousarray(queries)
+    L = olib()
+    return np.array([L.oracle_full_l2(P(base), dtype, base.shape[1], int(s), P(queries), int(r))
+                     for r, s in zip(pair_row, pair_sample)], np.float32)
+
+
 # ------------------------------------------------------ structure probes
 def seq_smmh(op, key, payload, use_ref=False):
     op = _c(op, np.int32)
@@ -367,6 +425,13 @@ def pickup_index(keys, vals, size: int) -> int:
     k = _c(keys, np.float32)
     v = _c(vals, np.uint32)
     return int(olib().oracle_pickup_index(P(k), P(v), int(size)))
+
+
+def full_pickup_index(keys, vals, size: int) -> int:
+    """The frontier entry the Full-GPU traversal's pickup takes (index, or -1)."""
+    k = _c(keys, np.float32)
+    v = _c(vals, np.uint32)
+    return int(olib().oracle_full_pickup_index(P(k), P(v), int(size)))
 
 
 def cpu_count() -> int:

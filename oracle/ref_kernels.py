@@ -192,3 +192,185 @@ def result_heap_cases(keys: np.ndarray, payloads: np.ndarray, cap: int, device="
         raise RuntimeError(f"gofann_ref_result_heap_cases returned {st}")
     torch.cuda.synchronize()
     return of.cpu().numpy(), os_.cpu().numpy().view(np.uint32)
+
+
+# ------------------------------------------------- the Full-GPU backend
+FULL_LIB = HERE / "_ref" / "libgofann_ref_full_gpu.so"
+
+
+class RefFullArgs(C.Structure):
+    """Byte-for-byte gofann_ref_full_args of oracle/ref_full_gpu.cu."""
+    _fields_ = [(n, _P) for n in (
+        "base", "queries", "graph", "active_ids", "query_vector_ids", "group_ids", "start_local", "label_size",
+        "label_offset", "row_to_sample", "row_filter_mask", "filter_bits", "filter_modes", "single_extra",
+        "active_range_counts", "qlabel_indptr", "qlabel_indices", "sample_indptr", "sample_indices",
+        "range_modes", "range_lower", "range_upper", "base_ranges", "low_sample_ids", "results", "distances",
+        "steps")] + \
+        [(n, _U32) for n in ("base_rows", "dim", "degree", "n_routes", "range_count", "finish_count", "max_steps",
+                             "topk")] + \
+        [(n, _I32) for n in ("early_stop_mode", "queue_size", "dtype", "reserved")]
+
+
+_F = None
+
+
+def full_available() -> bool:
+    return FULL_LIB.exists()
+
+
+def full_lib() -> C.CDLL:
+    global _F
+    if _F is None:
+        L = C.CDLL(str(FULL_LIB))
+        for fn in ("gofann_ref_full_highfreq", "gofann_ref_full_lowfreq"):
+            getattr(L, fn).argtypes = [C.POINTER(RefFullArgs)]
+            getattr(L, fn).restype = C.c_int
+        L.gofann_ref_full_args_size.restype = C.c_size_t
+        if L.gofann_ref_full_args_size() != C.sizeof(RefFullArgs):
+            raise RuntimeError("gofann_ref_full_args layout mismatch")
+        L.gofann_ref_block_pickup_cases.argtypes = [_P, _P, C.c_int, C.c_int, _P]
+        L.gofann_ref_block_pickup_cases.restype = C.c_int
+        _F = L
+    return _F
+
+
+def _full_common(a: RefFullArgs, case: dict, routes: dict, d, device):
+    """Fills the arguments both Full-GPU kernels share: vectors, the route's
+    residual labels (every query label but its own, filter mode
+    GenericWithRange = 5: active ranges, then the labels), filter bits and
+    ranges."""
+    attrs = case["attrs"]
+    n = int(routes["query_row"].shape[0])
+    base, queries = case["base"], case["queries"]
+    a.base, a.queries = d(base), d(queries)
+    a.base_rows, a.dim, a.dtype = int(base.shape[0]), int(base.shape[1]), int(case["dtype"])
+    a.active_ids = d(np.arange(n, dtype=np.uint32))
+    a.query_vector_ids = d(routes["query_row"])
+    a.n_routes = n
+    ip, ind, prim = routes["qlabel_indptr"], routes["qlabel_indices"], routes["primary_label"]
+    res = [np.array([x for x in ind[ip[r]:ip[r + 1]] if x != prim[r]], np.uint32) for r in range(n)]
+    rp = np.zeros(n + 1, np.uint32)
+    rp[1:] = np.cumsum([len(x) for x in res])
+    a.qlabel_indptr = d(rp)
+    a.qlabel_indices = d(np.concatenate(res + [np.zeros(1, np.uint32)]).astype(np.uint32))
+    a.sample_indptr = d(attrs["label_indptr"].astype(np.uint32))
+    a.sample_indices = d(attrs["label_indices"])
+    a.filter_bits = d(routes.get("filter_bits", np.full(n, np.uint64(0xFFFFFFFFFFFFFFFF), np.uint64)))
+    a.filter_modes = d(np.full(n, 5, np.uint8))
+    a.single_extra = d(np.full(n, U32MAX, np.uint32))
+    rm = routes.get("range_modes")
+    if rm is not None:
+        a.range_count = int(rm.shape[1])
+        a.range_modes, a.range_lower, a.range_upper = d(rm), d(routes["range_lower"]), d(routes["range_upper"])
+        a.base_ranges = d(attrs["range_values"])
+        a.active_range_counts = d((rm != 0).sum(1).astype(np.uint32))
+    else:
+        a.active_range_counts = d(np.zeros(n, np.uint32))
+
+
+def run_reference_full(case: dict, device="cuda") -> dict:
+    """The reference's graph-route kernel on a tests/ref_full_cases.py case:
+    per route the top-k sample ids, distances and step counts."""
+    import torch
+    keep = []
+
+    def d(x):
+        x = np.ascontiguousarray(x)
+        if x.dtype == np.uint64:
+            x = x.view(np.int64)
+        elif x.dtype == np.uint32:
+            x = x.view(np.int32)
+        elif x.dtype == np.uint16:
+            x = x.view(np.int16)
+        t = torch.from_numpy(x).to(device)
+        keep.append(t)
+        return t.data_ptr()
+
+    p, g, routes = case["params"], case["graph"], case["routes"]
+    a = RefFullArgs()
+    _full_common(a, case, routes, d, device)
+    n, k = a.n_routes, int(p["result_width"])
+    rows = int(g["adjacency"].shape[0])
+    off = g["label_offset"].astype(np.int64)
+    a.graph, a.degree = d(g["adjacency"]), int(g["adjacency"].shape[1])
+    a.label_offset = d(g["label_offset"])
+    a.label_size = d(np.diff(np.append(off, rows)).astype(np.uint32))
+    a.row_to_sample = d(g["row_to_sample"])
+    a.row_filter_mask = d(g.get("row_filter_mask", np.full(rows, np.uint64(0xFFFFFFFFFFFFFFFF), np.uint64)))
+    a.group_ids, a.start_local = d(routes["group_id"]), d(routes["start_local"])
+    a.finish_count, a.max_steps, a.topk = int(p["finish_limit"]), int(p["max_steps"]), k
+    a.early_stop_mode, a.queue_size = int(p["early_stop_mode"]), int(p["queue_size"])
+    ids = torch.full((n, k), -1, dtype=torch.int64, device=device)
+    dist = torch.full((n, k), float(np.finfo(np.float32).max), dtype=torch.float32, device=device)
+    steps = torch.zeros(n, dtype=torch.int32, device=device)
+    a.results, a.distances, a.steps = ids.data_ptr(), dist.data_ptr(), steps.data_ptr()
+    st = full_lib().gofann_ref_full_highfreq(C.byref(a))
+    if st != 0:
+        raise RuntimeError(f"gofann_ref_full_highfreq returned {st}")
+    torch.cuda.synchronize()
+    out = ids.cpu().numpy().astype(np.uint64)
+    res = {"ids": np.where(out > U32MAX, U32MAX, out).astype(np.uint32), "dists": dist.cpu().numpy(),
+           "steps": steps.cpu().numpy()}
+    del keep
+    return res
+
+
+def run_reference_full_low(case: dict, device="cuda") -> dict:
+    """The reference's posting-route kernel on a build_low_case case: each
+    route is its own low-frequency group (its slice of posting_ids), every
+    posting entry's row mask all ones."""
+    import torch
+    keep = []
+
+    def d(x):
+        x = np.ascontiguousarray(x)
+        if x.dtype == np.uint64:
+            x = x.view(np.int64)
+        elif x.dtype == np.uint32:
+            x = x.view(np.int32)
+        elif x.dtype == np.uint16:
+            x = x.view(np.int16)
+        t = torch.from_numpy(x).to(device)
+        keep.append(t)
+        return t.data_ptr()
+
+    routes = case["routes"]
+    a = RefFullArgs()
+    _full_common(a, case, routes, d, device)
+    n, k = a.n_routes, int(case["topk"])
+    a.group_ids = d(np.arange(n, dtype=np.uint32))
+    a.label_offset = d(case["begin"].astype(np.uint32))
+    a.label_size = d(case["count"])
+    a.low_sample_ids = d(case["posting_ids"])
+    a.row_filter_mask = d(np.full(case["posting_ids"].shape[0], np.uint64(0xFFFFFFFFFFFFFFFF), np.uint64))
+    a.topk = k
+    ids = torch.full((n, k), -1, dtype=torch.int64, device=device)
+    dist = torch.full((n, k), float(np.finfo(np.float32).max), dtype=torch.float32, device=device)
+    steps = torch.zeros(n, dtype=torch.int32, device=device)
+    a.results, a.distances, a.steps = ids.data_ptr(), dist.data_ptr(), steps.data_ptr()
+    st = full_lib().gofann_ref_full_lowfreq(C.byref(a))
+    if st != 0:
+        raise RuntimeError(f"gofann_ref_full_lowfreq returned {st}")
+    torch.cuda.synchronize()
+    out = ids.cpu().numpy().astype(np.uint64)
+    res = {"ids": np.where(out > U32MAX, U32MAX, out).astype(np.uint32), "dists": dist.cpu().numpy()}
+    del keep
+    return res
+
+
+def block_pickup_cases(keys: np.ndarray, used: np.ndarray, sizes: np.ndarray, device="cuda") -> np.ndarray:
+    """The Full-GPU backend's block pickup (128 threads) on frontiers
+    keys[c][:sizes[c]]: the index it picks per frontier, -1 when all used."""
+    import torch
+    n, stride = keys.shape
+    f = np.zeros((n, stride, 2), np.uint32)
+    f[:, :, 0] = np.ascontiguousarray(keys, np.float32).view(np.uint32)
+    f[:, :, 1] = np.arange(stride, dtype=np.uint32)[None, :] | (used.astype(np.uint32) << 31)
+    df = torch.from_numpy(f.view(np.int32)).to(device)
+    ds = torch.from_numpy(np.ascontiguousarray(sizes, np.int32)).to(device)
+    out = torch.empty(n, dtype=torch.int32, device=device)
+    st = full_lib().gofann_ref_block_pickup_cases(df.data_ptr(), ds.data_ptr(), n, stride, out.data_ptr())
+    if st != 0:
+        raise RuntimeError(f"gofann_ref_block_pickup_cases returned {st}")
+    torch.cuda.synchronize()
+    return out.cpu().numpy()

@@ -172,3 +172,48 @@ def test_oracle_result_heap_matches_reference_device_heap(cap):
     for c in range(hk.shape[0]):
         of, op = O.seq_result_heap(hk[c], np.arange(hk.shape[1], dtype=np.uint32), cap)
         assert np.array_equal(bits(of[:cap][::-1]), bits(f[c])) and np.array_equal(op[:cap][::-1], p[c])
+
+
+# ---- the reference's Full-GPU kernels, recorded on a B200
+# (tests/golden/make_ref_full_gpu_golden.py over tests/ref_full_cases.py)
+FG = np.load(Path.parent / "reference_full_gpu.npz")
+
+
+def _full_cases():
+    import ref_full_cases as R
+    return R
+
+
+@pytest.mark.parametrize("name", _full_cases().CASE_NAMES)
+def test_oracle_replays_reference_full_gpu_kernel(name):
+    """Exact-distance traversal: ids, distance bits and step counts of the
+    reference's full_gpu_highfreq_kernel on u8 / f32 / f16 cases with many
+    distance ties, filter bits, row masks and range modes."""
+    R = _full_cases()
+    c = R.build_case(name)
+    assert bytes(FG[f"{name}/digest"]).hex() == R.case_digest(c), "case inputs drifted from the golden file"
+    ids, d, steps = O.exact_search(c["graph"], c["attrs"], c["base"], c["dtype"], c["queries"], c["routes"],
+                                   threads=4, **c["params"])
+    assert np.array_equal(ids, FG[f"{name}/ids"])
+    assert np.array_equal(bits(d), FG[f"{name}/dist_bits"])
+    assert np.array_equal(steps, FG[f"{name}/steps"])
+
+
+@pytest.mark.parametrize("name", _full_cases().LOW_NAMES)
+def test_oracle_replays_reference_full_gpu_posting_kernel(name):
+    R = _full_cases()
+    c = R.build_low_case(name)
+    assert bytes(FG[f"{name}/digest"]).hex() == R.case_digest(c)
+    ids, d = O.exact_posting_scan(c["base"], c["dtype"], c["queries"], c["attrs"], c["routes"], c["posting_ids"],
+                                  c["begin"], c["count"], c["topk"])
+    assert np.array_equal(ids, FG[f"{name}/ids"])
+    assert np.array_equal(bits(d), FG[f"{name}/dist_bits"])
+
+
+def test_oracle_full_pickup_matches_reference_block_pickup():
+    """The block pickup's choice (smallest distance, then smallest index) on
+    600 tie-heavy frontiers."""
+    keys, used, sizes = FG["pickup/keys"], FG["pickup/used"], FG["pickup/sizes"]
+    vals = np.arange(keys.shape[1], dtype=np.uint32)[None, :] | (used.astype(np.uint32) << 31)
+    mine = np.array([O.full_pickup_index(keys[c], vals[c], int(sizes[c])) for c in range(keys.shape[0])])
+    assert np.array_equal(mine, FG["pickup/picked"])
