@@ -62,4 +62,20 @@ const char* gofann_last_error(void) { return gofann::g_last_error; }
 
 int gofann_device_sm_count(void) { return gofann::sm_count(); }
 
+int gofann_string_peq(const uint8_t* pattern, uint32_t length, uint32_t* peq_out)
+{
+    if ((!pattern && length) || !peq_out) return gofann::fail(GOFANN_ERR_INVALID, "string_peq: null argument");
+    if (length > GOFANN_FUZZY_MAX_LENGTH)
+        return gofann::fail(GOFANN_ERR_UNSUPPORTED, "string_peq: fuzzy pattern of %u bytes (at most %d)", length,
+                            GOFANN_FUZZY_MAX_LENGTH);
+    for (int c = 0; c < 128; ++c) peq_out[c] = 0u;
+    for (uint32_t i = 0; i < length; ++i) {
+        if (pattern[i] >= 128)
+            return gofann::fail(GOFANN_ERR_UNSUPPORTED, "string_peq: fuzzy pattern byte %u at %u is not ASCII",
+                                pattern[i], i);
+        peq_out[pattern[i]] |= 1u << i;
+    }
+    return GOFANN_OK;
+}
+
 }  // extern "C"

@@ -166,13 +166,7 @@ int plan_launch(const gofann_graph* graph, const gofann_attrs* attrs, const gofa
 
     BeamArgs& args = lp.args;
     args.graph = *graph;
-    if (attrs) {
-        args.attrs.indptr = attrs->label_indptr;
-        args.attrs.indices = attrs->label_indices;
-        args.attrs.ranges = attrs->range_values;
-        args.attrs.n_samples = attrs->n_samples;
-        args.attrs.range_count = attrs->range_count;
-    }
+    args.attrs = make_attr_view(attrs);
     args.codes = *codes;
     args.prep = *prep;
     args.routes = *routes;

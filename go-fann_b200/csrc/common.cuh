@@ -387,7 +387,28 @@ struct AttrView {
     const float* ranges;
     uint32_t n_samples;
     uint32_t range_count;
+    const uint64_t* str_offsets;
+    const uint8_t* str_bytes;
+    const int64_t* ints;
+    uint32_t int_count;
 };
+// The device view of a gofann_attrs descriptor (zeros for NULL).
+inline AttrView make_attr_view(const gofann_attrs* a)
+{
+    AttrView v{};
+    if (a) {
+        v.indptr = a->label_indptr;
+        v.indices = a->label_indices;
+        v.ranges = a->range_values;
+        v.n_samples = a->n_samples;
+        v.range_count = a->range_count;
+        v.str_offsets = a->string_offsets;
+        v.str_bytes = a->string_bytes;
+        v.ints = a->int_values;
+        v.int_count = a->int_count;
+    }
+    return v;
+}
 
 // Is `label` in the sorted label row indices[begin, end)?
 __device__ __forceinline__ bool row_contains(const uint32_t* indices, uint64_t begin, uint64_t end, uint32_t label)
@@ -419,9 +440,77 @@ __device__ __forceinline__ bool pred_enabled(const gofann_routes& r, uint32_t ro
     if (!r.pred_offsets) return false;
     return r.pred_enabled ? r.pred_enabled[route] != 0 : true;
 }
+// Levenshtein distance between a pattern of m <= 32 bytes (its match table
+// peq: bit i of peq[c] = pattern[i] == c) and text[0, n), by the
+// bit-parallel algorithm of Myers (J. ACM 46(3), 1999) in the global form of
+// Hyyro (2001): column j of the DP matrix is kept as vertical +1 / -1 delta
+// bit vectors, the top row D[0][j] = j contributes a horizontal +1 carried
+// into bit 0, and the last row's value is tracked in `score`.  Text bytes
+// of 128 and above match no pattern byte.
+__device__ __forceinline__ uint32_t myers_edit_distance(const uint32_t* __restrict__ peq, uint32_t m,
+                                                        const uint8_t* __restrict__ text, uint32_t n)
+{
+    if (m == 0) return n;
+    const uint32_t last = 1u << (m - 1);
+    uint32_t pv = m == 32 ? 0xffffffffu : (1u << m) - 1u, mv = 0u, score = m;
+    for (uint32_t j = 0; j < n; ++j) {
+        const uint8_t c = text[j];
+        const uint32_t eq = c < 128 ? __ldg(peq + c) : 0u;
+        const uint32_t xv = eq | mv;
+        const uint32_t xh = (((eq & pv) + pv) ^ pv) | eq;
+        uint32_t ph = mv | ~(xh | pv);
+        uint32_t mh = pv & xh;
+        if (ph & last) ++score;
+        else if (mh & last) --score;
+        ph = (ph << 1) | 1u;
+        mh <<= 1;
+        pv = mh | ~(xv | ph);
+        mv = ph & xv;
+    }
+    return score;
+}
+
+// String and integer atoms of clause `ci` for `sample` (all must hold).
+__device__ __forceinline__ bool ext_atoms_match(const gofann_routes& r, const AttrView& a, uint32_t ci,
+                                                uint32_t sample)
+{
+    const gofann_clause_ext x = r.pred_ext[ci];
+    for (uint32_t j = x.int_begin; j < x.int_end; ++j) {
+        const gofann_int_atom at = r.pred_ints[j];
+        if (at.mode == 0) continue;
+        if (a.ints == nullptr || at.dimension >= a.int_count) return false;
+        const int64_t v = a.ints[static_cast<uint64_t>(sample) * a.int_count + at.dimension];
+        const bool ok = at.mode == 1 ? v > at.lower : at.mode == 2 ? v < at.upper
+                                                     : at.mode == 3 ? (v >= at.lower && v < at.upper) : false;
+        if (!ok) return false;
+    }
+    if (x.string_begin == x.string_end) return true;
+    if (a.str_offsets == nullptr) return false;
+    const uint64_t sb = a.str_offsets[sample], se = a.str_offsets[sample + 1];
+    const uint8_t* text = a.str_bytes + sb;
+    const uint32_t n = static_cast<uint32_t>(se - sb);
+    for (uint32_t j = x.string_begin; j < x.string_end; ++j) {
+        const gofann_string_atom at = r.pred_strings[j];
+        const uint8_t* q = r.pred_string_bytes + at.offset;
+        if (at.kind == GOFANN_STRING_EXACT) {
+            if (n != at.length) return false;
+            for (uint32_t i = 0; i < n; ++i)
+                if (text[i] != q[i]) return false;
+        } else {
+            const uint32_t gap = n > at.length ? n - at.length : at.length - n;
+            if (gap > at.max_edits || at.length > GOFANN_FUZZY_MAX_LENGTH) return false;
+            if (myers_edit_distance(r.pred_string_peq + static_cast<size_t>(j) * 128, at.length, text, n) >
+                at.max_edits)
+                return false;
+        }
+    }
+    return true;
+}
+
 // gpu_predicate::matches with clauses (gpu_predicate_index.cuh:109-136),
 // given the sample's sorted label row labels[lbegin, lend) (the CSR's
-// indices, or a copy of the row).
+// indices, or a copy of the row), then the clause's string and integer
+// atoms when the routes carry them.
 __device__ __forceinline__ bool pred_matches_row(const gofann_routes& r, const AttrView& a, uint32_t route,
                                                  uint32_t sample, const uint32_t* labels, uint64_t lbegin,
                                                  uint64_t lend)
@@ -439,11 +528,13 @@ __device__ __forceinline__ bool pred_matches_row(const gofann_routes& r, const A
                    range_match(at.mode, at.lower, at.upper,
                                a.ranges[static_cast<uint64_t>(sample) * a.range_count + at.dimension]);
         }
+        if (pass && r.pred_ext) pass = ext_atoms_match(r, a, i, sample);
         if (pass) return true;
     }
     return false;
 }
-// gpu_predicate::matches with clauses (gpu_predicate_index.cuh:109-136).
+// gpu_predicate::matches with clauses (gpu_predicate_index.cuh:109-136),
+// plus the clauses' string and integer atoms.
 __device__ __forceinline__ bool pred_matches(const gofann_routes& r, const AttrView& a,
                                              uint32_t route, uint32_t sample)
 {
@@ -460,6 +551,7 @@ __device__ __forceinline__ bool pred_matches(const gofann_routes& r, const AttrV
                    range_match(at.mode, at.lower, at.upper,
                                a.ranges[static_cast<uint64_t>(sample) * a.range_count + at.dimension]);
         }
+        if (pass && r.pred_ext) pass = ext_atoms_match(r, a, i, sample);
         if (pass) return true;
     }
     return false;

@@ -599,11 +599,7 @@ int gofann_exact_search(const gofann_graph* graph, const uint32_t* label_size, c
     exact::ExactArgs a{};
     a.graph = *graph;
     a.label_size = label_size;
-    a.attrs.indptr = attrs->label_indptr;
-    a.attrs.indices = attrs->label_indices;
-    a.attrs.ranges = attrs->range_values;
-    a.attrs.n_samples = attrs->n_samples;
-    a.attrs.range_count = attrs->range_count;
+    a.attrs = make_attr_view(attrs);
     a.routes = *routes;
     a.p = p;
     a.out = *out;

@@ -518,13 +518,7 @@ int gofann_posting_scan(const gofann_codes* codes, const gofann_prepared* prep, 
     a.codes = *codes;
     a.prep = *prep;
     a.routes = *routes;
-    if (attrs) {
-        a.attrs.indptr = attrs->label_indptr;
-        a.attrs.indices = attrs->label_indices;
-        a.attrs.ranges = attrs->range_values;
-        a.attrs.n_samples = attrs->n_samples;
-        a.attrs.range_count = attrs->range_count;
-    }
+    a.attrs = make_attr_view(attrs);
     a.posting_ids = posting_ids;
     a.route_begin = route_begin;
     a.route_count = route_count;
@@ -607,15 +601,8 @@ int gofann_exact_posting_scan(const void* base, int dtype, uint32_t n_samples, u
     if (routes->n_routes == 0) return GOFANN_OK;
     ScanArgs a{};
     a.routes = *routes;
-    if (attrs) {
-        a.attrs.indptr = attrs->label_indptr;
-        a.attrs.indices = attrs->label_indices;
-        a.attrs.ranges = attrs->range_values;
-        a.attrs.n_samples = attrs->n_samples;
-        a.attrs.range_count = attrs->range_count;
-    } else {
-        a.attrs.n_samples = n_samples;
-    }
+    a.attrs = make_attr_view(attrs);
+    if (!attrs) a.attrs.n_samples = n_samples;
     a.posting_ids = posting_ids;
     a.route_begin = route_begin;
     a.route_count = route_count;

@@ -59,12 +59,7 @@ int gofann_predicate_pass_masks(const gofann_graph* graph, const gofann_attrs* a
     if (routes->pred_offsets && (!attrs->label_indptr || !routes->clauses || !routes->pred_handles))
         return fail(GOFANN_ERR_INVALID, "predicate_pass_masks: predicate arrays missing");
     if (n_candidates == 0) return GOFANN_OK;
-    AttrView at{};
-    at.indptr = attrs->label_indptr;
-    at.indices = attrs->label_indices;
-    at.ranges = attrs->range_values;
-    at.n_samples = attrs->n_samples;
-    at.range_count = attrs->range_count;
+    const AttrView at = make_attr_view(attrs);
     const int threads = 256;
     const uint64_t want = (static_cast<uint64_t>(n_candidates) + threads - 1) / threads;
     const int sms = sm_count() > 0 ? sm_count() : 148;

@@ -161,14 +161,7 @@ int gofann_rerank(const void* base, int dtype, uint32_t n_samples, uint32_t dim,
     if (check && (!attrs || !attrs->label_indptr || !attrs->label_indices))
         return fail(GOFANN_ERR_INVALID, "rerank: residual label check needs the sample label CSR");
     if (routes->n_routes == 0) return GOFANN_OK;
-    AttrView av{};
-    if (attrs) {
-        av.indptr = attrs->label_indptr;
-        av.indices = attrs->label_indices;
-        av.ranges = attrs->range_values;
-        av.n_samples = attrs->n_samples;
-        av.range_count = attrs->range_count;
-    }
+    const AttrView av = make_attr_view(attrs);
     const size_t smem = static_cast<size_t>(width) * 8 + 16;
     cudaStream_t s = as_stream(stream);
     const unsigned blocks = routes->n_routes;

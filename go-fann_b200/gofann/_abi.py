@@ -42,6 +42,11 @@ class RangeAtom(C.Structure):
     _fields_ = [("dimension", U32), ("mode", U32), ("lower", C.c_float), ("upper", C.c_float)]
 
 
+STRING_EXACT, STRING_FUZZY, FUZZY_MAX_LENGTH = 0, 1, 32
+CLAUSE_EXT_DTYPE = np.dtype([("string_begin", "<u4"), ("string_end", "<u4"), ("int_begin", "<u4"),
+                             ("int_end", "<u4")])
+STRING_ATOM_DTYPE = np.dtype([("kind", "<u4"), ("max_edits", "<u4"), ("offset", "<u4"), ("length", "<u4")])
+INT_ATOM_DTYPE = np.dtype([("dimension", "<u4"), ("mode", "<u4"), ("lower", "<i8"), ("upper", "<i8")])
 CLAUSE_DTYPE = np.dtype([("label_begin", "<u4"), ("label_end", "<u4"), ("range_begin", "<u4"), ("range_end", "<u4")])
 RANGE_ATOM_DTYPE = np.dtype([("dimension", "<u4"), ("mode", "<u4"), ("lower", "<f4"), ("upper", "<f4")])
 
@@ -54,7 +59,8 @@ class Graph(C.Structure):
 
 class Attrs(C.Structure):
     _fields_ = [("label_indptr", P), ("label_indices", P), ("range_values", P),
-                ("n_samples", U32), ("range_count", U32)]
+                ("n_samples", U32), ("range_count", U32), ("string_offsets", P), ("string_bytes", P),
+                ("int_values", P), ("int_count", U32), ("reserved", U32)]
 
 
 class Codes(C.Structure):
@@ -73,7 +79,8 @@ class Routes(C.Structure):
                 ("filter_bits", P), ("range_modes", P), ("range_lower", P), ("range_upper", P),
                 ("qlabel_indptr", P), ("qlabel_indices", P), ("primary_label", P), ("pred_offsets", P),
                 ("clauses", P), ("pred_handles", P), ("pred_ranges", P), ("pred_enabled", P),
-                ("route_compiled", P)]
+                ("route_compiled", P), ("pred_ext", P), ("pred_strings", P), ("pred_string_bytes", P),
+                ("pred_string_peq", P), ("pred_ints", P)]
 
 
 class SearchParams(C.Structure):
@@ -148,6 +155,11 @@ def fill_attrs(a: dict) -> Attrs:
     s.n_samples = int(a["label_indptr"].shape[0] - 1)
     rv = a.get("range_values")
     s.range_count = int(rv.shape[1]) if rv is not None else 0
+    s.string_offsets = ptr(a.get("string_offsets"))
+    s.string_bytes = ptr(a.get("string_bytes"))
+    iv = a.get("int_values")
+    s.int_values = ptr(iv)
+    s.int_count = int(iv.shape[1]) if iv is not None else 0
     return s
 
 
@@ -188,7 +200,8 @@ def fill_prepared(p: dict) -> Prepared:
 
 ROUTE_KEYS = ("query_row", "group_id", "start_local", "filter_bits", "range_modes", "range_lower",
               "range_upper", "qlabel_indptr", "qlabel_indices", "primary_label", "pred_offsets", "clauses",
-              "pred_handles", "pred_ranges", "pred_enabled", "route_compiled")
+              "pred_handles", "pred_ranges", "pred_enabled", "route_compiled", "pred_ext", "pred_strings",
+              "pred_string_bytes", "pred_string_peq", "pred_ints")
 
 
 def fill_routes(r: dict) -> Routes:
@@ -271,6 +284,8 @@ def lib() -> C.CDLL:
     L.gofann_beam_search_scratch_bytes.restype = C.c_size_t
     L.gofann_rabitq_gemm_scratch_bytes.argtypes = [U32, U32, U32, C.c_int]
     L.gofann_rabitq_gemm_scratch_bytes.restype = C.c_size_t
+    L.gofann_string_peq.argtypes = [sp, U32, sp]
+    L.gofann_string_peq.restype = C.c_int
     L.gofann_exact_search_scratch_bytes.argtypes = [U32]
     L.gofann_exact_search_scratch_bytes.restype = C.c_size_t
     L.gofann_row_record_stride.argtypes = [U32]
@@ -301,7 +316,8 @@ EXPORTED = ("gofann_abi_version", "gofann_last_error", "gofann_device_sm_count",
             "gofann_posting_scan", "gofann_segment_merge", "gofann_predicate_pass_masks", "gofann_search_batch_scratch_bytes",
             "gofann_search_batch", "gofann_rerank", "gofann_route_merge", "gofann_shard_merge",
             "gofann_row_record_stride", "gofann_build_row_records", "gofann_offset_ids",
-            "gofann_exact_search_scratch_bytes", "gofann_exact_search", "gofann_exact_posting_scan")
+            "gofann_exact_search_scratch_bytes", "gofann_exact_search", "gofann_exact_posting_scan",
+            "gofann_string_peq")
 
 
 def header_symbols(header: str | os.PathLike | None = None) -> list[str]:

@@ -50,7 +50,7 @@
 extern "C" {
 #endif
 
-#define GOFANN_ABI_VERSION 3
+#define GOFANN_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define GOFANN_API __attribute__((visibility("default")))
@@ -103,6 +103,36 @@ typedef struct gofann_range_atom {
     float lower, upper;
 } gofann_range_atom;
 
+/* String atom of a DNF clause: the sample's string attribute equals the
+ * query string (GOFANN_STRING_EXACT), or is within max_edits insertions,
+ * deletions and substitutions of it (GOFANN_STRING_FUZZY, Levenshtein
+ * distance).  The query string is pred_string_bytes[offset, offset +
+ * length).  A fuzzy atom's query string has at most 32 bytes, all below 128,
+ * and its row of pred_string_peq holds gofann_string_peq() of it.  The
+ * reference has no edit-distance predicate (it rewrites fuzzy queries into
+ * token labels, src/data/dataloader.cpp:2973-3010); this is the device check
+ * its configurations call for. */
+enum { GOFANN_STRING_EXACT = 0, GOFANN_STRING_FUZZY = 1 };
+#define GOFANN_FUZZY_MAX_LENGTH 32
+typedef struct gofann_string_atom {
+    uint32_t kind, max_edits, offset, length;
+} gofann_string_atom;
+
+/* Integer range atom over an int64 attribute column: mode 0 any, 1
+ * v>lower, 2 v<upper, 3 lower<=v<upper (the float atom's modes, exact on
+ * int64 values; the reference compares float32, range_filter.cuh:28-45). */
+typedef struct gofann_int_atom {
+    uint32_t dimension, mode;
+    int64_t lower, upper;
+} gofann_int_atom;
+
+/* Further atoms of clause i (parallel to the clauses array): string atoms
+ * [string_begin, string_end) of pred_strings and integer atoms [int_begin,
+ * int_end) of pred_ints, ANDed with the clause's labels and float ranges. */
+typedef struct gofann_clause_ext {
+    uint32_t string_begin, string_end, int_begin, int_end;
+} gofann_clause_ext;
+
 /* Concatenated per-label graphs: row = label_offset[group] + local_row
  * (GraphRuntime::graph + GraphMetadata, dataloader.h:583-602,753-836). */
 typedef struct gofann_graph {
@@ -150,6 +180,13 @@ typedef struct gofann_attrs {
     const float* range_values;     /* device [n_samples][range_count] or NULL */
     uint32_t n_samples;
     uint32_t range_count;
+    /* one string per sample: bytes string_bytes[string_offsets[s],
+     * string_offsets[s+1]) (device, or NULL when no clause has string atoms) */
+    const uint64_t* string_offsets;
+    const uint8_t* string_bytes;
+    const int64_t* int_values;     /* device [n_samples][int_count] or NULL */
+    uint32_t int_count;
+    uint32_t reserved;
 } gofann_attrs;
 
 /* Navigation codes.  PQ: uint8 [n][pq_dim] (pq.codes.bin rows).  RaBitQ:
@@ -210,6 +247,12 @@ typedef struct gofann_routes {
     const gofann_range_atom* pred_ranges;
     const uint8_t* pred_enabled;    /* [n_routes] or NULL = enabled iff pred_offsets */
     const uint8_t* route_compiled;  /* [n_routes] or NULL */
+    /* string and integer atoms of the clauses (NULL pred_ext = none) */
+    const gofann_clause_ext* pred_ext;
+    const gofann_string_atom* pred_strings;
+    const uint8_t* pred_string_bytes;
+    const uint32_t* pred_string_peq; /* [n_string_atoms][128], rows of fuzzy atoms filled */
+    const gofann_int_atom* pred_ints;
 } gofann_routes;
 
 typedef struct gofann_search_params {
@@ -250,6 +293,11 @@ typedef struct gofann_search_out {
 
 /* ---------------------------------------------------------------- basics */
 GOFANN_API int gofann_abi_version(void);
+/* Host helper (no device work): the 128-entry match table of a fuzzy string
+ * atom -- bit i of peq_out[c] is set when pattern[i] == c -- for the
+ * bit-parallel edit distance of Myers (J. ACM 46(3), 1999) that the device
+ * check runs.  length <= GOFANN_FUZZY_MAX_LENGTH, bytes below 128. */
+GOFANN_API int gofann_string_peq(const uint8_t* pattern, uint32_t length, uint32_t* peq_out);
 GOFANN_API const char* gofann_last_error(void);
 /* Number of streaming multiprocessors of the current device (0 on error). */
 GOFANN_API int gofann_device_sm_count(void);

@@ -527,7 +527,65 @@ int oracle_pred_enabled(const gofann_routes* r, uint32_t route)
     if (!r->pred_offsets) return 0;
     return r->pred_enabled ? r->pred_enabled[route] != 0 : 1;
 }
-/* gpu_predicate::matches with clauses, gpu_predicate_index.cuh:109-136 */
+/* Levenshtein distance by the textbook dynamic programme (Wagner and
+ * Fischer, J. ACM 21(1), 1974), two rows. */
+uint32_t oracle_levenshtein(const uint8_t* p, uint32_t m, const uint8_t* t, uint32_t n)
+{
+    uint32_t* prev = (uint32_t*)malloc(sizeof(uint32_t) * (n + 1));
+    uint32_t* cur = (uint32_t*)malloc(sizeof(uint32_t) * (n + 1));
+    for (uint32_t j = 0; j <= n; ++j) prev[j] = j;
+    for (uint32_t i = 1; i <= m; ++i) {
+        cur[0] = i;
+        for (uint32_t j = 1; j <= n; ++j) {
+            uint32_t v = prev[j - 1] + (p[i - 1] != t[j - 1]);
+            if (prev[j] + 1 < v) v = prev[j] + 1;
+            if (cur[j - 1] + 1 < v) v = cur[j - 1] + 1;
+            cur[j] = v;
+        }
+        uint32_t* tmp = prev; prev = cur; cur = tmp;
+    }
+    const uint32_t d = prev[n];
+    free(prev);
+    free(cur);
+    return d;
+}
+
+/* String and integer atoms of clause ci (gofann_clause_ext): exact string
+ * equality, Levenshtein distance <= max_edits, int64 ranges in the float
+ * atom's modes. */
+static int ext_atoms_match(const gofann_routes* r, const gofann_attrs* a, uint32_t ci, uint32_t sample)
+{
+    const gofann_clause_ext x = r->pred_ext[ci];
+    for (uint32_t j = x.int_begin; j < x.int_end; ++j) {
+        const gofann_int_atom at = r->pred_ints[j];
+        if (at.mode == 0) continue;
+        if (!a->int_values || at.dimension >= a->int_count) return 0;
+        const int64_t v = a->int_values[(size_t)sample * a->int_count + at.dimension];
+        int ok = 0;
+        if (at.mode == 1) ok = v > at.lower;
+        else if (at.mode == 2) ok = v < at.upper;
+        else if (at.mode == 3) ok = v >= at.lower && v < at.upper;
+        if (!ok) return 0;
+    }
+    if (x.string_begin == x.string_end) return 1;
+    if (!a->string_offsets) return 0;
+    const uint8_t* t = a->string_bytes + a->string_offsets[sample];
+    const uint32_t n = (uint32_t)(a->string_offsets[sample + 1] - a->string_offsets[sample]);
+    for (uint32_t j = x.string_begin; j < x.string_end; ++j) {
+        const gofann_string_atom at = r->pred_strings[j];
+        const uint8_t* q = r->pred_string_bytes + at.offset;
+        if (at.kind == GOFANN_STRING_EXACT) {
+            if (n != at.length || memcmp(t, q, n) != 0) return 0;
+        } else {
+            if (at.length > GOFANN_FUZZY_MAX_LENGTH) return 0;
+            if (oracle_levenshtein(q, at.length, t, n) > at.max_edits) return 0;
+        }
+    }
+    return 1;
+}
+
+/* gpu_predicate::matches with clauses, gpu_predicate_index.cuh:109-136,
+ * then each clause's string and integer atoms */
 int oracle_pred_matches(const gofann_routes* r, const gofann_attrs* a, uint32_t route,
                         uint32_t sample)
 {
@@ -543,6 +601,7 @@ int oracle_pred_matches(const gofann_routes* r, const gofann_attrs* a, uint32_t 
                    range_match(at.mode, at.lower, at.upper,
                                a->range_values[(size_t)sample * a->range_count + at.dimension]);
         }
+        if (pass && r->pred_ext) pass = ext_atoms_match(r, a, i, sample);
         if (pass) return 1;
     }
     return 0;

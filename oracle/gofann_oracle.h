@@ -76,6 +76,7 @@ int oracle_exact_posting_scan(const void* base, int dtype, uint32_t dim, const v
                               const gofann_attrs* a, const gofann_routes* r, const uint32_t* posting_ids,
                               const uint64_t* route_begin, const uint32_t* route_count, int k,
                               uint32_t* out_ids, float* out_d);
+uint32_t oracle_levenshtein(const uint8_t* p, uint32_t m, const uint8_t* t, uint32_t n);
 int oracle_full_pickup_index(const float* keys, const uint32_t* vals, int size);
 void oracle_seq_hash(const uint32_t* values, int n, uint32_t* table, int32_t* outcome);
 

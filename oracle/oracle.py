@@ -79,6 +79,8 @@ def olib() -> C.CDLL:
         L.oracle_pred_matches.argtypes = [C.POINTER(A.Routes), C.POINTER(A.Attrs), U32, U32]
         L.oracle_pred_enabled.argtypes = [C.POINTER(A.Routes), U32]
         L.oracle_labels_match.argtypes = [C.POINTER(A.Routes), C.POINTER(A.Attrs), U32, U32]
+        L.oracle_levenshtein.argtypes = [sp, U32, sp, U32]
+        L.oracle_levenshtein.restype = U32
         L.oracle_full_pickup_index.argtypes = [sp, sp, C.c_int]
         L.oracle_full_pickup_index.restype = C.c_int
         L.oracle_full_l2.argtypes = [sp, C.c_int, U32, U32, sp, U32]
@@ -432,6 +434,12 @@ def full_pickup_index(keys, vals, size: int) -> int:
     k = _c(keys, np.float32)
     v = _c(vals, np.uint32)
     return int(olib().oracle_full_pickup_index(P(k), P(v), int(size)))
+
+
+def levenshtein(a: bytes, b: bytes) -> int:
+    pa = np.frombuffer(a, np.uint8) if a else np.zeros(1, np.uint8)
+    pb = np.frombuffer(b, np.uint8) if b else np.zeros(1, np.uint8)
+    return int(olib().oracle_levenshtein(P(pa), len(a), P(pb), len(b)))
 
 
 def cpu_count() -> int:

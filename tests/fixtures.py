@@ -168,3 +168,118 @@ def with_predicates(w, idx, routes: dict, seed=0, range_count=2):
     legacy["range_upper"] = (lo + rng.uniform(300, 900, size=(n, range_count))).astype(np.float32)
     legacy["route_compiled"] = (rng.random(n) < 0.25).astype(np.uint8)
     return attrs, graph, dnf, legacy
+
+
+def string_table(strings):
+    """Per-sample strings as (offsets u64 [n+1], bytes u8)."""
+    enc = [s.encode() for s in strings]
+    off = np.zeros(len(enc) + 1, np.uint64)
+    off[1:] = np.cumsum([len(e) for e in enc])
+    data = np.frombuffer(b"".join(enc), np.uint8).copy() if off[-1] else np.zeros(1, np.uint8)
+    return off, data
+
+
+def synth_strings(n, rng, vocab_size=300):
+    """ASCII strings of 8-32 bytes built from Zipf-distributed 3-gram tokens
+    (the config-4 string attribute); some strings repeat exactly."""
+    letters = np.frombuffer(b"abcdefghijklmnopqrstuvwxyz", np.uint8)
+    vocab = [bytes(rng.choice(letters, size=3)).decode() for _ in range(vocab_size)]
+    p = 1.0 / np.arange(1, vocab_size + 1) ** 1.1
+    p /= p.sum()
+    out = []
+    for _ in range(n):
+        target = int(rng.integers(8, 33))
+        s = ""
+        while len(s) < target:
+            s += vocab[int(rng.choice(vocab_size, p=p))]
+        out.append(s[:target])
+    return out
+
+
+def mutate(s: str, edits: int, rng) -> str:
+    """s with `edits` random insertions, deletions or substitutions."""
+    letters = "abcdefghijklmnopqrstuvwxyz"
+    s = list(s)
+    for _ in range(edits):
+        op = int(rng.integers(0, 3))
+        i = int(rng.integers(0, max(1, len(s))))
+        if op == 0 and len(s) < 32:
+            s.insert(i, letters[int(rng.integers(0, 26))])
+        elif op == 1 and len(s) > 1:
+            del s[i]
+        elif s:
+            s[i] = letters[int(rng.integers(0, 26))]
+    return "".join(s)
+
+
+def with_hybrid_predicates(w, idx, routes: dict, seed=0, int_count=2):
+    """The config-4 predicate kinds on a small workload: every sample gets a
+    string and int64 attributes; each route gets 1-3 OR-ed clauses mixing its
+    residual labels, an exact-string atom (a sample's string), a fuzzy atom
+    (a sample's string with 0-3 edits, max_edits 0-2) and int64 range atoms
+    in modes 0-3; some routes keep only label clauses.
+    Returns (attrs, routes) with the extended DNF."""
+    from gofann import _abi as A
+    rng = np.random.default_rng(seed)
+    attrs = dict(idx.attrs())
+    strings = synth_strings(w.n, rng)
+    attrs["string_offsets"], attrs["string_bytes"] = string_table(strings)
+    iv = rng.integers(-(1 << 40), 1 << 40, size=(w.n, int_count), dtype=np.int64)
+    iv[::53, 0] = 1 << 33  # exact bound hits
+    attrs["int_values"] = iv
+    n = routes["query_row"].shape[0]
+    rip, rind = routes["qlabel_indptr"], routes["qlabel_indices"]
+    offs, clauses, handles, ext, satoms, sbytes, iatoms = [0], [], [], [], [], bytearray(), []
+    peq_rows = []
+    for r in range(n):
+        prim = routes["primary_label"][r]
+        for c in range(int(rng.integers(1, 4))):
+            lb = len(handles)
+            if c == 0:
+                handles += [int(x) for x in rind[rip[r]:rip[r + 1]] if x != prim]
+            sb, ib = len(satoms), len(iatoms)
+            kind = int(rng.integers(0, 4))
+            if kind in (1, 3):  # a string atom
+                s = strings[int(rng.integers(0, w.n))]
+                fuzzy = rng.random() < 0.6
+                if fuzzy:
+                    s = mutate(s, int(rng.integers(0, 4)), rng)
+                b = s.encode()
+                satoms.append((A.STRING_FUZZY if fuzzy else A.STRING_EXACT, int(rng.integers(0, 3)), len(sbytes),
+                               len(b)))
+                sbytes += b
+                peq = np.zeros(128, np.uint32)
+                if fuzzy:
+                    for i, ch in enumerate(b):
+                        peq[ch] |= np.uint32(1 << i)
+                peq_rows.append(peq)
+            if kind in (2, 3):  # int64 atoms
+                for _ in range(int(rng.integers(1, 3))):
+                    lo, hi = np.sort(rng.integers(-(1 << 40), 1 << 40, size=2))
+                    if rng.random() < 0.2:
+                        lo = 1 << 33
+                    iatoms.append((int(rng.integers(0, int_count)), int(rng.integers(0, 4)), int(lo), int(hi)))
+            clauses.append((lb, len(handles), 0, 0))
+            ext.append((sb, len(satoms), ib, len(iatoms)))
+        offs.append(len(clauses))
+    cl = np.zeros(len(clauses), A.CLAUSE_DTYPE)
+    for i, x in enumerate(clauses):
+        cl[i] = x
+    ex = np.zeros(len(ext), A.CLAUSE_EXT_DTYPE)
+    for i, x in enumerate(ext):
+        ex[i] = x
+    sa = np.zeros(max(1, len(satoms)), A.STRING_ATOM_DTYPE)
+    for i, x in enumerate(satoms):
+        sa[i] = x
+    ia = np.zeros(max(1, len(iatoms)), A.INT_ATOM_DTYPE)
+    for i, x in enumerate(iatoms):
+        ia[i] = x
+    out = dict(routes)
+    out.update(pred_offsets=np.asarray(offs, np.uint32), clauses=cl,
+               pred_handles=np.asarray(handles if handles else [0], np.uint32),
+               pred_enabled=(rng.random(n) < 0.95).astype(np.uint8), pred_ext=ex, pred_strings=sa,
+               pred_string_bytes=np.frombuffer(bytes(sbytes) if sbytes else b"\0", np.uint8).copy(),
+               pred_string_peq=np.stack(peq_rows) if peq_rows else np.zeros((1, 128), np.uint32),
+               pred_ints=ia)
+    out.pop("pred_ranges", None)
+    return attrs, out

@@ -19,7 +19,7 @@ def test_library_exports_every_header_symbol():
     for name in declared:
         assert hasattr(lib, name), name
     assert set(declared) == set(A.EXPORTED)
-    assert lib.gofann_abi_version() == 3
+    assert lib.gofann_abi_version() == 4
 
 
 def test_nm_dynamic_symbols():
