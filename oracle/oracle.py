@@ -117,6 +117,10 @@ def rlib() -> C.CDLL | None:
         L.ref_fp16_l2.argtypes = [sp, sp, U32, U32, sp]
         L.ref_fp16_decode.argtypes = [C.c_uint16]
         L.ref_fp16_decode.restype = C.c_float
+        L.ref_graph_write.argtypes = [C.c_char_p, sp, C.c_uint64, U32, C.c_char_p, C.c_int]
+        L.ref_graph_write.restype = C.c_int
+        L.ref_graph_load.argtypes = [C.c_char_p, sp, C.c_uint64, sp, sp, C.c_char_p, C.c_int]
+        L.ref_graph_load.restype = C.c_int
         _R = L
     return _R
 

@@ -16,6 +16,7 @@
 //   predicates/gpu_predicate_index.cuh            DNF matches / priority
 //   search/rabitq/rabitq_lowfreq_merge.h          route -> original merge
 //   data/fp16_l2.h                                fp16 decode and scalar L2
+//   index/graph_file_format.h (+ .cpp, compiled)  FDRG graph file writer / loader
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -32,6 +33,7 @@
 #include "predicates/gpu_predicate_index.cuh"
 #include "search/rabitq/rabitq_lowfreq_merge.h"
 #include "data/fp16_l2.h"
+#include "index/graph_file_format.h"
 
 namespace {
 
@@ -187,5 +189,38 @@ void ref_fp16_l2(const uint16_t* base, const float* query, uint32_t rows, uint32
 }
 
 float ref_fp16_decode(uint16_t v) { return go_fann::fp16_l2::decode(v); }
+
+// The reference's FDRG graph file code (src/index/graph_file_format.cpp,
+// compiled in place): write rows x degree adjacency with its sequential
+// writer, or load a file into a contiguous matrix.  0 = ok, -1 = the
+// reference threw (the message is copied into err).
+int ref_graph_write(const char* path, const uint32_t* adj, uint64_t rows, uint32_t degree, char* err, int err_len)
+{
+    try {
+        go_fann::graph_file::GraphFileSequentialWriter w(path, rows, degree);
+        w.append_rows(adj, rows);
+        w.close();
+        return 0;
+    } catch (const std::exception& e) {
+        std::snprintf(err, static_cast<size_t>(err_len), "%s", e.what());
+        return -1;
+    }
+}
+
+int ref_graph_load(const char* path, uint32_t* out, uint64_t capacity, uint64_t* rows, uint64_t* cols, char* err,
+                   int err_len)
+{
+    try {
+        const auto m = go_fann::graph_file::load_graph_file_as_contiguous_matrix(path);
+        *rows = m.rows;
+        *cols = m.cols;
+        if (m.data.size() > capacity) return -2;
+        std::copy(m.data.begin(), m.data.end(), out);
+        return 0;
+    } catch (const std::exception& e) {
+        std::snprintf(err, static_cast<size_t>(err_len), "%s", e.what());
+        return -1;
+    }
+}
 
 }  // extern "C"
