@@ -71,7 +71,9 @@ def parse():
     ap.add_argument("--mode", default="pq", choices=["pq", "exact"],
                     help="config 2: PQ navigation + exact rerank (pq), or the Full-GPU exact-distance mode (exact: "
                          "traversal and posting scans on the exact distances of the HBM-resident base vectors)")
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3],
+    ap.add_argument("--scan-rows", type=int, default=20_000,
+                    help="config 4: tag postings and int64 range slices of at most this many rows are scanned")
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4],
                     help="BASELINE configuration: 2 (10M x 192 u8, PQ; the default) or 3 (2.7M x 4096 f32, RaBitQ)")
     return ap.parse_args()
 
@@ -1174,6 +1176,205 @@ def run_config3(args):
     print(json.dumps(line), flush=True)
 
 
+C4_METRIC = "filtered QPS @ recall@10=0.95 (config 4 shard)"
+
+
+def c4_cpu_sample(idx, plan, q, pipe, sel, qs, threads):
+    """The reference path restated on the host (oracle/) for the queries
+    `sel` of configuration 4: RaBitQ traversal and posting scans under the
+    hybrid DNF (labels, int64 and string atoms) on the GPU-prepared query
+    state, exact FP16 rerank, route merge.  Returns the merged top-10."""
+    import torch
+    from oracle import oracle as O
+    h = lambda t, dt=None: t.cpu().numpy() if dt is None else t.cpu().numpy().view(dt)
+    codes = {"rq_codes": h(idx.codes), "rq_factors": h(idx.factors), "rq_anchor_ids": h(idx.anchor_ids, np.uint32),
+             "num_anchors": int(idx.anchors.shape[0])}
+    graph = {"adjacency": h(idx.adjacency, np.uint32), "row_to_sample": np.arange(idx.n, dtype=np.uint32),
+             "label_offset": np.zeros(1, np.uint32)}
+    ea = idx.extra_attrs
+    attrs = {"label_indptr": h(idx.set_indptr, np.uint64), "label_indices": h(idx.set_indices, np.uint32),
+             "string_offsets": h(ea["string_offsets"], np.uint64), "string_bytes": h(ea["string_bytes"]),
+             "int_values": h(ea["int_values"])}
+    qs_rows = torch.from_numpy(sel).to(pipe.q8.device)
+    prep = {"rq_q8": h(pipe.q8[qs_rows]), "rq_scale": h(pipe.scale[qs_rows]), "rq_k1xsumq": h(pipe.k1[qs_rows]),
+            "rq_centroid_dist": h(pipe.gdist[qs_rows])}
+    gr, gsel, pr, psel = plan.subset(sel)
+    gr["start_local"] = pipe.groutes["start_local"].cpu().numpy().view(np.uint32)[gsel]  # entries set on the device
+    gi = np.zeros((0, pipe.shortlist), np.uint32)
+    if gsel.size:
+        gi, _, _, _ = O.beam_search(graph, attrs, codes, prep, gr, threads=threads, queue_size=qs,
+                                    result_width=pipe.shortlist, predicate_bias=1, alpha=0.15,
+                                    scorer=1, early_stop_mode=2)
+    pi = np.zeros((0, pipe.shortlist), np.uint32)
+    if psel.size:
+        pi, _ = O.posting_scan(codes, prep, attrs, pr, 1, h(idx.posting_ids, np.uint32), plan.posting_begin[psel],
+                               plan.posting_count[psel], pipe.shortlist)
+    cand = np.concatenate([gi, pi])
+    uniq, inv = np.unique(cand[cand != U32MAX], return_inverse=True)
+    sub = idx.base[torch.from_numpy(uniq.astype(np.int64)).to(idx.base.device)].cpu().numpy().view(np.uint16)
+    remap = np.full(cand.shape, U32MAX, np.uint32)
+    remap[cand != U32MAX] = inv.astype(np.uint32)
+    routes = {"query_row": np.concatenate([gr["query_row"], pr["query_row"]])}
+    qv = h(q.vectors[qs_rows])
+    ri, rd = O.rerank(sub, 2, qv, None, routes, remap, 10)
+    ri = np.where(ri != U32MAX, uniq[np.minimum(ri, len(uniq) - 1)], U32MAX).astype(np.uint32)
+    r2q = routes["query_row"].astype(np.int64)
+    order = np.argsort(r2q, kind="stable").astype(np.uint32)
+    qoff = np.zeros(len(sel) + 1, np.uint32)
+    qoff[1:] = np.cumsum(np.bincount(r2q, minlength=len(sel)))
+    return O.route_merge(ri, rd, qoff, order, 10)
+
+
+def run_config4(args):
+    """BASELINE configuration 4 at one GPU's shard of the 100M-vector case."""
+    import torch
+    from gofann import workload_gpu as W, workload_hybrid as WH
+    from gofann.rabitq_pipeline import RabitqPipeline
+    torch.cuda.set_device(0)
+    t0 = time.time()
+    n = args.n if args.n != 10_000_000 else 12_500_000
+    nq = args.queries
+    data = WH.generate(n=n, n_queries=nq, seed=args.seed, t0=t0)
+    idx = WH.build_index(data, seed=args.seed, t0=t0)
+    q = data["queries"]
+    plan = WH.plan_queries(idx, data, q, scan_rows=args.scan_rows)
+    WH._log(f"planned: {plan.graph_query.shape[0]} graph routes, {plan.posting_query.shape[0]} posting routes "
+            f"(fuzzy rewrite {plan.rewrite_ms:.0f} ms)", t0)
+    eval_idx = np.arange(min(args.eval if args.eval != 2000 else 1000, nq))
+    gt = WH.ground_truth(idx, data, q, plan, eval_idx)
+    WH._log(f"ground truth for {len(eval_idx)} queries", t0)
+    kinds = {nm: q.kind[eval_idx] == k for k, nm in enumerate(WH.KIND_NAMES)}
+    sweep = [args.queue_size] if args.queue_size else QUEUE_SWEEP
+    recalls, by_kind, chosen, pipe = {}, {}, None, None
+    for qs in sweep:
+        pipe = RabitqPipeline(idx, plan, qs, shortlist=100, segment_rows=args.segment_rows)
+        pipe.prepare(q.vectors)
+        ids, _ = pipe.search(q.vectors)
+        torch.cuda.synchronize()
+        pred = ids[torch.from_numpy(eval_idx).cuda()].cpu().numpy().view(np.uint32)
+        recalls[qs] = round(W.recall_at_k(pred, gt, 10), 4)
+        by_kind = {k: round(W.recall_at_k(pred[m], gt[m], 10), 4) for k, m in kinds.items() if m.any()}
+        WH._log(f"queue {qs}: recall@10 {recalls[qs]} by kind {by_kind}", t0)
+        if recalls[qs] >= args.recall:
+            chosen = qs
+            break
+    if chosen is None:
+        chosen = max(recalls, key=lambda x: recalls[x])
+        pipe = RabitqPipeline(idx, plan, chosen, shortlist=100, segment_rows=args.segment_rows)
+    stream = torch.cuda.current_stream()
+    pipe.prepare(q.vectors)
+    for _ in range(args.warmup):
+        pipe.search(q.vectors)
+    torch.cuda.synchronize()
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    p0, p1 = ev(), ev()
+    p0.record(stream)
+    for _ in range(args.steps):
+        pipe.prepare(q.vectors)
+    p1.record(stream)
+    sampler = ClockSampler(0)
+    sampler.start()
+    torch.cuda.synchronize()
+    stage = {k: [] for k in ("beam", "posting", "rerank")}
+    s0, s1 = ev(), ev()
+    s0.record(stream)
+    for _ in range(args.steps):
+        e = [ev() for _ in range(4)]
+        e[0].record(stream)
+        pipe.beam_search()
+        e[1].record(stream)
+        pipe.posting_scan()
+        e[2].record(stream)
+        pipe.rerank(q.vectors)
+        e[3].record(stream)
+        pipe.merge()
+        stage["beam"].append((e[0], e[1]))
+        stage["posting"].append((e[1], e[2]))
+        stage["rerank"].append((e[2], e[3]))
+    s1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = s0.elapsed_time(s1) / args.steps
+    prep_ms = p0.elapsed_time(p1) / args.steps
+    st_ms = {k: float(np.mean([a.elapsed_time(b) for a, b in v])) for k, v in stage.items()}
+    hq = q.vectors.cpu().pin_memory()
+    hid = torch.empty((nq, 10), dtype=torch.int32).pin_memory()
+    hd = torch.empty((nq, 10), dtype=torch.float32).pin_memory()
+    dq = torch.empty_like(q.vectors)
+    e0, e1 = ev(), ev()
+    e_steps = max(3, args.steps // 2)
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(e_steps):
+        dq.copy_(hq, non_blocking=True)
+        pipe.prepare(dq)
+        ids, d = pipe.search(dq)
+        hid.copy_(ids, non_blocking=True)
+        hd.copy_(d, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = max(e0.elapsed_time(e1), (time.perf_counter() - wall0) * 1e3) / e_steps
+    final = hid[torch.from_numpy(eval_idx)].numpy().view(np.uint32)
+    final_recall = W.recall_at_k(final, gt, 10)
+    peaks = measured_peaks()
+    dom = max(st_ms, key=lambda k: st_ms[k])
+    code = idx.padded_dim // 8 + 4 + 12 + 4
+    if dom == "beam":
+        c = pipe.g_counters[:pipe.ng].cpu().numpy().astype(np.int64)
+        bytes_dom = float(c[:, 0].sum() * (idx.adjacency.shape[1] * 4) + c[:, 1].sum() * code + c[:, 2].sum() * 64 +
+                          pipe.ng * pipe.shortlist * 8)
+    elif dom == "posting":
+        bytes_dom = float(plan.posting_count.astype(np.int64).sum() * code + pipe.npo * pipe.shortlist * 8)
+    else:
+        n_cand = int((pipe.g_ids[:pipe.ng] != -1).sum()) + int((pipe.p_ids[:pipe.npo] != -1).sum())
+        bytes_dom = float(n_cand * (idx.dim * 2 + 4) + (pipe.ng + pipe.npo) * idx.dim * 4)
+    achieved = bytes_dom / (st_ms[dom] / 1e3) / 1e9
+    line = {
+        "metric": C4_METRIC, "value": round(nq / (ms / 1e3), 1), "unit": "queries/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"config4 shard: {n} x {idx.dim} f16 (one 8-GPU shard of the 100M case), 1-bit "
+                               f"RaBitQ ({idx.padded_dim // 8} B codes), degree-32 graph; categorical / int64 range / "
+                               f"exact-string / fuzzy-string (edit distance <= 2) / hybrid AND predicates; exact "
+                               f"FP16 rerank of 100", "n_base": n, "n_queries": nq, "queue_size": chosen,
+                   "recall_at_10": round(final_recall, 4), "recall_sweep": recalls, "recall_by_kind": by_kind,
+                   "graph_routes": pipe.ng, "posting_routes": pipe.npo, "scan_rows": args.scan_rows,
+                   "fuzzy_rewrite_ms": round(plan.rewrite_ms, 1),
+                   "planning": "routing and the fuzzy rewrite run before the timed region (query preparation)",
+                   "prep_ms": round(prep_ms, 3), "stage_ms": {k: round(v, 3) for k, v in st_ms.items()},
+                   "l2_flush": "inputs larger than L2 (12.8 GB FP16 store, 0.8 GB codes)", "parallelism": "single"},
+        "e2e": {"value": round(nq / (e_ms / 1e3), 1), "unit": "queries/s",
+                "h2d_bytes_per_step": int(hq.numel() * 4), "d2h_bytes_per_step": int(nq * 10 * 8),
+                "includes": "query H2D, preparation, search, top-10 D2H"},
+        "gpu_launches": int(pipe.launches_per_run * args.steps),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "kernel": {"beam": "beam_search_kernel", "posting": "posting_scan_kernel",
+                                "rerank": "rerank_kernel"}[dom], "kernel_ms": round(st_ms[dom], 3),
+                     "algorithmic_bytes_per_launch": int(bytes_dom), "peak_source": peaks["source"]},
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline:
+        from oracle import oracle as O
+        threads = O.cpu_count()
+        rng = np.random.default_rng(1)
+        sel = np.sort(rng.choice(nq, min(nq, args.cpu_sample or 300), replace=False))
+        tt = time.perf_counter()
+        ci, cd = c4_cpu_sample(idx, plan, q, pipe, sel, chosen, threads)
+        el = time.perf_counter() - tt
+        gi, gd = pipe.out_ids.cpu().numpy().view(np.uint32)[sel], pipe.out_d.cpu().numpy()[sel]
+        line["cpu_baseline"] = {"value": round(len(sel) / el, 1), "unit": "queries/s", "cores": threads,
+                                "kind": "port", "sample": f"{len(sel)} of {nq} config-4 queries, queue {chosen}; "
+                                f"RaBitQ traversal + posting scans + FP16 rerank + merge on the GPU-prepared state, "
+                                f"{el:.1f} s on {threads} threads"}
+        rel = np.where(ci != U32MAX, np.abs(gd - cd) / np.maximum(np.abs(cd), 1e-30), 0)
+        line["parity"] = {"checked_queries": int(len(sel)), "id_mismatches": int(np.any(gi != ci, axis=1).sum()),
+                          "dist_rel_max": float(np.nanmax(rel)) if rel.size else 0.0,
+                          "tolerance": "ids equal, FP16 rerank distances within 1e-3 relative"}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.config == 1:
@@ -1181,6 +1382,11 @@ def main():
             print(json.dumps({"impl": "reference", "unavailable": "config 1 reference arm not built; run --config 2"}))
             return
         run_config1(args)
+    elif args.config == 4:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "config 4 reference arm not built; run --config 2"}))
+            return
+        run_config4(args)
     elif args.config == 3:
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "config 3 reference arm not built; run --config 2"}))

@@ -37,6 +37,8 @@ class RabitqPipeline:
         self.graph = {"adjacency": idx.adjacency, "row_to_sample": torch.arange(idx.n, dtype=torch.int32, device=d),
                       "label_offset": torch.zeros(1, dtype=torch.int32, device=d)}
         self.attrs = {"label_indptr": idx.set_indptr, "label_indices": idx.set_indices, "range_values": idx.attr}
+        self.attrs.update(idx.extra_attrs)
+        self.base_dtype = A.DTYPE_F16 if idx.base.dtype == torch.float16 else A.DTYPE_F32
         self.codes = {"rq_codes": idx.codes, "rq_factors": idx.factors, "rq_anchor_ids": idx.anchor_ids,
                       "num_anchors": na}
         self.gs, self.at, self.cs = A.fill_graph(self.graph), A.fill_attrs(self.attrs), A.fill_codes(self.codes)
@@ -151,12 +153,13 @@ class RabitqPipeline:
         s = stream_handle(stream)
         idx, k = self.idx, self.topk
         if self.ng:
-            A.check(self.L.gofann_rerank(A.ptr(idx.base), A.DTYPE_F32, idx.n, idx.dim, A.ptr(queries), C.byref(self.at),
-                                         C.byref(self.grs), A.ptr(self.g_ids), self.shortlist, k, A.ptr(self.r_ids),
+            A.check(self.L.gofann_rerank(A.ptr(idx.base), self.base_dtype, idx.n, idx.dim, A.ptr(queries),
+                                         C.byref(self.at), C.byref(self.grs), A.ptr(self.g_ids), self.shortlist, k,
+                                         A.ptr(self.r_ids),
                                          A.ptr(self.r_d), s), "gofann_rerank(graph)")
         if self.npo:
-            A.check(self.L.gofann_rerank(A.ptr(idx.base), A.DTYPE_F32, idx.n, idx.dim, A.ptr(queries), C.byref(self.at),
-                                         C.byref(self.prs), A.ptr(self.p_ids), self.shortlist, k,
+            A.check(self.L.gofann_rerank(A.ptr(idx.base), self.base_dtype, idx.n, idx.dim, A.ptr(queries),
+                                         C.byref(self.at), C.byref(self.prs), A.ptr(self.p_ids), self.shortlist, k,
                                          A.ptr(self.r_ids[self.ng:]), A.ptr(self.r_d[self.ng:]), s),
                     "gofann_rerank(posting)")
 

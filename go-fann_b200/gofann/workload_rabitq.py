@@ -94,6 +94,7 @@ class RqIndex:
     order_base: int              # offset of the attribute order in posting_ids
     range_index: object          # the FARPIDX1 range postings (range_postings.Index)
     stats: dict = field(default_factory=dict)
+    extra_attrs: dict = field(default_factory=dict)  # further gofann_attrs arrays (strings, int64 values)
 
 
 def _mixture(g, centres, bases, comp, spread, noise):
@@ -197,7 +198,7 @@ def _window_knn(base: torch.Tensor, order: torch.Tensor, k: int, tile=1024, wind
     for q0 in range(0, n, tile):
         q1 = min(n, q0 + tile)
         w0, w1 = max(0, q0 - half), min(n, q1 + half)
-        xw = base[order[w0:w1]]
+        xw = base[order[w0:w1]].float()
         sq = xw.square().sum(1)
         xq, sqq = xw[q0 - w0:q1 - w0], sq[q0 - w0:q1 - w0]
         d = sqq[:, None] + sq[None, :] - 2.0 * (xq @ xw.T)
@@ -208,14 +209,19 @@ def _window_knn(base: torch.Tensor, order: torch.Tensor, k: int, tile=1024, wind
     return out
 
 
-def build_index(data: dict, degree=32, n_random=8, seed=0, t0=None, chunk=1 << 18) -> RqIndex:
+def build_index(data: dict, degree=32, n_random=8, seed=0, t0=None, chunk=1 << 18, normalize_anchors=True,
+                range_postings=True) -> RqIndex:
+    """RaBitQ index of data["base"] (f32, or f16 read in f32 chunks): anchors
+    = the mixture centres (normalised when the base is), codes, factors,
+    graph, membership postings and (range_postings) the FARPIDX1 order of the
+    float attribute."""
     t0 = t0 or time.time()
     base = data["base"]
     n, dim = base.shape
     dev = base.device
     p = ((dim + 63) // 64) * 64
     rot = random_rotation(p, seed, dev)[:dim].contiguous()  # [dim][p]
-    anchors = torch.nn.functional.normalize(data["centres"], dim=1)
+    anchors = torch.nn.functional.normalize(data["centres"], dim=1) if normalize_anchors else data["centres"]
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = True
     try:
@@ -223,7 +229,7 @@ def build_index(data: dict, degree=32, n_random=8, seed=0, t0=None, chunk=1 << 1
         an = anchors.square().sum(1)
         aid = torch.empty(n, dtype=torch.int64, device=dev)
         for s in range(0, n, chunk):
-            aid[s:s + chunk] = (an - 2.0 * base[s:s + chunk] @ anchors.T).argmin(1)
+            aid[s:s + chunk] = (an - 2.0 * base[s:s + chunk].float() @ anchors.T).argmin(1)
         ranchors = rotate(anchors, rot, A.GEMM_TF32X3)
         codes = torch.empty((n, p // 8), dtype=torch.uint8, device=dev)
         factors = torch.empty((n, 3), dtype=torch.float32, device=dev)
@@ -231,7 +237,7 @@ def build_index(data: dict, degree=32, n_random=8, seed=0, t0=None, chunk=1 << 1
         aid32 = aid.to(torch.int32)
         for s in range(0, n, chunk):
             e = min(n, s + chunk)
-            res = rotate(base[s:e], rot, A.GEMM_TF32)
+            res = rotate(base[s:e].float().contiguous(), rot, A.GEMM_TF32)
             res -= ranchors[aid[s:e]]
             A.check(L.gofann_rabitq_encode(A.ptr(res), A.ptr(ranchors), A.ptr(aid32[s:e]), e - s, p,
                                            A.ptr(codes[s:e]), A.ptr(factors[s:e]), _stream()), "gofann_rabitq_encode")
@@ -240,7 +246,8 @@ def build_index(data: dict, degree=32, n_random=8, seed=0, t0=None, chunk=1 << 1
         _log(f"rotation, anchors ({anchors.shape[0]}), RaBitQ 1-bit codes ({p // 8} B) and factors", t0)
         # global graph: order by anchor then a random projection, window k-NN
         gp = torch.Generator(device=dev).manual_seed(seed + 11)
-        proj = base @ torch.randn((dim, 1), generator=gp, device=dev)
+        rvec = torch.randn((dim, 1), generator=gp, device=dev)
+        proj = torch.cat([base[s0:s0 + chunk].float() @ rvec for s0 in range(0, n, chunk)])
         pr = proj.squeeze(1).double()
         order = torch.argsort(aid.double() * 1e3 + (pr - pr.min()))
         inv = torch.empty_like(order)
@@ -272,12 +279,14 @@ def build_index(data: dict, degree=32, n_random=8, seed=0, t0=None, chunk=1 << 1
         dup |= (rnd.unsqueeze(2) == adj[:, :n_near].to(torch.int64).unsqueeze(1)).any(2)
         dup |= rnd == torch.arange(n, device=dev).unsqueeze(1)
         adj[:, n_near:] = torch.where(dup, torch.full_like(rnd, -1), rnd).to(torch.int32)
-        mean = base.mean(0)
-        seed_row = int((base - mean).square().sum(1).argmin())
+        mean = base.mean(0, dtype=torch.float32)
+        dm = torch.cat([(base[s0:s0 + chunk].float() - mean).square().sum(1) for s0 in range(0, n, chunk)])
+        seed_row = int(dm.argmin())
+        del dm
         # entry row per anchor: its nearest member
         dist_a = torch.empty(n, device=dev)
         for s0 in range(0, n, chunk):
-            x = base[s0:s0 + chunk]
+            x = base[s0:s0 + chunk].float()
             dist_a[s0:s0 + chunk] = (x - anchors[aid[s0:s0 + chunk]]).square().sum(1)
         key = aid.double() * 1e6 + dist_a.double()
         first = torch.argsort(key)[start[cnt > 0]] if bool((cnt > 0).any()) else torch.zeros(0, dtype=torch.int64)
@@ -290,14 +299,17 @@ def build_index(data: dict, degree=32, n_random=8, seed=0, t0=None, chunk=1 << 1
         torch.backends.cuda.matmul.allow_tf32 = prev
     # ordered range postings: written as a FARPIDX1 file and loaded back the
     # way the reference maps its ordered_postings.bin
-    attr = data["attr"]
-    rdir = tempfile.mkdtemp(prefix="gofann_rp_")
-    rpath = os.path.join(rdir, "ordered_postings.bin")
-    RP.write(rpath, attr.cpu().numpy())
-    rindex = RP.load(rpath)
-    order_attr = torch.from_numpy(rindex.dimensions[0].sample_ids.astype(np.int64)).to(dev)
-    posting_ids = torch.cat([data["postings"], order_attr.to(torch.int32)])
-    _log(f"range postings {rpath}: {rindex.dimensions[0].unique_values.shape[0]} distinct values", t0)
+    attr = data.get("attr")
+    rindex = None
+    posting_ids = data["postings"]
+    if range_postings:
+        rdir = tempfile.mkdtemp(prefix="gofann_rp_")
+        rpath = os.path.join(rdir, "ordered_postings.bin")
+        RP.write(rpath, attr.cpu().numpy())
+        rindex = RP.load(rpath)
+        order_attr = torch.from_numpy(rindex.dimensions[0].sample_ids.astype(np.int64)).to(dev)
+        posting_ids = torch.cat([data["postings"], order_attr.to(torch.int32)])
+        _log(f"range postings {rpath}: {rindex.dimensions[0].unique_values.shape[0]} distinct values", t0)
     return RqIndex(n=n, dim=dim, padded_dim=p, base=base, attr=attr, set_indptr=data["set_indptr"],
                    set_indices=data["set_indices"], rotation=rot, anchors=ranchors, codes=codes, factors=factors,
                    anchor_ids=aid32, adjacency=adj, seed=seed_row, anchor_entry=anchor_entry, posting_ids=posting_ids,
