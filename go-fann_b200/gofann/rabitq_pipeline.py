@@ -23,6 +23,30 @@ from .engine import _t, stream_handle
 from .workload_rabitq import RqIndex, RqPlan
 
 
+PER_ROUTE = ("query_row", "group_id", "start_local", "filter_bits", "primary_label", "pred_enabled",
+             "route_compiled")
+
+
+def _segment_routes(routes: dict, sel: np.ndarray) -> dict:
+    """Route tables of the segments, segment j scanning for route sel[j]:
+    per-route arrays gathered; with one DNF clause per route (pred_offsets =
+    0..n) the clauses and their extensions gathered as well, the atom arrays
+    they index shared."""
+    out = {}
+    one_clause = "pred_offsets" in routes and np.array_equal(routes["pred_offsets"],
+                                                             np.arange(routes["query_row"].shape[0] + 1))
+    if "pred_offsets" in routes and not one_clause:
+        raise ValueError("segmented scans need one predicate clause per route")
+    for k, v in routes.items():
+        if k in PER_ROUTE or (one_clause and k in ("clauses", "pred_ext")):
+            out[k] = np.ascontiguousarray(v[sel])
+        elif k == "pred_offsets":
+            out[k] = np.arange(sel.shape[0] + 1, dtype=np.uint32)
+        else:
+            out[k] = v
+    return out
+
+
 class RabitqPipeline:
     def __init__(self, idx: RqIndex, plan: RqPlan, queue_size: int, shortlist: int = 200, topk: int = 10,
                  alpha: float = 0.15, entries: bool = True, segment_rows: int = 0):
@@ -53,7 +77,7 @@ class RabitqPipeline:
         if segment_rows and npo:
             sp = RP.make_plan(np.arange(npo), plan.posting_begin, plan.posting_count, segment_rows)
             sel = sp.query_positions.astype(np.int64)
-            seg_routes = {k: _t(np.ascontiguousarray(v[sel]), d) for k, v in plan.posting_routes.items()}
+            seg_routes = {k: _t(v, d) for k, v in _segment_routes(plan.posting_routes, sel).items()}
             nseg = int(sel.shape[0])
             self.seg = {"routes": seg_routes, "rs": A.fill_routes(seg_routes), "n": nseg,
                         "begin": _t(sp.offsets, d), "count": _t(sp.sizes.astype(np.uint32), d),
