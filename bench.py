@@ -71,7 +71,7 @@ def parse():
     ap.add_argument("--mode", default="pq", choices=["pq", "exact"],
                     help="config 2: PQ navigation + exact rerank (pq), or the Full-GPU exact-distance mode (exact: "
                          "traversal and posting scans on the exact distances of the HBM-resident base vectors)")
-    ap.add_argument("--scan-rows", type=int, default=20_000,
+    ap.add_argument("--scan-rows", type=int, default=50_000,
                     help="config 4: tag postings and int64 range slices of at most this many rows are scanned")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4],
                     help="BASELINE configuration: 2 (10M x 192 u8, PQ; the default) or 3 (2.7M x 4096 f32, RaBitQ)")
@@ -1239,7 +1239,8 @@ def run_config4(args):
     q = data["queries"]
     plan = WH.plan_queries(idx, data, q, scan_rows=args.scan_rows)
     WH._log(f"planned: {plan.graph_query.shape[0]} graph routes, {plan.posting_query.shape[0]} posting routes "
-            f"(fuzzy rewrite {plan.rewrite_ms:.0f} ms)", t0)
+            f"scanning {int(plan.posting_count.astype(np.int64).sum())} rows (fuzzy rewrite {plan.rewrite_ms:.0f} ms)",
+            t0)
     eval_idx = np.arange(min(args.eval if args.eval != 2000 else 1000, nq))
     gt = WH.ground_truth(idx, data, q, plan, eval_idx)
     WH._log(f"ground truth for {len(eval_idx)} queries", t0)
@@ -1247,7 +1248,7 @@ def run_config4(args):
     sweep = [args.queue_size] if args.queue_size else QUEUE_SWEEP
     recalls, by_kind, chosen, pipe = {}, {}, None, None
     for qs in sweep:
-        pipe = RabitqPipeline(idx, plan, qs, shortlist=100, segment_rows=args.segment_rows)
+        pipe = RabitqPipeline(idx, plan, qs, shortlist=200, segment_rows=args.segment_rows)
         pipe.prepare(q.vectors)
         ids, _ = pipe.search(q.vectors)
         torch.cuda.synchronize()
@@ -1260,7 +1261,7 @@ def run_config4(args):
             break
     if chosen is None:
         chosen = max(recalls, key=lambda x: recalls[x])
-        pipe = RabitqPipeline(idx, plan, chosen, shortlist=100, segment_rows=args.segment_rows)
+        pipe = RabitqPipeline(idx, plan, chosen, shortlist=200, segment_rows=args.segment_rows)
     stream = torch.cuda.current_stream()
     pipe.prepare(q.vectors)
     for _ in range(args.warmup):
@@ -1337,7 +1338,7 @@ def run_config4(args):
         "config": {"workload": f"config4 shard: {n} x {idx.dim} f16 (one 8-GPU shard of the 100M case), 1-bit "
                                f"RaBitQ ({idx.padded_dim // 8} B codes), degree-32 graph; categorical / int64 range / "
                                f"exact-string / fuzzy-string (edit distance <= 2) / hybrid AND predicates; exact "
-                               f"FP16 rerank of 100", "n_base": n, "n_queries": nq, "queue_size": chosen,
+                               f"FP16 rerank of 200", "n_base": n, "n_queries": nq, "queue_size": chosen,
                    "recall_at_10": round(final_recall, 4), "recall_sweep": recalls, "recall_by_kind": by_kind,
                    "graph_routes": pipe.ng, "posting_routes": pipe.npo, "scan_rows": args.scan_rows,
                    "fuzzy_rewrite_ms": round(plan.rewrite_ms, 1),

@@ -24,16 +24,20 @@ share when the base set is split by contiguous id range over 8 B200s:
     25 % hybrid AND (a tag and an int64 range);
   * planning (the reference's categorical / range access split,
     dataloader.cpp:11862, and its fuzzy rewrite into an OR of exact terms,
-    dataloader.cpp:2973-3010): a tag with at most `scan_rows` rows scans its
-    posting, otherwise the global graph runs with the tag as a label atom; a
-    range of at most `scan_rows` rows scans its slice of the int64 order,
-    otherwise the graph runs with an int64 atom; a hybrid query scans the
-    smaller of its tag posting and range slice when it is small enough, the
-    other atom as the residual; an exact string scans its rows; a fuzzy
-    string is rewritten on the device into the dictionary strings within
-    the edit distance (the device's bit-parallel check, gofann_predicate_
-    pass_masks over the dictionary) and scans their rows, one posting route
-    each, merged per query with a fuzzy atom as the residual;
+    dataloader.cpp:2973-3010): a term whose rows number at most `scan_rows`
+    is scanned, a more frequent one runs the global graph with the term as
+    a DNF atom.  A tag scans its posting, a range its slice of the int64
+    order.  A string term is first resolved to dictionary strings -- the
+    exact string, or for a fuzzy term the strings within the edit distance,
+    found on the device (gofann_predicate_pass_masks runs the bit-parallel
+    check over the dictionary) -- whose row groups are scanned, one posting
+    route each, merged per query (the rows match, so no residual), or, when
+    they hold more than `scan_rows` rows, the graph runs with the exact or
+    fuzzy atom.  A hybrid query scans the smaller of its tag posting and
+    range slice (the other atom as the residual) when that side is short,
+    or when the conjunction is expected to match fewer than `selective_rows`
+    rows and the side has at most `max_scan_rows`; otherwise the graph runs
+    with both atoms;
   * ground truth: exact filtered top-10 of FP32 distances over the FP16 base.
 """
 from __future__ import annotations
@@ -274,9 +278,10 @@ def fuzzy_rewrite(data: dict, strings: list, max_edits: int = 2, device="cuda") 
         A.check(L.gofann_predicate_pass_masks(C.byref(gs), C.byref(at), C.byref(rs), A.ptr(d_cr), A.ptr(d_cand), m,
                                               A.ptr(masks), None, torch.cuda.current_stream().cuda_stream),
                 "gofann_predicate_pass_masks(fuzzy rewrite)")
-        bits = np.unpackbits(masks.cpu().numpy().view(np.uint8), bitorder="little")[:m].astype(bool)
+        hit = np.nonzero(np.unpackbits(masks.cpu().numpy().view(np.uint8), bitorder="little")[:m])[0]
+        cuts = np.searchsorted(cr[hit], np.arange(n + 1))  # cr is grouped by query
         for j, i in enumerate(cq):
-            out[i] = cand[bits & (cr == j)].astype(np.int64)
+            out[i] = cand[hit[cuts[j]:cuts[j + 1]]].astype(np.int64)
     return out
 
 
@@ -343,7 +348,8 @@ def _tables(rows: list, n_str_bytes=None):
             "pred_string_peq": np.stack(peqs) if peqs else np.zeros((1, 128), np.uint32)}
 
 
-def plan_queries(idx: WR.RqIndex, data: dict, q: HyQueries, scan_rows=20_000) -> HyPlan:
+def plan_queries(idx: WR.RqIndex, data: dict, q: HyQueries, scan_rows=50_000, selective_rows=5_000,
+                 max_scan_rows=1_000_000) -> HyPlan:
     t0 = time.perf_counter()
     fuzzy = [b if k == 3 else b"" for b, k in zip(q.string, q.kind)]
     matches = fuzzy_rewrite(data, fuzzy)
@@ -376,7 +382,11 @@ def plan_queries(idx: WR.RqIndex, data: dict, q: HyQueries, scan_rows=20_000) ->
                 g_rows.append((i, idx.seed, [], int_atom, [])); g_q.append(i)
         elif k == 4:
             tc, rc = card[q.tag[i]], hi - lo
-            if min(tc, rc) <= scan_rows:
+            # a conjunction expected to match few rows is scanned from its
+            # smaller side even when that side is long (graph traversals
+            # under very selective predicates wander)
+            est = tc * rc / max(1, idx.n)
+            if min(tc, rc) <= scan_rows or (est < selective_rows and min(tc, rc) <= max_scan_rows):
                 if tc <= rc:
                     p_rows.append((i, 0, [], int_atom, [])); p_b.append(tbeg[q.tag[i]]); p_c.append(tc)
                 else:
@@ -384,14 +394,17 @@ def plan_queries(idx: WR.RqIndex, data: dict, q: HyQueries, scan_rows=20_000) ->
                 p_q.append(i)
             else:
                 g_rows.append((i, idx.seed, tag_atom, int_atom, [])); g_q.append(i)
-        else:  # exact or fuzzy string: scan the rows of each matching dictionary string
-            atom = [(A.STRING_EXACT if k == 2 else A.STRING_FUZZY, q.string[i])]
-            for sid in matches[i]:
-                c = int(st["string_count"][sid])
-                if c == 0:
-                    continue
-                p_rows.append((i, 0, [], [], atom)); p_q.append(i)
-                p_b.append(st["string_order_base"] + int(st["string_begin"][sid])); p_c.append(c)
+        else:  # exact or fuzzy string: the rows of each matching dictionary string
+            counts = st["string_count"][matches[i]] if len(matches[i]) else np.zeros(0, np.int64)
+            if counts.sum() <= scan_rows:
+                for sid, c in zip(matches[i], counts):  # the rows match: no residual
+                    if c == 0:
+                        continue
+                    p_rows.append((i, 0, [], [], [])); p_q.append(i)
+                    p_b.append(st["string_order_base"] + int(st["string_begin"][sid])); p_c.append(int(c))
+            else:  # a popular string: the graph with the string atom
+                atom = [(A.STRING_EXACT if k == 2 else A.STRING_FUZZY, q.string[i])]
+                g_rows.append((i, idx.seed, [], [], atom)); g_q.append(i)
     graph = _tables(g_rows)
     post = _tables(p_rows)
     return HyPlan(graph, np.asarray(g_q, np.uint32), post, np.asarray(p_q, np.uint32),
