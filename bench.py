@@ -71,9 +71,9 @@ def parse():
     ap.add_argument("--mode", default="pq", choices=["pq", "exact"],
                     help="config 2: PQ navigation + exact rerank (pq), or the Full-GPU exact-distance mode (exact: "
                          "traversal and posting scans on the exact distances of the HBM-resident base vectors)")
-    ap.add_argument("--scan-rows", type=int, default=50_000,
+    ap.add_argument("--scan-rows", type=int, default=150_000,
                     help="config 4: tag postings and int64 range slices of at most this many rows are scanned")
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4],
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
                     help="BASELINE configuration: 2 (10M x 192 u8, PQ; the default) or 3 (2.7M x 4096 f32, RaBitQ)")
     return ap.parse_args()
 
@@ -1225,36 +1225,101 @@ def c4_cpu_sample(idx, plan, q, pipe, sel, qs, threads):
     return O.route_merge(ri, rd, qoff, order, 10)
 
 
-def run_config4(args):
-    """BASELINE configuration 4 at one GPU's shard of the 100M-vector case."""
+def _c4_setup(args, t0):
+    """Process group (several ranks), this rank's shard of the config-4
+    workload, its index and plan; the ground truth of the eval queries
+    merged over all shards (on rank 0)."""
     import torch
-    from gofann import workload_gpu as W, workload_hybrid as WH
-    from gofann.rabitq_pipeline import RabitqPipeline
-    torch.cuda.set_device(0)
-    t0 = time.time()
-    n = args.n if args.n != 10_000_000 else 12_500_000
-    nq = args.queries
-    data = WH.generate(n=n, n_queries=nq, seed=args.seed, t0=t0)
+    import torch.distributed as dist
+    from gofann import workload_hybrid as WH
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=900))
+    n = args.n if args.n != 10_000_000 else 12_500_000  # rows per shard: one eighth of the 100M case
+    data = WH.generate(device=device, n=n, n_queries=args.queries, seed=args.seed, t0=t0, shard=rank)
     idx = WH.build_index(data, seed=args.seed, t0=t0)
+    return world, rank, local, device, n, data, idx
+
+
+def _c4_gt(idx, data, q, plan, eval_idx, world, rank, shard_base, device):
+    """Exact filtered top-10 over every shard (rank 0 returns it)."""
+    import torch
+    import torch.distributed as dist
+    from gofann import workload_hybrid as WH
+    gi, gd = WH.ground_truth(idx, data, q, plan, eval_idx, with_dists=True)
+    gi = np.where(gi != U32MAX, gi.astype(np.int64) + shard_base, U32MAX)
+    if world == 1:
+        return gi.astype(np.uint32)
+    ti = torch.from_numpy(gi).to(device)
+    td = torch.from_numpy(gd).to(device)
+    ai = torch.zeros((world,) + ti.shape, dtype=ti.dtype, device=device)
+    ad = torch.zeros((world,) + td.shape, dtype=td.dtype, device=device)
+    dist.all_gather_into_tensor(ai, ti)
+    dist.all_gather_into_tensor(ad, td)
+    if rank != 0:
+        return None
+    ai = ai.cpu().numpy().transpose(1, 0, 2).reshape(len(eval_idx), -1)
+    ad = ad.cpu().numpy().transpose(1, 0, 2).reshape(len(eval_idx), -1)
+    out = np.full((len(eval_idx), 10), U32MAX, np.uint32)
+    for r in range(len(eval_idx)):
+        ok = ai[r] != U32MAX
+        o = np.lexsort((ai[r][ok], ad[r][ok]))[:10]
+        out[r, :len(o)] = ai[r][ok][o]
+    return out
+
+
+def run_config4(args):
+    """one shard of the 100M-vector case per GPU
+    (12.5M rows each; 8 ranks hold the whole case), replicated queries,
+    per-shard search, one all-gather of the top-10 and a device merge."""
+    import torch
+    import torch.distributed as dist
+    from gofann import workload_gpu as W, workload_hybrid as WH
+    from gofann.engine import stream_handle
+    from gofann.rabitq_pipeline import RabitqPipeline
+    from gofann.sharding import ShardExchange
+    t0 = time.time()
+    world, rank, local, device, n, data, idx = _c4_setup(args, t0)
+    nq = args.queries
+    shard_base = rank * n
     q = data["queries"]
     plan = WH.plan_queries(idx, data, q, scan_rows=args.scan_rows)
     WH._log(f"planned: {plan.graph_query.shape[0]} graph routes, {plan.posting_query.shape[0]} posting routes "
             f"scanning {int(plan.posting_count.astype(np.int64).sum())} rows (fuzzy rewrite {plan.rewrite_ms:.0f} ms)",
             t0)
     eval_idx = np.arange(min(args.eval if args.eval != 2000 else 1000, nq))
-    gt = WH.ground_truth(idx, data, q, plan, eval_idx)
+    gt = _c4_gt(idx, data, q, plan, eval_idx, world, rank, shard_base, device)
     WH._log(f"ground truth for {len(eval_idx)} queries", t0)
     kinds = {nm: q.kind[eval_idx] == k for k, nm in enumerate(WH.KIND_NAMES)}
+    xchg = ShardExchange(world, nq, 10, device) if world > 1 else None
+
+    def search(pipe, queries):
+        ids, d = pipe.search(queries)
+        if world == 1:
+            return ids, d
+        return xchg.exchange(ids, d, shard_base, stream_handle())
+
     sweep = [args.queue_size] if args.queue_size else QUEUE_SWEEP
     recalls, by_kind, chosen, pipe = {}, {}, None, None
     for qs in sweep:
         pipe = RabitqPipeline(idx, plan, qs, shortlist=200, segment_rows=args.segment_rows)
         pipe.prepare(q.vectors)
-        ids, _ = pipe.search(q.vectors)
+        ids, _ = search(pipe, q.vectors)
         torch.cuda.synchronize()
-        pred = ids[torch.from_numpy(eval_idx).cuda()].cpu().numpy().view(np.uint32)
-        recalls[qs] = round(W.recall_at_k(pred, gt, 10), 4)
-        by_kind = {k: round(W.recall_at_k(pred[m], gt[m], 10), 4) for k, m in kinds.items() if m.any()}
+        r = 0.0
+        if rank == 0:
+            pred = ids[torch.from_numpy(eval_idx).to(device)].cpu().numpy().view(np.uint32)
+            r = W.recall_at_k(pred, gt, 10)
+            by_kind = {k: round(W.recall_at_k(pred[m], gt[m], 10), 4) for k, m in kinds.items() if m.any()}
+        rr = torch.tensor([r], device=device)
+        if world > 1:
+            dist.broadcast(rr, 0)
+        recalls[qs] = round(float(rr.item()), 4)
         WH._log(f"queue {qs}: recall@10 {recalls[qs]} by kind {by_kind}", t0)
         if recalls[qs] >= args.recall:
             chosen = qs
@@ -1265,7 +1330,7 @@ def run_config4(args):
     stream = torch.cuda.current_stream()
     pipe.prepare(q.vectors)
     for _ in range(args.warmup):
-        pipe.search(q.vectors)
+        search(pipe, q.vectors)
     torch.cuda.synchronize()
     ev = lambda: torch.cuda.Event(enable_timing=True)
     p0, p1 = ev(), ev()
@@ -1273,14 +1338,20 @@ def run_config4(args):
     for _ in range(args.steps):
         pipe.prepare(q.vectors)
     p1.record(stream)
-    sampler = ClockSampler(0)
-    sampler.start()
     torch.cuda.synchronize()
-    stage = {k: [] for k in ("beam", "posting", "rerank")}
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    names = ["beam", "posting", "rerank", "route_merge"] + (["shard_exchange"] if world > 1 else [])
+    stage = {k: [] for k in names}
     s0, s1 = ev(), ev()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     s0.record(stream)
     for _ in range(args.steps):
-        e = [ev() for _ in range(4)]
+        e = [ev() for _ in range(len(names) + 1)]
         e[0].record(stream)
         pipe.beam_search()
         e[1].record(stream)
@@ -1289,15 +1360,27 @@ def run_config4(args):
         pipe.rerank(q.vectors)
         e[3].record(stream)
         pipe.merge()
-        stage["beam"].append((e[0], e[1]))
-        stage["posting"].append((e[1], e[2]))
-        stage["rerank"].append((e[2], e[3]))
+        e[4].record(stream)
+        if world > 1:
+            xchg.exchange(pipe.out_ids, pipe.out_d, shard_base, stream_handle())
+            e[5].record(stream)
+        for j, k in enumerate(names):
+            stage[k].append((e[j], e[j + 1]))
     s1.record(stream)
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     clocks = sampler.stop()
     ms = s0.elapsed_time(s1) / args.steps
     prep_ms = p0.elapsed_time(p1) / args.steps
-    st_ms = {k: float(np.mean([a.elapsed_time(b) for a, b in v])) for k, v in stage.items()}
+    st = torch.tensor([float(np.mean([a.elapsed_time(b) for a, b in stage[k]])) for k in names] + [ms, prep_ms],
+                      device=device)
+    st_min = st.clone()
+    if world > 1:
+        dist.all_reduce(st, op=dist.ReduceOp.MAX)
+        dist.all_reduce(st_min, op=dist.ReduceOp.MIN)
+    st_ms = {k: float(st[j]) for j, k in enumerate(names)}
+    ms, prep_ms = float(st[-2]), float(st[-1])
     hq = q.vectors.cpu().pin_memory()
     hid = torch.empty((nq, 10), dtype=torch.int32).pin_memory()
     hd = torch.empty((nq, 10), dtype=torch.float32).pin_memory()
@@ -1305,21 +1388,25 @@ def run_config4(args):
     e0, e1 = ev(), ev()
     e_steps = max(3, args.steps // 2)
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     wall0 = time.perf_counter()
     e0.record(stream)
     for _ in range(e_steps):
         dq.copy_(hq, non_blocking=True)
         pipe.prepare(dq)
-        ids, d = pipe.search(dq)
+        ids, d = search(pipe, dq)
         hid.copy_(ids, non_blocking=True)
         hd.copy_(d, non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
     e_ms = max(e0.elapsed_time(e1), (time.perf_counter() - wall0) * 1e3) / e_steps
-    final = hid[torch.from_numpy(eval_idx)].numpy().view(np.uint32)
-    final_recall = W.recall_at_k(final, gt, 10)
+    te = torch.tensor([e_ms], device=device)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e_ms = float(te[0])
     peaks = measured_peaks()
-    dom = max(st_ms, key=lambda k: st_ms[k])
+    dom = max(("beam", "posting", "rerank"), key=lambda k: st_ms[k])
     code = idx.padded_dim // 8 + 4 + 12 + 4
     if dom == "beam":
         c = pipe.g_counters[:pipe.ng].cpu().numpy().astype(np.int64)
@@ -1330,50 +1417,189 @@ def run_config4(args):
     else:
         n_cand = int((pipe.g_ids[:pipe.ng] != -1).sum()) + int((pipe.p_ids[:pipe.npo] != -1).sum())
         bytes_dom = float(n_cand * (idx.dim * 2 + 4) + (pipe.ng + pipe.npo) * idx.dim * 4)
-    achieved = bytes_dom / (st_ms[dom] / 1e3) / 1e9
-    line = {
-        "metric": C4_METRIC, "value": round(nq / (ms / 1e3), 1), "unit": "queries/s", "n_gpus": 1,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": f"config4 shard: {n} x {idx.dim} f16 (one 8-GPU shard of the 100M case), 1-bit "
-                               f"RaBitQ ({idx.padded_dim // 8} B codes), degree-32 graph; categorical / int64 range / "
-                               f"exact-string / fuzzy-string (edit distance <= 2) / hybrid AND predicates; exact "
-                               f"FP16 rerank of 200", "n_base": n, "n_queries": nq, "queue_size": chosen,
-                   "recall_at_10": round(final_recall, 4), "recall_sweep": recalls, "recall_by_kind": by_kind,
-                   "graph_routes": pipe.ng, "posting_routes": pipe.npo, "scan_rows": args.scan_rows,
-                   "fuzzy_rewrite_ms": round(plan.rewrite_ms, 1),
-                   "planning": "routing and the fuzzy rewrite run before the timed region (query preparation)",
-                   "prep_ms": round(prep_ms, 3), "stage_ms": {k: round(v, 3) for k, v in st_ms.items()},
-                   "l2_flush": "inputs larger than L2 (12.8 GB FP16 store, 0.8 GB codes)", "parallelism": "single"},
-        "e2e": {"value": round(nq / (e_ms / 1e3), 1), "unit": "queries/s",
-                "h2d_bytes_per_step": int(hq.numel() * 4), "d2h_bytes_per_step": int(nq * 10 * 8),
-                "includes": "query H2D, preparation, search, top-10 D2H"},
-        "gpu_launches": int(pipe.launches_per_run * args.steps),
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
-                     "kernel": {"beam": "beam_search_kernel", "posting": "posting_scan_kernel",
-                                "rerank": "rerank_kernel"}[dom], "kernel_ms": round(st_ms[dom], 3),
-                     "algorithmic_bytes_per_launch": int(bytes_dom), "peak_source": peaks["source"]},
-        "clocks": clocks,
-    }
-    if not args.no_cpu_baseline:
-        from oracle import oracle as O
-        threads = O.cpu_count()
-        rng = np.random.default_rng(1)
-        sel = np.sort(rng.choice(nq, min(nq, args.cpu_sample or 300), replace=False))
-        tt = time.perf_counter()
-        ci, cd = c4_cpu_sample(idx, plan, q, pipe, sel, chosen, threads)
-        el = time.perf_counter() - tt
-        gi, gd = pipe.out_ids.cpu().numpy().view(np.uint32)[sel], pipe.out_d.cpu().numpy()[sel]
-        line["cpu_baseline"] = {"value": round(len(sel) / el, 1), "unit": "queries/s", "cores": threads,
-                                "kind": "port", "sample": f"{len(sel)} of {nq} config-4 queries, queue {chosen}; "
-                                f"RaBitQ traversal + posting scans + FP16 rerank + merge on the GPU-prepared state, "
-                                f"{el:.1f} s on {threads} threads"}
-        rel = np.where(ci != U32MAX, np.abs(gd - cd) / np.maximum(np.abs(cd), 1e-30), 0)
-        line["parity"] = {"checked_queries": int(len(sel)), "id_mismatches": int(np.any(gi != ci, axis=1).sum()),
-                          "dist_rel_max": float(np.nanmax(rel)) if rel.size else 0.0,
-                          "tolerance": "ids equal, FP16 rerank distances within 1e-3 relative"}
-    print(json.dumps(line), flush=True)
+    achieved = bytes_dom / (float(np.mean([a.elapsed_time(b) for a, b in stage[dom]])) / 1e3) / 1e9
+    if rank == 0:
+        final = hid[torch.from_numpy(eval_idx)].numpy().view(np.uint32)
+        final_recall = W.recall_at_k(final, gt, 10)
+        line = {
+            "metric": C4_METRIC, "value": round(nq / (ms / 1e3), 1), "unit": "queries/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": f"config4: {world} shard(s) of {n} x {idx.dim} f16 (12.5M rows per GPU: 8 GPUs "
+                                   f"hold the 100M case), 1-bit RaBitQ ({idx.padded_dim // 8} B codes), degree-32 "
+                                   f"graphs; categorical / int64 range / exact-string / fuzzy-string (edit distance "
+                                   f"<= 2) / hybrid AND predicates; exact FP16 rerank of 200",
+                       "n_base": n * world, "n_base_per_gpu": n, "n_queries": nq, "queue_size": chosen,
+                       "recall_at_10": round(final_recall, 4), "recall_sweep": recalls, "recall_by_kind": by_kind,
+                       "graph_routes_rank0": pipe.ng, "posting_routes_rank0": pipe.npo, "scan_rows": args.scan_rows,
+                       "fuzzy_rewrite_ms": round(plan.rewrite_ms, 1),
+                       "planning": "routing and the fuzzy rewrite run before the timed region (query preparation)",
+                       "prep_ms": round(prep_ms, 3), "stage_ms": {k: round(v, 3) for k, v in st_ms.items()},
+                       "stage_ms_min_rank": {k: round(float(st_min[j]), 3) for j, k in enumerate(names)},
+                       "l2_flush": "inputs larger than L2 (12.8 GB FP16 store, 0.8 GB codes per GPU)",
+                       "parallelism": f"shard{world}" if world > 1 else "single"},
+            "e2e": {"value": round(nq / (e_ms / 1e3), 1), "unit": "queries/s",
+                    "h2d_bytes_per_step": int(hq.numel() * 4), "d2h_bytes_per_step": int(nq * 10 * 8),
+                    "includes": "query H2D, preparation, search, top-10 D2H"},
+            "gpu_launches": int((pipe.launches_per_run + (2 if world > 1 else 0)) * args.steps),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                         "kernel": {"beam": "beam_search_kernel", "posting": "posting_scan_kernel",
+                                    "rerank": "rerank_kernel"}[dom], "kernel_ms": round(st_ms[dom], 3),
+                         "algorithmic_bytes_per_launch": int(bytes_dom), "peak_source": peaks["source"]},
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            from oracle import oracle as O
+            threads = O.cpu_count()
+            rng = np.random.default_rng(1)
+            sel = np.sort(rng.choice(nq, min(nq, args.cpu_sample or 300), replace=False))
+            tt = time.perf_counter()
+            ci, cd = c4_cpu_sample(idx, plan, q, pipe, sel, chosen, threads)
+            el = time.perf_counter() - tt
+            gi, gd = pipe.out_ids.cpu().numpy().view(np.uint32)[sel], pipe.out_d.cpu().numpy()[sel]
+            line["cpu_baseline"] = {"value": round(len(sel) / el, 1), "unit": "queries/s", "cores": threads,
+                                    "kind": "port", "sample": f"{len(sel)} of {nq} config-4 queries, queue {chosen}; "
+                                    f"RaBitQ traversal + posting scans + FP16 rerank + merge on the GPU-prepared "
+                                    f"state, {el:.1f} s on {threads} threads"}
+            rel = np.where(ci != U32MAX, np.abs(gd - cd) / np.maximum(np.abs(cd), 1e-30), 0)
+            line["parity"] = {"checked_queries": int(len(sel)),
+                              "id_mismatches": int(np.any(gi != ci, axis=1).sum()),
+                              "dist_rel_max": float(np.nanmax(rel)) if rel.size else 0.0,
+                              "tolerance": "ids equal, FP16 rerank distances within 1e-3 relative"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+C5_METRIC = "filtered QPS @ recall@10=0.95 (config 5 sweep, batch 100k, all selectivities)"
+
+
+def run_config5(args):
+    """the config-4 shards at 1/2/4/8 GPUs, an int64
+    range filter swept over selectivities 1e-5 ... 0.5, batches of 1k, 10k and
+    100k queries, QPS at recall@10 = 0.9 / 0.95 / 0.99 (the smallest queue of
+    the sweep reaching each), and the per-shard top-k merge cost (all-gather
+    + gofann_shard_merge) at N > 1."""
+    import torch
+    import torch.distributed as dist
+    from gofann import workload_gpu as W, workload_hybrid as WH
+    from gofann.engine import stream_handle
+    from gofann.rabitq_pipeline import RabitqPipeline
+    from gofann.sharding import ShardExchange
+    t0 = time.time()
+    world, rank, local, device, n, data, idx = _c4_setup(args, t0)
+    shard_base = rank * n
+    q0 = data["queries"]
+    nq = q0.kind.shape[0]
+    batches = [b for b in (1_000, 10_000, 100_000) if b <= nq]
+    targets = (0.9, 0.95, 0.99)
+    rng = np.random.default_rng(args.seed + 101)
+    stream = torch.cuda.current_stream()
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    cells, merge_ms = [], {}
+    sampler = ClockSampler(local)
+    sampler.start()
+    for sel in WH.SELECTIVITIES:
+        lower = (rng.random(nq) * (1.0 - sel) * WH.INT_SPAN).astype(np.int64)
+        upper = lower + np.maximum(1, int(sel * WH.INT_SPAN))
+        q = WH.HyQueries(q0.vectors, np.ones(nq, np.int64), np.zeros(nq, np.int64), lower, upper, [b""] * nq)
+        plans = {b: WH.plan_queries(idx, data, WH.HyQueries(q.vectors[:b], q.kind[:b], q.tag[:b], q.lower[:b],
+                                                            q.upper[:b], q.string[:b]), scan_rows=args.scan_rows)
+                 for b in batches}
+        eval_idx = np.arange(min(500, nq))
+        gt = _c4_gt(idx, data, q, plans[batches[-1]], eval_idx, world, rank, shard_base, device)
+        xch = {b: ShardExchange(world, b, 10, device) if world > 1 else None for b in batches}
+
+        def timed(pipe, b, steps):
+            vecs = q.vectors[:b]
+            pipe.prepare(vecs)
+            for _ in range(2):
+                pipe.search(vecs)
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1, m0, m1 = ev(), ev(), ev(), ev()
+            e0.record(stream)
+            for _ in range(steps):
+                pipe.search(vecs)
+                if world > 1:
+                    m0.record(stream)
+                    xch[b].exchange(pipe.out_ids, pipe.out_d, shard_base, stream_handle())
+                    m1.record(stream)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) / steps, m0.elapsed_time(m1) if world > 1 else 0.0],
+                             device=device)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t[0]), float(t[1])
+
+        reached, row = {}, {"selectivity": sel}
+        big = batches[-1]
+        for qs in QUEUE_SWEEP:
+            pipe = RabitqPipeline(idx, plans[big], qs, shortlist=200, segment_rows=args.segment_rows)
+            pipe.prepare(q.vectors[:big])
+            ids, _ = pipe.search(q.vectors[:big])
+            if world > 1:
+                ids, _ = xch[big].exchange(ids, pipe.out_d, shard_base, stream_handle())
+            torch.cuda.synchronize()
+            r = 0.0
+            if rank == 0:
+                r = W.recall_at_k(ids[torch.from_numpy(eval_idx).to(device)].cpu().numpy().view(np.uint32), gt, 10)
+            rr = torch.tensor([r], device=device)
+            if world > 1:
+                dist.broadcast(rr, 0)
+            r = float(rr.item())
+            for t in targets:
+                if t not in reached and r >= t:
+                    reached[t] = (qs, r)
+            if len(reached) == len(targets):
+                break
+        for t in targets:
+            if t not in reached:
+                row[f"recall_{t}"] = None
+                continue
+            qs, r = reached[t]
+            cell = {"queue": qs, "recall": round(r, 4)}
+            for b in batches:
+                pipe = RabitqPipeline(idx, plans[b], qs, shortlist=200, segment_rows=args.segment_rows)
+                ms, mm = timed(pipe, b, max(3, args.steps // 2))
+                cell[f"qps_batch_{b}"] = round(b / (ms / 1e3), 1)
+                if world > 1:
+                    merge_ms.setdefault(b, []).append(mm)
+            row[f"recall_{t}"] = cell
+        cells.append(row)
+        if rank == 0:
+            WH._log(f"selectivity {sel}: {row}", t0)
+    clocks = sampler.stop()
+    if rank == 0:
+        big = batches[-1]
+        tot_q = tot_s = 0.0
+        for row in cells:
+            c = row.get("recall_0.95")
+            if c:
+                tot_q += big
+                tot_s += big / c[f"qps_batch_{big}"]
+        value = tot_q / tot_s if tot_s else None
+        line = {
+            "metric": C5_METRIC, "value": round(value, 1) if value else None, "unit": "queries/s", "n_gpus": world,
+            "steps": max(3, args.steps // 2), "warmup": 2, "ms_per_step": round(1e3 * big / value, 3) if value else None,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": f"config5: config-4 shards ({n} x 512 f16 per GPU, {world} GPU(s)), int64 range "
+                                   f"filter swept over selectivities, batches {batches}, QPS at recall@10 0.9 / "
+                                   f"0.95 / 0.99", "n_base": n * world, "sweep": cells,
+                       "value_definition": "queries / time over the selectivities at recall 0.95, batch 100k",
+                       "shard_merge_ms": {str(b): round(float(np.mean(v)), 3) for b, v in merge_ms.items()},
+                       "scan_rows": args.scan_rows, "parallelism": f"shard{world}" if world > 1 else "single",
+                       "l2_flush": "inputs larger than L2"},
+            "gpu_launches": None, "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def main():
@@ -1383,6 +1609,11 @@ def main():
             print(json.dumps({"impl": "reference", "unavailable": "config 1 reference arm not built; run --config 2"}))
             return
         run_config1(args)
+    elif args.config == 5:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "config 5 reference arm not built; run --config 2"}))
+            return
+        run_config5(args)
     elif args.config == 4:
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "config 4 reference arm not built; run --config 2"}))

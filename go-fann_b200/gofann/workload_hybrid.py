@@ -38,6 +38,10 @@ share when the base set is split by contiguous id range over 8 B200s:
     or when the conjunction is expected to match fewer than `selective_rows`
     rows and the side has at most `max_scan_rows`; otherwise the graph runs
     with both atoms;
+  * several GPUs: rank r holds shard r (its own rows, index and plan; the
+    shared centres, dictionary and queries come from the common seed), and
+    the per-shard top-10 are exchanged and merged (gofann_shard_merge), so
+    8 ranks hold the 100M-vector case;
   * ground truth: exact filtered top-10 of FP32 distances over the FP16 base.
 """
 from __future__ import annotations
@@ -119,23 +123,29 @@ def _mutate(s: bytes, edits: int, rng) -> bytes:
 
 
 def generate(device="cuda", seed=0, n=12_500_000, dim=512, n_centres=16_384, rank=32, spread=4.0, noise=0.1,
-             vocab=50_000, max_tags=10, n_strings=200_000, n_queries=100_000, t0=None):
+             vocab=50_000, max_tags=10, n_strings=200_000, n_queries=100_000, t0=None, shard=0):
+    """Shard `shard` (n rows) of the workload.  Everything shared by the
+    shards -- mixture centres, the string dictionary and its popularity,
+    the queries -- comes from a generator seeded with `seed` alone, so every
+    rank builds the same queries; the shard's rows come from a generator
+    seeded with (seed, shard)."""
     t0 = t0 or time.time()
     g = torch.Generator(device=device).manual_seed(seed)
+    gs = torch.Generator(device=device).manual_seed(seed * 1_000_003 + 7919 * (shard + 1))
     centres = torch.randn((n_centres, dim), generator=g, device=device)
     bases = torch.linalg.qr(torch.randn((64, dim, rank), generator=g, device=device))[0].contiguous()
     base = torch.empty((n, dim), dtype=torch.float16, device=device)
     chunk = 1 << 18
     for s in range(0, n, chunk):
         e = min(n, s + chunk)
-        comp = torch.randint(0, n_centres, (e - s,), generator=g, device=device)
-        base[s:e] = WR._mixture(g, centres, bases, comp, spread, noise).to(torch.float16)
-    _log(f"base {n} x {dim} f16 ({base.numel() * 2 / 1e9:.1f} GB)", t0)
+        comp = torch.randint(0, n_centres, (e - s,), generator=gs, device=device)
+        base[s:e] = WR._mixture(gs, centres, bases, comp, spread, noise).to(torch.float16)
+    _log(f"base {n} x {dim} f16 ({base.numel() * 2 / 1e9:.1f} GB), shard {shard}", t0)
     # tags: 1..max_tags per row, Zipf(1.1) over the vocabulary
     pz = _zipf_probs(vocab, 1.1, device)
-    per = torch.randint(1, max_tags + 1, (n,), generator=g, device=device)
+    per = torch.randint(1, max_tags + 1, (n,), generator=gs, device=device)
     rows = torch.repeat_interleave(torch.arange(n, device=device, dtype=torch.int64), per)
-    vals = torch.cat([torch.multinomial(pz, int(min(1 << 24, rows.numel() - s)), replacement=True, generator=g)
+    vals = torch.cat([torch.multinomial(pz, int(min(1 << 24, rows.numel() - s)), replacement=True, generator=gs)
                       for s in range(0, rows.numel(), 1 << 24)])
     key = torch.unique((rows << 16) | vals)
     rows_u, vals_u = key >> 16, (key & 0xFFFF).to(torch.int32)
@@ -150,31 +160,30 @@ def generate(device="cuda", seed=0, n=12_500_000, dim=512, n_centres=16_384, ran
     begin[1:] = np.cumsum(card)[:-1]
     _log(f"{int(vals_u.numel())} tags over {vocab} values", t0)
     # int64 attribute
-    ival = torch.randint(0, INT_SPAN, (n, 1), generator=g, device=device, dtype=torch.int64)
+    ival = torch.randint(0, INT_SPAN, (n, 1), generator=gs, device=device, dtype=torch.int64)
     # strings: a dictionary, each row one of its strings (Zipf over rows)
     dict_b, dict_l = _dictionary(g, n_strings, device)
-    sid = torch.multinomial(_zipf_probs(n_strings, 1.1, device), n, replacement=True, generator=g)
+    pstr = _zipf_probs(n_strings, 1.1, device)
     perm = torch.randperm(n_strings, generator=g, device=device)  # popularity independent of dictionary order
-    sid = perm[sid]
+    sid = perm[torch.multinomial(pstr, n, replacement=True, generator=gs)]
     lens = torch.from_numpy(dict_l).to(device)[sid]
     soff = torch.zeros(n + 1, dtype=torch.int64, device=device)
     soff[1:] = torch.cumsum(lens, 0)
     db = torch.from_numpy(dict_b).to(device)
     sbytes = db[sid][torch.arange(32, device=device)[None, :] < lens[:, None]]
     _log(f"strings: {n_strings} distinct, {int(soff[-1]) / 1e9:.2f} GB of bytes", t0)
-    # queries
+    # queries (shared by every shard): tags and strings drawn by the rows'
+    # own popularity distributions
     rng = np.random.default_rng(seed + 29)
     qc = torch.randint(0, n_centres, (n_queries,), generator=g, device=device)
     qv = WR._mixture(g, centres, bases, qc, spread, noise)
     kind = rng.choice(5, size=n_queries, p=[0.25, 0.20, 0.15, 0.15, 0.25])
-    ip = indptr.cpu().numpy()
-    host_row = rng.integers(0, n, n_queries)
-    pick = ip[host_row] + (rng.random(n_queries) * (ip[host_row + 1] - ip[host_row])).astype(np.int64)
-    tag = vals_u[torch.from_numpy(pick).to(device)].cpu().numpy().astype(np.int64)
+    # a row carries a tag about once per draw: its frequency follows pz
+    tag = torch.multinomial(pz, n_queries, replacement=True, generator=g).cpu().numpy().astype(np.int64)
     sel = np.asarray(SELECTIVITIES)[rng.integers(0, len(SELECTIVITIES), n_queries)]
     lower = (rng.random(n_queries) * (1.0 - sel) * INT_SPAN).astype(np.int64)
     upper = lower + np.maximum(1, (sel * INT_SPAN).astype(np.int64))
-    sid_h = sid[torch.from_numpy(rng.integers(0, n, n_queries)).to(device)].cpu().numpy()
+    sid_h = perm[torch.multinomial(pstr, n_queries, replacement=True, generator=g)].cpu().numpy()
     strings = []
     for i in range(n_queries):
         if kind[i] in (2, 3):
@@ -348,7 +357,7 @@ def _tables(rows: list, n_str_bytes=None):
             "pred_string_peq": np.stack(peqs) if peqs else np.zeros((1, 128), np.uint32)}
 
 
-def plan_queries(idx: WR.RqIndex, data: dict, q: HyQueries, scan_rows=50_000, selective_rows=5_000,
+def plan_queries(idx: WR.RqIndex, data: dict, q: HyQueries, scan_rows=150_000, selective_rows=5_000,
                  max_scan_rows=1_000_000) -> HyPlan:
     t0 = time.perf_counter()
     fuzzy = [b if k == 3 else b"" for b, k in zip(q.string, q.kind)]
@@ -413,7 +422,7 @@ def plan_queries(idx: WR.RqIndex, data: dict, q: HyQueries, scan_rows=50_000, se
 
 
 def ground_truth(idx: WR.RqIndex, data: dict, q: HyQueries, plan: HyPlan, sample: np.ndarray, k=10,
-                 chunk=1 << 20) -> np.ndarray:
+                 chunk=1 << 20, with_dists=False):
     """Exact filtered top-k (FP32 distances of the FP16 rows, ties by id):
     the rows passing each query's predicate, found from the attribute
     arrays (tags from the CSR, int64 values, string ids; a fuzzy term's
@@ -426,6 +435,7 @@ def ground_truth(idx: WR.RqIndex, data: dict, q: HyQueries, plan: HyPlan, sample
     ival = data["ival"][:, 0]
     tag_post = idx.posting_ids
     out = np.full((len(sample), k), A.U32MAX, np.uint32)
+    out_d = np.full((len(sample), k), np.inf, np.float32)
     for r, i in enumerate(sample):
         kd = int(q.kind[i])
         if kd in (0, 4):
@@ -456,4 +466,5 @@ def ground_truth(idx: WR.RqIndex, data: dict, q: HyQueries, plan: HyPlan, sample
         ids_h, dd = best_i.cpu().numpy(), best_d.cpu().numpy()
         o = np.lexsort((ids_h, dd))
         out[r, :len(o)] = ids_h[o]
-    return out
+        out_d[r, :len(o)] = dd[o]
+    return (out, out_d) if with_dists else out
