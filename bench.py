@@ -62,9 +62,10 @@ def parse():
     ap.add_argument("--cpu-sample", type=int, default=0, help="queries in the CPU baseline sample (0 = auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--segment-rows", type=int, default=4096,
-                    help="config 3: posting and range slices are scanned in segments of at most this many rows "
-                         "and merged per route (0 = one block per slice)")
+    ap.add_argument("--segment-rows", type=int, default=None,
+                    help="configs 3-5: posting and range slices are scanned in segments of at most this many rows "
+                         "and merged per route (0 = one block per slice; default 4096 for config 3, where few long "
+                         "slices need the parallelism, and 0 for configs 4 and 5, whose many routes fill the GPU)")
     ap.add_argument("--range-scan-rows", type=int, default=30_000,
                     help="config 3: a range predicate of at most this many rows scans its slice, a wider one "
                          "traverses the graph")
@@ -1030,6 +1031,8 @@ def run_config1(args):
 
 def run_config3(args):
     import torch
+    if args.segment_rows is None:
+        args.segment_rows = 4096
     from gofann import workload_rabitq as WR
     from gofann.rabitq_pipeline import RabitqPipeline
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1284,6 +1287,8 @@ def run_config4(args):
     from gofann.rabitq_pipeline import RabitqPipeline
     from gofann.sharding import ShardExchange
     t0 = time.time()
+    if args.segment_rows is None:
+        args.segment_rows = 0
     world, rank, local, device, n, data, idx = _c4_setup(args, t0)
     nq = args.queries
     shard_base = rank * n
@@ -1489,6 +1494,8 @@ def run_config5(args):
     from gofann.rabitq_pipeline import RabitqPipeline
     from gofann.sharding import ShardExchange
     t0 = time.time()
+    if args.segment_rows is None:
+        args.segment_rows = 0
     world, rank, local, device, n, data, idx = _c4_setup(args, t0)
     shard_base = rank * n
     q0 = data["queries"]

@@ -88,12 +88,13 @@ struct TopKState {
     int n_buf;
     float thr_d;
     uint32_t thr_id;
+    int fresh;  // 1 until the first merge: the top-k holds only the fill
 };
 
 __device__ __forceinline__ void topk_reset(const TopK& t, TopKState& st, int tid)
 {
     for (int i = tid; i < t.keep; i += kScanThreads) { t.sd[i] = FLT_MAX; t.sid[i] = kU32Max; }
-    if (tid == 0) { st.n_buf = 0; st.thr_d = FLT_MAX; st.thr_id = kU32Max; }
+    if (tid == 0) { st.n_buf = 0; st.thr_d = FLT_MAX; st.thr_id = kU32Max; st.fresh = 1; }
     __syncthreads();
 }
 
@@ -109,15 +110,36 @@ __device__ __forceinline__ void topk_offer(const TopK& t, TopKState& st, float t
     }
 }
 
-// Sorts the top-k and `n_buf` buffered pairs (block-uniform n_buf).
+// Sorts the top-k and `n_buf` buffered pairs (block-uniform n_buf).  At
+// the first merge the top-k holds only the fill, so only the buffer is
+// sorted (in place, padded with the fill to a power of two) and its first
+// `keep` pairs become the top-k: a short route sorts its own candidates
+// instead of keep + n_buf pairs.
 __device__ __forceinline__ void topk_merge(const TopK& t, TopKState& st, int n_buf, int tid)
 {
+    const int fresh = st.fresh;
+    const int nb2 = static_cast<int>(next_pow2(static_cast<uint32_t>(n_buf)));
+    if (fresh && t.keep + nb2 <= kSortSize) {
+        float* bd = t.sd + t.keep;
+        uint32_t* bi = t.sid + t.keep;
+        for (int i = n_buf + tid; i < nb2; i += kScanThreads) { bd[i] = FLT_MAX; bi[i] = kU32Max; }
+        __syncthreads();
+        bitonic_sort_pairs(bd, bi, nb2, tid);
+        for (int i = tid; i < t.keep; i += kScanThreads) {
+            t.sd[i] = i < nb2 ? bd[i] : FLT_MAX;
+            t.sid[i] = i < nb2 ? bi[i] : kU32Max;
+        }
+        __syncthreads();
+        if (tid == 0) { st.n_buf = 0; st.thr_d = t.sd[t.k - 1]; st.thr_id = t.sid[t.k - 1]; st.fresh = 0; }
+        __syncthreads();
+        return;
+    }
     const int n = t.keep + n_buf;
     const int np2 = static_cast<int>(next_pow2(static_cast<uint32_t>(n)));
     for (int i = n + tid; i < np2; i += kScanThreads) { t.sd[i] = FLT_MAX; t.sid[i] = kU32Max; }
     __syncthreads();
     bitonic_sort_pairs(t.sd, t.sid, np2, tid);
-    if (tid == 0) { st.n_buf = 0; st.thr_d = t.sd[t.k - 1]; st.thr_id = t.sid[t.k - 1]; }
+    if (tid == 0) { st.n_buf = 0; st.thr_d = t.sd[t.k - 1]; st.thr_id = t.sid[t.k - 1]; st.fresh = 0; }
     __syncthreads();
 }
 
