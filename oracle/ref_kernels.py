@@ -374,3 +374,46 @@ def block_pickup_cases(keys: np.ndarray, used: np.ndarray, sizes: np.ndarray, de
         raise RuntimeError(f"gofann_ref_block_pickup_cases returned {st}")
     torch.cuda.synchronize()
     return out.cpu().numpy()
+
+
+# ------------------------------------------------- the RaBitQ estimator
+RQ_LIB = HERE / "_ref" / "libgofann_ref_rabitq.so"
+_Q = None
+
+
+def rq_available() -> bool:
+    return RQ_LIB.exists()
+
+
+def run_reference_rq_score(case: dict, device="cuda") -> np.ndarray:
+    """The reference's score_rabitq_code_device<true> on a
+    tests/ref_rabitq_cases.py case: one estimate per (row, point) pair."""
+    import torch
+    global _Q
+    if _Q is None:
+        L = C.CDLL(str(RQ_LIB))
+        L.gofann_ref_rq_score.argtypes = [_P] * 9 + [_U32, _U32, _U32, _P]
+        L.gofann_ref_rq_score.restype = C.c_int
+        _Q = L
+    keep = []
+
+    def d(x):
+        x = np.ascontiguousarray(x)
+        if x.dtype == np.uint32:
+            x = x.view(np.int32)
+        t = torch.from_numpy(x).to(device)
+        keep.append(t)
+        return t.data_ptr()
+
+    n = int(case["pair_row"].shape[0])
+    out = torch.empty(n, dtype=torch.float32, device=device)
+    st = _Q.gofann_ref_rq_score(d(case["anchor_ids"]), d(case["codes"]), d(case["factors"]), d(case["k1"]),
+                                d(case["gdist"]), d(case["q8"]), d(case["scale"]), d(case["pair_row"]),
+                                d(case["pair_point"]), n, int(case["num_anchors"]), int(case["padded_dim"]),
+                                out.data_ptr())
+    if st != 0:
+        raise RuntimeError(f"gofann_ref_rq_score returned {st}")
+    torch.cuda.synchronize()
+    res = out.cpu().numpy()
+    del keep
+    return res
