@@ -471,27 +471,37 @@ __device__ __forceinline__ uint32_t myers_edit_distance(const uint32_t* __restri
 }
 
 // String and integer atoms of clause `ci` for `sample` (all must hold).
-__device__ __forceinline__ bool ext_atoms_match(const gofann_routes& r, const AttrView& a, uint32_t ci,
-                                                uint32_t sample)
+// Not inlined, and given plain pointers: the traversal's step loop calls it
+// only for routes whose clauses carry such atoms, and neither its code nor
+// a copy of the descriptors enters the hot loop.
+static __device__ __noinline__ bool ext_atoms_match(const gofann_clause_ext* __restrict__ ext,
+                                                    const gofann_int_atom* __restrict__ int_atoms,
+                                                    const gofann_string_atom* __restrict__ str_atoms,
+                                                    const uint8_t* __restrict__ str_query,
+                                                    const uint32_t* __restrict__ peq_rows,
+                                                    const int64_t* __restrict__ ints, uint32_t int_count,
+                                                    const uint64_t* __restrict__ str_offsets,
+                                                    const uint8_t* __restrict__ str_bytes, uint32_t ci,
+                                                    uint32_t sample)
 {
-    const gofann_clause_ext x = r.pred_ext[ci];
+    const gofann_clause_ext x = ext[ci];
     for (uint32_t j = x.int_begin; j < x.int_end; ++j) {
-        const gofann_int_atom at = r.pred_ints[j];
+        const gofann_int_atom at = int_atoms[j];
         if (at.mode == 0) continue;
-        if (a.ints == nullptr || at.dimension >= a.int_count) return false;
-        const int64_t v = a.ints[static_cast<uint64_t>(sample) * a.int_count + at.dimension];
+        if (ints == nullptr || at.dimension >= int_count) return false;
+        const int64_t v = ints[static_cast<uint64_t>(sample) * int_count + at.dimension];
         const bool ok = at.mode == 1 ? v > at.lower : at.mode == 2 ? v < at.upper
                                                      : at.mode == 3 ? (v >= at.lower && v < at.upper) : false;
         if (!ok) return false;
     }
     if (x.string_begin == x.string_end) return true;
-    if (a.str_offsets == nullptr) return false;
-    const uint64_t sb = a.str_offsets[sample], se = a.str_offsets[sample + 1];
-    const uint8_t* text = a.str_bytes + sb;
+    if (str_offsets == nullptr) return false;
+    const uint64_t sb = str_offsets[sample], se = str_offsets[sample + 1];
+    const uint8_t* text = str_bytes + sb;
     const uint32_t n = static_cast<uint32_t>(se - sb);
     for (uint32_t j = x.string_begin; j < x.string_end; ++j) {
-        const gofann_string_atom at = r.pred_strings[j];
-        const uint8_t* q = r.pred_string_bytes + at.offset;
+        const gofann_string_atom at = str_atoms[j];
+        const uint8_t* q = str_query + at.offset;
         if (at.kind == GOFANN_STRING_EXACT) {
             if (n != at.length) return false;
             for (uint32_t i = 0; i < n; ++i)
@@ -499,12 +509,17 @@ __device__ __forceinline__ bool ext_atoms_match(const gofann_routes& r, const At
         } else {
             const uint32_t gap = n > at.length ? n - at.length : at.length - n;
             if (gap > at.max_edits || at.length > GOFANN_FUZZY_MAX_LENGTH) return false;
-            if (myers_edit_distance(r.pred_string_peq + static_cast<size_t>(j) * 128, at.length, text, n) >
-                at.max_edits)
+            if (myers_edit_distance(peq_rows + static_cast<size_t>(j) * 128, at.length, text, n) > at.max_edits)
                 return false;
         }
     }
     return true;
+}
+__device__ __forceinline__ bool ext_atoms_match(const gofann_routes& r, const AttrView& a, uint32_t ci,
+                                                uint32_t sample)
+{
+    return ext_atoms_match(r.pred_ext, r.pred_ints, r.pred_strings, r.pred_string_bytes, r.pred_string_peq, a.ints,
+                           a.int_count, a.str_offsets, a.str_bytes, ci, sample);
 }
 
 // gpu_predicate::matches with clauses (gpu_predicate_index.cuh:109-136),

@@ -217,3 +217,20 @@ def test_oracle_full_pickup_matches_reference_block_pickup():
     vals = np.arange(keys.shape[1], dtype=np.uint32)[None, :] | (used.astype(np.uint32) << 31)
     mine = np.array([O.full_pickup_index(keys[c], vals[c], int(sizes[c])) for c in range(keys.shape[0])])
     assert np.array_equal(mine, FG["pickup/picked"])
+
+
+# ---- the reference's 1-bit RaBitQ estimator, recorded on a B200
+# (tests/golden/make_ref_rabitq_golden.py over tests/ref_rabitq_cases.py)
+RQ = np.load(Path.parent / "reference_rabitq_score.npz")
+
+
+@pytest.mark.parametrize("pd", (128, 512, 4096))
+def test_oracle_replays_reference_rabitq_estimator(pd):
+    """The oracle's combine order, fma(f_rescale, fma(ip, scale, k1xsumq),
+    f_add + gdist), gives the reference kernel's estimate bits on 6,000
+    pairs per padded dim."""
+    import ref_rabitq_cases as R
+    c = R.build_case(pd)
+    assert bytes(RQ[f"pd{pd}/digest"]).hex() == R.case_digest(c)
+    est, _ = O.rabitq_score(R.codes_dict(c), R.prep_dict(c), c["pair_row"], c["pair_point"])
+    assert np.array_equal(bits(est), RQ[f"pd{pd}/est_bits"])
