@@ -280,7 +280,7 @@ struct WarpBufs {
 };
 
 // One route from its seed to its shortlist.
-template <int kScorer, bool kBias, int kMode, int kW, int kMaxM>
+template <int kScorer, bool kBias, int kMode, int kW, int kMaxM, bool kExt>
 __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
                                           const Scorer<kScorer, kMode, kW, kMaxM>& score, uint32_t route,
                                           uint32_t label_offset, uint32_t begin_id, uint64_t qbit, bool pred_on,
@@ -345,7 +345,7 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
         kp.first = start;
         kp.second = begin_id;
         kp.base = start;
-        if (kBias && pred_on && pred_matches(a.routes, a.attrs, route, begin_sample)) kp.second |= kPassBit;
+        if (kBias && pred_on && pred_matches<kExt>(a.routes, a.attrs, route, begin_sample)) kp.second |= kPassBit;
         h.key[1] = kp.first; h.val[1] = kp.second; h.base[1] = kp.base;
         st.heap_size = 2;
         hash_add(hash, begin_id);
@@ -420,7 +420,7 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
                 if (kBias)
                     nfr = (st.now.second & kPassBit) ? 1 : 2;
                 else
-                    nfr = pred_matches(a.routes, a.attrs, route, sample) ? 1 : 2;
+                    nfr = pred_matches<kExt>(a.routes, a.attrs, route, sample) ? 1 : 2;
                 ++st.n_probe;
             } else if (!a.routes.route_compiled || !a.routes.route_compiled[route]) {
                 nfr = (nfr == 1 && bit_match && exact_range) ? 1 : 2;
@@ -532,12 +532,12 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
                         const uint32_t* lab = inl ? reinterpret_cast<const uint32_t*>(rec + meta_off + 16)
                                                   : a.attrs.indices;
                         const uint64_t lb = inl ? 0ull : meta.y;
-                        pass = pred_matches_row(a.routes, a.attrs, route, meta.x, lab, lb, lb + meta.z);
+                        pass = pred_matches_row<kExt>(a.routes, a.attrs, route, meta.x, lab, lb, lb + meta.z);
                     }
                     d = score.code_row(a.codes, rec);
                 } else {
                     const uint32_t smp = ldg_u32(a.graph.row_to_sample + label_offset + list[i], stream);
-                    if (kBias && pred_on) pass = pred_matches(a.routes, a.attrs, route, smp);
+                    if (kBias && pred_on) pass = pred_matches<kExt>(a.routes, a.attrs, route, smp);
                     d = score(a.codes, smp);
                 }
                 const float pr = (kBias && pred_on) ? pred_priority(d, st.penalty, pass) : d;
@@ -727,7 +727,7 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
     __syncwarp();
 }
 
-template <int kScorer, bool kBias, int kMode, int kW, int kMaxM>
+template <int kScorer, bool kBias, int kMode, int kW, int kMaxM, bool kExt>
 __global__ void __launch_bounds__(block_warps<kMode>() * 32, min_blocks<kMode>()) beam_search_kernel(BeamArgs a)
 {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -825,7 +825,7 @@ __global__ void __launch_bounds__(block_warps<kMode>() * 32, min_blocks<kMode>()
         }
         __syncwarp();
 
-        run_route<kScorer, kBias, kMode, kW, kMaxM>(a, w, score, route, label_offset, begin_id, qbit, pred_on, deg,
+        run_route<kScorer, kBias, kMode, kW, kMaxM, kExt>(a, w, score, route, label_offset, begin_id, qbit, pred_on, deg,
                                                     stream, lane);
     }
 }
@@ -834,11 +834,12 @@ using KernelFn = void (*)(BeamArgs);
 
 // Variant pickers, one per file that instantiates them.  w4: 4-wide
 // subvectors (vector loads / the chunked u8 scorer); small_m: pq_dim <= 64
-// (a shorter unrolled subspace loop).
-KernelFn pick_u8(bool bias, bool w4, bool small_m);
-KernelFn pick_direct(bool bias, bool w4, bool small_m);
-KernelFn pick_table(bool shared, bool bias, bool small_m);
-KernelFn pick_rabitq(bool bias);
+// (a shorter unrolled subspace loop); ext: the routes' clauses may carry
+// string and integer atoms.
+KernelFn pick_u8(bool bias, bool w4, bool small_m, bool ext);
+KernelFn pick_direct(bool bias, bool w4, bool small_m, bool ext);
+KernelFn pick_table(bool shared, bool bias, bool small_m, bool ext);
+KernelFn pick_rabitq(bool bias, bool ext);
 
 }  // namespace beam
 }  // namespace gofann

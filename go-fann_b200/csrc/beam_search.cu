@@ -17,14 +17,16 @@ using beam::kMaxBlockWarps;
 using beam::kU8BlockWarps;
 using beam::kWarpsPerBlock;
 
-KernelFn pick_kernel(int scorer, bool bias, int pq_mode, bool w4, bool small_m)
+// ext: the routes' clauses carry string / integer atoms (a variant without
+// their check otherwise)
+KernelFn pick_kernel(int scorer, bool bias, int pq_mode, bool w4, bool small_m, bool ext)
 {
-    if (scorer != GOFANN_SCORER_PQ) return beam::pick_rabitq(bias);
+    if (scorer != GOFANN_SCORER_PQ) return beam::pick_rabitq(bias, ext);
     switch (pq_mode) {
-    case GOFANN_PQ_U8: return beam::pick_u8(bias, w4, small_m);
-    case GOFANN_PQ_DIRECT: return beam::pick_direct(bias, w4, small_m);
-    case GOFANN_PQ_LUT_SHARED: return beam::pick_table(true, bias, small_m);
-    default: return beam::pick_table(false, bias, small_m);
+    case GOFANN_PQ_U8: return beam::pick_u8(bias, w4, small_m, ext);
+    case GOFANN_PQ_DIRECT: return beam::pick_direct(bias, w4, small_m, ext);
+    case GOFANN_PQ_LUT_SHARED: return beam::pick_table(true, bias, small_m, ext);
+    default: return beam::pick_table(false, bias, small_m, ext);
     }
 }
 
@@ -185,7 +187,8 @@ int plan_launch(const gofann_graph* graph, const gofann_attrs* attrs, const gofa
     const size_t smem = args.block_smem + static_cast<size_t>(L.total) * wpb;
     if (smem > kMaxSmem)
         return fail(GOFANN_ERR_UNSUPPORTED, "%s: %zu bytes of shared memory per warp exceed 227 KB", who, smem);
-    const KernelFn kern = pick_kernel(p.scorer, p.predicate_bias != 0, pq_mode, w4, small_m);
+    const KernelFn kern = pick_kernel(p.scorer, p.predicate_bias != 0, pq_mode, w4, small_m,
+                                      routes->pred_offsets != nullptr && routes->pred_ext != nullptr);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return cuda_status(e, "beam_search: shared memory attribute");
     int per_sm = 0;

@@ -5,9 +5,10 @@
 namespace gofann {
 namespace beam {
 
-KernelFn pick_rabitq(bool bias)
+KernelFn pick_rabitq(bool bias, bool ext)
 {
-    return bias ? beam_search_kernel<1, true, 0, 0, 64> : beam_search_kernel<1, false, 0, 0, 64>;
+    if (ext) return bias ? beam_search_kernel<1, true, 0, 0, 64, true> : beam_search_kernel<1, false, 0, 0, 64, true>;
+    return bias ? beam_search_kernel<1, true, 0, 0, 64, false> : beam_search_kernel<1, false, 0, 0, 64, false>;
 }
 
 }  // namespace beam

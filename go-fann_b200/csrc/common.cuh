@@ -525,7 +525,10 @@ __device__ __forceinline__ bool ext_atoms_match(const gofann_routes& r, const At
 // gpu_predicate::matches with clauses (gpu_predicate_index.cuh:109-136),
 // given the sample's sorted label row labels[lbegin, lend) (the CSR's
 // indices, or a copy of the row), then the clause's string and integer
-// atoms when the routes carry them.
+// atoms when the routes carry them (kExt: traversal variants compiled with
+// kExt = false serve routes without such atoms, with no trace of the check
+// in their code).
+template <bool kExt = true>
 __device__ __forceinline__ bool pred_matches_row(const gofann_routes& r, const AttrView& a, uint32_t route,
                                                  uint32_t sample, const uint32_t* labels, uint64_t lbegin,
                                                  uint64_t lend)
@@ -543,13 +546,14 @@ __device__ __forceinline__ bool pred_matches_row(const gofann_routes& r, const A
                    range_match(at.mode, at.lower, at.upper,
                                a.ranges[static_cast<uint64_t>(sample) * a.range_count + at.dimension]);
         }
-        if (pass && r.pred_ext) pass = ext_atoms_match(r, a, i, sample);
+        if (kExt && pass && r.pred_ext) pass = ext_atoms_match(r, a, i, sample);
         if (pass) return true;
     }
     return false;
 }
 // gpu_predicate::matches with clauses (gpu_predicate_index.cuh:109-136),
 // plus the clauses' string and integer atoms.
+template <bool kExt = true>
 __device__ __forceinline__ bool pred_matches(const gofann_routes& r, const AttrView& a,
                                              uint32_t route, uint32_t sample)
 {
@@ -566,7 +570,7 @@ __device__ __forceinline__ bool pred_matches(const gofann_routes& r, const AttrV
                    range_match(at.mode, at.lower, at.upper,
                                a.ranges[static_cast<uint64_t>(sample) * a.range_count + at.dimension]);
         }
-        if (pass && r.pred_ext) pass = ext_atoms_match(r, a, i, sample);
+        if (kExt && pass && r.pred_ext) pass = ext_atoms_match(r, a, i, sample);
         if (pass) return true;
     }
     return false;
