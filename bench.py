@@ -159,7 +159,11 @@ def build_workload(args, rank, world, device, t0):
     shard = data
     if world > 1:
         shard = S.shard_data(data, lo, hi, device)
+    torch.cuda.synchronize()
+    tb = time.perf_counter()
     idx = W.build_index(shard, seed=args.seed, t0=t0, float_codebook=args.float_codebook)
+    torch.cuda.synchronize()
+    idx.stats["build_s"] = round(time.perf_counter() - tb, 2)
     return data, idx, gt, eval_idx, lo
 
 
@@ -399,6 +403,7 @@ def run_gofann(args):
                        "recall_sweep": recalls,
                        "graph_routes": dplan.n_graph, "posting_routes": dplan.n_post,
                        "graph_rows": idx.stats.get("graph_rows"), "label_graphs": idx.stats.get("groups"),
+                       "index_build_s": idx.stats.get("build_s"),
                        "pq_mode": PQ_MODE_NAMES.get(args.pq_mode, str(args.pq_mode)),
                        "codebook": "float (trained)" if args.float_codebook else "integer (trained, rounded)",
                        "l2_flush": "inputs larger than L2 (index ~25 GB resident, rows read at random)",
@@ -615,6 +620,7 @@ def run_exact_mode(args):
             "config": {"workload": "config2 in the Full-GPU exact-distance mode: 10M x 192 u8, 200k-tag Zipf(1.1), "
                                    "AND of 1-2 tags, degree 64, exact u8 distances in the traversal and posting "
                                    "scans (no PQ, no rerank)", "mode": "exact", "n_base": args.n, "n_queries": nq,
+                       "index_build_s": idx.stats.get("build_s"),
                        "queue_size": chosen, "recall_at_10": round(final_recall, 4), "recall_sweep": recalls,
                        "graph_routes": dplan.n_graph, "posting_routes": dplan.n_post,
                        "l2_flush": "inputs larger than L2 (base 1.9 GB + graphs 18.5 GB, rows read at random)",
@@ -1245,7 +1251,11 @@ def _c4_setup(args, t0):
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=900))
     n = args.n if args.n != 10_000_000 else 12_500_000  # rows per shard: one eighth of the 100M case
     data = WH.generate(device=device, n=n, n_queries=args.queries, seed=args.seed, t0=t0, shard=rank)
+    torch.cuda.synchronize()
+    tb = time.perf_counter()
     idx = WH.build_index(data, seed=args.seed, t0=t0)
+    torch.cuda.synchronize()
+    idx.stats["build_s"] = round(time.perf_counter() - tb, 2)
     return world, rank, local, device, n, data, idx
 
 
@@ -1435,6 +1445,7 @@ def run_config4(args):
                                    f"graphs; categorical / int64 range / exact-string / fuzzy-string (edit distance "
                                    f"<= 2) / hybrid AND predicates; exact FP16 rerank of 200",
                        "n_base": n * world, "n_base_per_gpu": n, "n_queries": nq, "queue_size": chosen,
+                       "index_build_s_per_gpu": idx.stats.get("build_s"),
                        "recall_at_10": round(final_recall, 4), "recall_sweep": recalls, "recall_by_kind": by_kind,
                        "graph_routes_rank0": pipe.ng, "posting_routes_rank0": pipe.npo, "scan_rows": args.scan_rows,
                        "fuzzy_rewrite_ms": round(plan.rewrite_ms, 1),
