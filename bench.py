@@ -72,6 +72,9 @@ def parse():
     ap.add_argument("--mode", default="pq", choices=["pq", "exact"],
                     help="config 2: PQ navigation + exact rerank (pq), or the Full-GPU exact-distance mode (exact: "
                          "traversal and posting scans on the exact distances of the HBM-resident base vectors)")
+    ap.add_argument("--route-order", default="work", choices=["plan", "work"],
+                    help="config 2: traverse graph routes in plan order, or longest-expected first (by the "
+                         "estimated pass rate of their residual predicates)")
     ap.add_argument("--scan-rows", type=int, default=150_000,
                     help="config 4: tag postings and int64 range slices of at most this many rows are scanned")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
@@ -250,6 +253,8 @@ def run_gofann(args):
     data, idx, gt, eval_idx, shard_base = build_workload(args, rank, world, device, t0)
     q = data["queries"]
     plan = planner.plan_queries(idx, q.labels)
+    if args.route_order == "work":
+        plan = planner.order_by_work(plan, idx)
     dplan = DevicePlan(plan, device)
     dindex = DeviceIndex(idx, device)
     L = A.lib()
@@ -409,6 +414,7 @@ def run_gofann(args):
                        "l2_flush": "inputs larger than L2 (index ~25 GB resident, rows read at random)",
                        "planning": "route planning runs before the timed region, as the reference's query "
                                    "preparation does (validate_and_prepare_queries runs before qps_start)",
+                       "route_order": args.route_order,
                        "parallelism": f"shard{world}" if world > 1 else "single",
                        "stage_ms": stages["max"], "stage_ms_min_rank": stages["min"],
                        "stage_timing": "CUDA events around each stage in an untimed pass of the same steps; "
@@ -497,6 +503,8 @@ def run_exact_mode(args):
     data, idx, gt, eval_idx, shard_base = build_workload(args, rank, world, device, t0)
     q = data["queries"]
     plan = planner.plan_queries(idx, q.labels)
+    if args.route_order == "work":
+        plan = planner.order_by_work(plan, idx)
     dplan = DevicePlan(plan, device)
     dindex = DeviceIndex(idx, device, row_records=False)
     nq, k = len(q.labels), 10

@@ -140,3 +140,33 @@ def concat_routes(a: dict, b: dict) -> dict:
     out.update(qlabel_indptr=ip.astype(np.uint64), qlabel_indices=ind, pred_offsets=np.arange(n + 1, dtype=np.uint32),
                clauses=clauses, pred_handles=handles, pred_enabled=enabled)
     return out
+
+
+def order_by_work(plan: Plan, index) -> Plan:
+    """The same plan with its graph routes reordered longest-expected first.
+
+    Persistent warps take routes in table order, so a long route taken last
+    keeps its warp busy after the others have run dry.  A route's length
+    grows as its predicate's pass rate falls (the stop rule counts only
+    passing expansions), so routes are ordered by the pass rate estimated from
+    label frequencies: the product over the residual labels of card / n, the
+    labels taken as independent.  Ties go to the larger graph first.  Results
+    do not depend on the order: every route writes its own output row, and
+    the route -> query merge reads the plan's tables."""
+    routes = plan.graph_routes
+    n_routes = routes["query_row"].shape[0]
+    if n_routes == 0:
+        return plan
+    card = np.asarray(index.posting_count, np.float64)
+    n = float(max(1, getattr(index, "n", card.max())))
+    ip, ind, prim = routes["qlabel_indptr"], routes["qlabel_indices"], routes["primary_label"]
+    rate = np.ones(n_routes)
+    for r in range(n_routes):
+        for lab in ind[ip[r]:ip[r + 1]]:
+            if lab != prim[r]:
+                rate[r] *= card[lab] / n
+    size = card[prim]
+    perm = np.lexsort((-size, rate)).astype(np.int64)
+    out = subset_routes(routes, perm)
+    return Plan(out, plan.graph_query[perm], plan.posting_routes, plan.posting_query, plan.posting_begin,
+                plan.posting_count, plan.n_queries)

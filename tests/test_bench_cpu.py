@@ -36,3 +36,16 @@ def test_cpu_search_sample_matches_full_oracle_pipeline():
     wi, wd = O.route_merge(np.concatenate([ri, rpi]), np.concatenate([rd, rpd]), qoff, order, 10)
     assert np.array_equal(res["final_ids"], wi[sel])
     assert np.array_equal(res["final_d"].view(np.uint32), wd[sel].view(np.uint32))
+
+
+def test_route_order_by_work_keeps_results():
+    """Graph routes reordered longest-expected first (planner.order_by_work):
+    the CPU path gives the same merged top-10 per query as in plan order."""
+    from gofann import planner
+    w, idx, plan = cfg2_small()
+    hidx = bench.host_index(idx)
+    sel = np.arange(w.queries.shape[0])
+    a = bench.cpu_search(hidx, plan, w.queries, sel, 64, 2)
+    b = bench.cpu_search(hidx, planner.order_by_work(plan, idx), w.queries, sel, 64, 2)
+    assert np.array_equal(a["final_ids"], b["final_ids"])
+    assert np.array_equal(a["final_d"].view(np.uint32), b["final_d"].view(np.uint32))
