@@ -252,7 +252,9 @@ def run_gofann(args):
     t0 = time.time()
     data, idx, gt, eval_idx, shard_base = build_workload(args, rank, world, device, t0)
     q = data["queries"]
-    plan = planner.plan_queries(idx, q.labels)
+    tp = time.perf_counter()
+    plan = planner.plan_queries_native(idx, q.labels)
+    plan_ms = (time.perf_counter() - tp) * 1e3
     if args.route_order == "work":
         plan = planner.order_by_work(plan, idx)
     dplan = DevicePlan(plan, device)
@@ -415,6 +417,9 @@ def run_gofann(args):
                        "planning": "route planning runs before the timed region, as the reference's query "
                                    "preparation does (validate_and_prepare_queries runs before qps_start)",
                        "route_order": args.route_order,
+                       "plan_ms": round(plan_ms, 1),
+                       "plan": "routing and residual clauses of the whole batch by the library's host planner "
+                               "(gofann_plan_categorical), outside the timed region",
                        "parallelism": f"shard{world}" if world > 1 else "single",
                        "stage_ms": stages["max"], "stage_ms_min_rank": stages["min"],
                        "stage_timing": "CUDA events around each stage in an untimed pass of the same steps; "

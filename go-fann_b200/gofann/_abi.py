@@ -83,6 +83,13 @@ class Routes(C.Structure):
                 ("pred_string_peq", P), ("pred_ints", P)]
 
 
+class PlanTables(C.Structure):
+    _fields_ = [(n, P) for n in ("query", "group_id", "start_local", "primary_label", "qlabel_indptr",
+                                 "qlabel_indices", "pred_handles", "clauses", "pred_enabled", "posting_begin",
+                                 "posting_count")] + [("n_routes", U32), ("n_labels", U32), ("n_handles", U32),
+                                                      ("reserved", U32)]
+
+
 class SearchParams(C.Structure):
     _fields_ = [("queue_size", I32), ("stop_width", I32), ("result_width", I32), ("finish_limit", I32),
                 ("early_stop_mode", I32), ("max_steps", I32), ("scorer", I32), ("predicate_bias", I32),
@@ -284,6 +291,9 @@ def lib() -> C.CDLL:
     L.gofann_beam_search_scratch_bytes.restype = C.c_size_t
     L.gofann_rabitq_gemm_scratch_bytes.argtypes = [U32, U32, U32, C.c_int]
     L.gofann_rabitq_gemm_scratch_bytes.restype = C.c_size_t
+    L.gofann_plan_categorical.argtypes = [sp, sp, U32, sp, sp, sp, sp, U32, U32, C.POINTER(PlanTables),
+                                          C.POINTER(PlanTables)]
+    L.gofann_plan_categorical.restype = C.c_int
     L.gofann_string_peq.argtypes = [sp, U32, sp]
     L.gofann_string_peq.restype = C.c_int
     L.gofann_exact_search_scratch_bytes.argtypes = [U32]
@@ -317,7 +327,7 @@ EXPORTED = ("gofann_abi_version", "gofann_last_error", "gofann_device_sm_count",
             "gofann_search_batch", "gofann_rerank", "gofann_route_merge", "gofann_shard_merge",
             "gofann_row_record_stride", "gofann_build_row_records", "gofann_offset_ids",
             "gofann_exact_search_scratch_bytes", "gofann_exact_search", "gofann_exact_posting_scan",
-            "gofann_string_peq")
+            "gofann_string_peq", "gofann_plan_categorical")
 
 
 def header_symbols(header: str | os.PathLike | None = None) -> list[str]:

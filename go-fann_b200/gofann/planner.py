@@ -13,6 +13,7 @@ Route tables are returned as numpy arrays in the gofann_routes layout.
 """
 from __future__ import annotations
 
+import ctypes as C
 from dataclasses import dataclass
 
 import numpy as np
@@ -106,6 +107,54 @@ def plan_queries(index, query_labels: list) -> Plan:
                 np.asarray(p_b, np.uint64), np.asarray(p_c, np.uint32), len(query_labels))
 
 
+def plan_queries_native(index, query_labels) -> Plan:
+    """plan_queries through the library's host planner
+    (gofann_plan_categorical): the same tables, built in C++ for the whole
+    batch.  query_labels: a list of label arrays, or (indptr u64, labels u32)."""
+    if isinstance(query_labels, tuple):
+        qptr, qlab = (np.ascontiguousarray(query_labels[0], np.uint64),
+                      np.ascontiguousarray(query_labels[1], np.uint32))
+    else:
+        qptr = np.zeros(len(query_labels) + 1, np.uint64)
+        qptr[1:] = np.cumsum([len(x) for x in query_labels])
+        qlab = (np.concatenate([np.asarray(x, np.uint32) for x in query_labels]) if len(query_labels)
+                else np.zeros(0, np.uint32))
+    nq, nnz = qptr.shape[0] - 1, int(qptr[-1])
+    card = np.ascontiguousarray(index.posting_count, np.uint32)
+    group = np.ascontiguousarray(index.label_group, np.int64)
+    seeds = np.ascontiguousarray(index.seeds, np.uint32)
+    pbeg = np.ascontiguousarray(index.posting_begin, np.uint64)
+    bufs = []
+    for _ in range(2):
+        b = dict(query=np.empty(nq, np.uint32), group_id=np.empty(nq, np.uint32),
+                 start_local=np.empty(nq, np.uint32), primary_label=np.empty(nq, np.uint32),
+                 qlabel_indptr=np.empty(nq + 1, np.uint64), qlabel_indices=np.empty(max(nnz, 1), np.uint32),
+                 pred_handles=np.empty(max(nnz, 1), np.uint32), clauses=np.zeros(max(nq, 1), A.CLAUSE_DTYPE),
+                 pred_enabled=np.empty(max(nq, 1), np.uint8), posting_begin=np.empty(max(nq, 1), np.uint64),
+                 posting_count=np.empty(max(nq, 1), np.uint32))
+        t = A.PlanTables(**{k: A.ptr(v) for k, v in b.items()})
+        bufs.append((b, t))
+    A.check(A.lib().gofann_plan_categorical(A.ptr(qptr), A.ptr(qlab), nq, A.ptr(card), A.ptr(group), A.ptr(seeds),
+                                            A.ptr(pbeg), card.shape[0], seeds.shape[0], C.byref(bufs[0][1]),
+                                            C.byref(bufs[1][1])), "gofann_plan_categorical")
+
+    def tables(b, t):
+        n, nl, nh = t.n_routes, t.n_labels, t.n_handles
+        return {"query_row": b["query"][:n].copy(), "group_id": b["group_id"][:n].copy(),
+                "start_local": b["start_local"][:n].copy(), "qlabel_indptr": b["qlabel_indptr"][:n + 1].copy(),
+                "qlabel_indices": b["qlabel_indices"][:nl].copy(), "primary_label": b["primary_label"][:n].copy(),
+                "pred_offsets": np.arange(n + 1, dtype=np.uint32), "clauses": b["clauses"][:n].copy(),
+                "pred_handles": b["pred_handles"][:nh].copy() if nh else np.zeros(1, np.uint32),
+                "pred_enabled": b["pred_enabled"][:n].copy()}, b["posting_begin"][:n].copy(), \
+            b["posting_count"][:n].copy()
+
+    g, _, _ = tables(*bufs[0])
+    p, pb, pc = tables(*bufs[1])
+    p["group_id"][:] = 0
+    p["start_local"][:] = 0
+    return Plan(g, g["query_row"].copy(), p, p["query_row"].copy(), pb, pc, nq)
+
+
 def subset_routes(routes: dict, sel: np.ndarray) -> dict:
     """Route tables restricted to the routes `sel` (label CSR re-based)."""
     sel = np.asarray(sel, np.int64)
@@ -159,12 +208,12 @@ def order_by_work(plan: Plan, index) -> Plan:
         return plan
     card = np.asarray(index.posting_count, np.float64)
     n = float(max(1, getattr(index, "n", card.max())))
-    ip, ind, prim = routes["qlabel_indptr"], routes["qlabel_indices"], routes["primary_label"]
-    rate = np.ones(n_routes)
-    for r in range(n_routes):
-        for lab in ind[ip[r]:ip[r + 1]]:
-            if lab != prim[r]:
-                rate[r] *= card[lab] / n
+    ip, ind, prim = routes["qlabel_indptr"].astype(np.int64), routes["qlabel_indices"], routes["primary_label"]
+    owner = np.repeat(np.arange(n_routes), np.diff(ip))
+    resid = ind != prim[owner]
+    logp = np.zeros(n_routes)
+    np.add.at(logp, owner[resid], np.log(np.maximum(card[ind[resid]], 1e-300) / n))
+    rate = np.exp(logp)
     size = card[prim]
     perm = np.lexsort((-size, rate)).astype(np.int64)
     out = subset_routes(routes, perm)

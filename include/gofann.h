@@ -39,6 +39,11 @@
  *   gofann_route_merge        merge_route_results_to_original src/search/rabitq/rabitq_lowfreq_merge.h:710-815
  *   gofann_shard_merge        (no reference counterpart: the reference is single-GPU; the merge
  *                             order is the (dist, id) rule of rabitq_lowfreq_merge.h:800-806)
+ *   gofann_exact_search       run_full_gpu_highfreq_route src/search/full_gpu/backend_full_gpu.cu:1682-2043
+ *   gofann_exact_posting_scan full_gpu_lowfreq_kernel src/search/full_gpu/backend_full_gpu.cu:2124-2260
+ *   gofann_plan_categorical   greedy_min_posting routing + route_predicate::compile (host)
+ *                                                     src/data/dataloader.cpp:7833, 10972;
+ *                                                     src/planning/route_predicate_plan.h:175-315
  */
 #ifndef GOFANN_H
 #define GOFANN_H
@@ -565,6 +570,40 @@ GOFANN_API int gofann_predicate_pass_masks(const gofann_graph* graph, const gofa
                                            const gofann_routes* routes, const uint32_t* cand_route,
                                            const uint32_t* cand_rows, uint32_t n_candidates,
                                            uint32_t* out_masks, int32_t* status, void* stream);
+
+/* ------------------------------------------------------ route planning */
+/* Route tables written by gofann_plan_categorical (host arrays the caller
+ * allocates: routes up to the batch's query count, labels and handles up to
+ * its label count).  One DNF clause per route (pred_offsets = 0, 1, ..., the
+ * caller's identity array); the counts are outputs. */
+typedef struct gofann_plan_tables {
+    uint32_t* query;           /* [routes] original query of the route (route_to_original_query) */
+    uint32_t* group_id;        /* [routes] graph group, 0 for posting routes */
+    uint32_t* start_local;     /* [routes] seed row of the group, 0 for posting routes */
+    uint32_t* primary_label;   /* [routes] the label the route covers */
+    uint64_t* qlabel_indptr;   /* [routes + 1] */
+    uint32_t* qlabel_indices;  /* the query's labels, as given */
+    uint32_t* pred_handles;    /* the residual labels (all but the primary one) */
+    gofann_clause* clauses;    /* [routes] */
+    uint8_t* pred_enabled;     /* [routes] 1 when the residual is not empty */
+    uint64_t* posting_begin;   /* [routes] posting routes: the label's posting slice */
+    uint32_t* posting_count;
+    uint32_t n_routes, n_labels, n_handles, reserved;
+} gofann_plan_tables;
+
+/* Host-side routing of a batch of AND-of-labels queries (greedy_min_posting,
+ * src/data/dataloader.cpp:7833-7836, in validate_and_prepare_queries
+ * :10972; the residual compiled as in route_predicate::compile,
+ * src/planning/route_predicate_plan.h:175-315): a query's route is its label
+ * with the smallest label_card (the first on ties); a label with
+ * label_group >= 0 gives a graph route seeded at group_seed[group], any other
+ * a posting route over label_posting_begin / label_card.  Host pointers; no
+ * device work. */
+GOFANN_API int gofann_plan_categorical(const uint64_t* q_indptr, const uint32_t* q_labels, uint32_t n_queries,
+                                       const uint32_t* label_card, const int64_t* label_group,
+                                       const uint32_t* group_seed, const uint64_t* label_posting_begin,
+                                       uint32_t n_labels, uint32_t n_groups, gofann_plan_tables* graph,
+                                       gofann_plan_tables* post);
 
 /* ---------------------------------------------------------- exact rerank */
 /* Exact L2 of each candidate against its query row, residual label check

@@ -8,6 +8,7 @@ v > lower, 2 v < upper, 3 lower <= v < upper.  The pass bitmap keeps
 candidate order, 32 candidates per word, candidate i at bit i % 32.
 """
 import numpy as np
+import pytest
 
 from fixtures import cfg1_small, with_predicates
 from oracle import oracle as O
@@ -49,3 +50,30 @@ def test_oracle_dnf_and_pass_masks_match_semantics():
     masks = O.predicate_pass_masks(graph, attrs, dnf, cr, rows)
     bits = np.unpackbits(masks.view(np.uint8), bitorder="little")[:n].astype(bool)
     assert np.array_equal(bits, want)
+
+
+@pytest.mark.parametrize("wl", ["cfg1", "cfg2"])
+def test_native_planner_equals_python_planner(wl):
+    """gofann_plan_categorical (host C++) builds the same route tables as
+    planner.plan_queries: route split, seeds, posting slices, label lists,
+    residual clauses and their enable flags."""
+    from fixtures import cfg1_small, cfg2_small
+    from gofann import planner
+    w, idx, plan = cfg1_small() if wl == "cfg1" else cfg2_small()
+    nat = planner.plan_queries_native(idx, w.query_labels)
+    for a, b in ((plan.graph_routes, nat.graph_routes), (plan.posting_routes, nat.posting_routes)):
+        assert sorted(a) == sorted(b)
+        for k in a:
+            assert np.array_equal(np.asarray(a[k]).view(np.uint8), np.asarray(b[k]).view(np.uint8)), k
+    for k in ("graph_query", "posting_query", "posting_begin", "posting_count"):
+        assert np.array_equal(getattr(plan, k), getattr(nat, k)), k
+
+
+def test_native_planner_rejects_bad_labels():
+    from fixtures import cfg2_small
+    from gofann import _abi as A, planner
+    w, idx, plan = cfg2_small()
+    with pytest.raises(A.GofannError):
+        planner.plan_queries_native(idx, [np.array([10 ** 7], np.uint32)])
+    with pytest.raises(A.GofannError):
+        planner.plan_queries_native(idx, [np.array([], np.uint32)])
