@@ -674,10 +674,11 @@ __device__ __forceinline__ void run_route(const BeamArgs& a, const WarpBufs& w,
         if (lane == 0) st.now = st.next;
         // the next step's visited-table lines (after this step's inserts),
         // fetched now into L1.  The neighbours' records are not prefetched:
-        // most of a step's neighbours are already visited, and on the 10M
-        // categorical workload a one-step-ahead L2 prefetch of every
-        // neighbour's record made the traversal 1.1 % slower (80.5 against
-        // 79.6 ms per batch), a 64-byte bulk prefetch 10 % slower.
+        // the prefetch would also fetch the records of visited neighbours,
+        // which are never read.  On the 10M categorical workload a
+        // one-step-ahead L2 prefetch of every neighbour's record made the
+        // traversal 1.1 % slower (80.5 against 79.6 ms per batch) and added a
+        // quarter to its DRAM reads; a 64-byte bulk prefetch was 10 % slower.
 #pragma unroll
         for (int h = 0; h < GOFANN_MAX_DEGREE / kWarp; ++h) {
             nb[h] = nb_next[h];
