@@ -49,3 +49,14 @@ def test_route_order_by_work_keeps_results():
     b = bench.cpu_search(hidx, planner.order_by_work(plan, idx), w.queries, sel, 64, 2)
     assert np.array_equal(a["final_ids"], b["final_ids"])
     assert np.array_equal(a["final_d"].view(np.uint32), b["final_d"].view(np.uint32))
+
+
+def test_profiled_traffic_record_is_consistent():
+    """roofline.traffic of the config-2 line scales the committed capture's
+    DRAM-bytes-per-algorithmic-byte ratio; the ratio must match the bytes it
+    was computed from, and a launch moves at least its algorithmic bytes."""
+    t = bench.profiled_traffic()
+    assert t is not None and t["kernel"] == "beam_search_kernel"
+    ratio = t["dram_bytes"] / t["algorithmic_bytes"]
+    assert abs(ratio - t["traffic_per_algorithmic_byte"]) < 5e-4
+    assert ratio >= 1.0
